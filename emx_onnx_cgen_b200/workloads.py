@@ -1,0 +1,248 @@
+"""The five graphs this backend is measured on, as seeded synthetic ONNX graphs.
+
+Each builder returns a ``GraphSpec`` whose weights are drawn from
+``numpy.random.default_rng(weight_seed)`` and an ``inputs(seed)`` function
+that draws the graph inputs from ``default_rng(seed)``.  Sizes are parameters
+so the same graph runs at full size (benchmark) and at slices the CPU oracle
+finishes in seconds (parity tests).  Distributions follow the workload
+definitions:
+
+* ``mlp_fp32``           Gemm(transB) -> Relu -> Gemm(transB), fp32, opset 17
+* ``qconv_stack_int8``   4 x QLinearConv 3x3 (64->64) with a com.microsoft
+                         QLinearAdd residual after every second conv
+* ``llama_mlp_int4``     com.microsoft MatMulNBits gate/up -> Swish(gate)*up ->
+                         MatMulNBits down, fp16 activations, int4 weights
+* ``attention_fp16``     opset-23 Attention, causal, fp16
+* ``lstm_fp32``          ONNX LSTM, forward, fp32
+
+No public dataset is involved; all inputs are synthetic.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import numpy as np
+
+from .spec import GraphSpec, NodeSpec, TensorSpec
+
+
+@dataclass
+class Workload:
+    name: str
+    graph: GraphSpec
+    make_inputs: Callable[[int], dict[str, np.ndarray]]
+    batch_axis: dict[str, int]          # graph input/output name -> axis of independent rows
+    params: dict[str, object]
+
+
+def _scalar(value, dtype) -> np.ndarray:
+    return np.asarray(value, dtype=dtype).reshape(())
+
+
+# --------------------------------------------------------------------------- cfg 1
+def mlp_fp32(m: int = 64, k: int = 1024, hidden: int = 4096, weight_seed: int = 1) -> Workload:
+    rng = np.random.default_rng(weight_seed)
+    w1 = rng.normal(0.0, 1.0 / np.sqrt(k), (hidden, k)).astype(np.float32)
+    b1 = rng.uniform(-0.1, 0.1, hidden).astype(np.float32)
+    w2 = rng.normal(0.0, 1.0 / np.sqrt(hidden), (k, hidden)).astype(np.float32)
+    b2 = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    g = GraphSpec(
+        name="mlp_fp32",
+        inputs=[TensorSpec("X", "f32", (m, k))],
+        outputs=[TensorSpec("Y", "f32", (m, k))],
+        nodes=[
+            NodeSpec("Gemm", "gemm1", ("X", "W1", "b1"), ("H",), {"transB": 1}),
+            NodeSpec("Relu", "relu", ("H",), ("R",)),
+            NodeSpec("Gemm", "gemm2", ("R", "W2", "b2"), ("Y",), {"transB": 1}),
+        ],
+        initializers={"W1": w1, "b1": b1, "W2": w2, "b2": b2},
+        values=[TensorSpec("H", "f32", (m, hidden)), TensorSpec("R", "f32", (m, hidden))],
+        opset_imports=(("", 17),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        r = np.random.default_rng(seed)
+        return {"X": r.uniform(-1.0, 1.0, (m, k)).astype(np.float32)}
+
+    return Workload("mlp_fp32", g, make_inputs, {"X": 0, "Y": 0},
+                    dict(m=m, k=k, hidden=hidden))
+
+
+# --------------------------------------------------------------------------- cfg 2
+def qconv_stack_int8(batch: int = 32, channels: int = 64, height: int = 56, width: int = 56,
+                     n_convs: int = 4, wscale_range: tuple[float, float] = (0.001, 0.01),
+                     weight_seed: int = 1) -> Workload:
+    """uint8 NCHW activations, per-tensor scale 0.02 / zero point 128 at the input.
+
+    Every QLinearConv has int8 OIHW weights ~U(-127,127), per-output-channel
+    fp32 scales ~U(wscale_range), weight zero point 0, int32 bias
+    ~U(-1000,1000) and output scale 0.02 / zero point 0 (the ReLU folded into
+    the output zero point and the uint8 clamp).  After every second conv a
+    com.microsoft QLinearAdd adds the block input back in (output scale 0.04,
+    zero point 128); the last add is the graph output.
+    """
+    rng = np.random.default_rng(weight_seed)
+    c = channels
+    inits: dict[str, np.ndarray] = {
+        "x_scale": _scalar(0.02, np.float32),
+        "x_zero": _scalar(128, np.uint8),
+        "h_scale": _scalar(0.02, np.float32),
+        "h_zero": _scalar(0, np.uint8),
+        "a_scale": _scalar(0.04, np.float32),
+        "a_zero": _scalar(128, np.uint8),
+    }
+    nodes: list[NodeSpec] = []
+    values: list[TensorSpec] = []
+    shape = (batch, c, height, width)
+    cur, cur_scale, cur_zero = "X", "x_scale", "x_zero"
+    block_in, block_scale, block_zero = cur, cur_scale, cur_zero
+    for i in range(n_convs):
+        inits[f"w{i}"] = rng.integers(-127, 128, (c, c, 3, 3)).astype(np.int8)
+        inits[f"ws{i}"] = rng.uniform(wscale_range[0], wscale_range[1], c).astype(np.float32)
+        inits[f"wz{i}"] = np.zeros(c, np.int8)
+        inits[f"b{i}"] = rng.integers(-1000, 1001, c).astype(np.int32)
+        out = f"H{i}"
+        nodes.append(NodeSpec(
+            "QLinearConv", f"conv{i}",
+            (cur, cur_scale, cur_zero, f"w{i}", f"ws{i}", f"wz{i}", "h_scale", "h_zero", f"b{i}"),
+            (out,), {"kernel_shape": [3, 3], "pads": [1, 1, 1, 1], "strides": [1, 1]}))
+        values.append(TensorSpec(out, "u8", shape))
+        cur, cur_scale, cur_zero = out, "h_scale", "h_zero"
+        if i % 2 == 1:
+            last = i == n_convs - 1
+            aout = "Y" if last else f"A{i}"
+            nodes.append(NodeSpec(
+                "QLinearAdd", f"add{i}",
+                (cur, cur_scale, cur_zero, block_in, block_scale, block_zero, "a_scale", "a_zero"),
+                (aout,), {}, "com.microsoft"))
+            if not last:
+                values.append(TensorSpec(aout, "u8", shape))
+            cur, cur_scale, cur_zero = aout, "a_scale", "a_zero"
+            block_in, block_scale, block_zero = cur, cur_scale, cur_zero
+    if n_convs % 2 == 1:   # odd stack: the last conv is the output
+        nodes[-1] = NodeSpec(nodes[-1].op_type, nodes[-1].name, nodes[-1].inputs, ("Y",),
+                             nodes[-1].attrs)
+        values = [v for v in values if v.name != cur]
+    g = GraphSpec(
+        name="qconv_stack_int8",
+        inputs=[TensorSpec("X", "u8", shape)],
+        outputs=[TensorSpec("Y", "u8", shape)],
+        nodes=nodes, initializers=inits, values=values,
+        opset_imports=(("", 17), ("com.microsoft", 1)),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        r = np.random.default_rng(seed)
+        return {"X": r.integers(0, 256, shape).astype(np.uint8)}
+
+    return Workload("qconv_stack_int8", g, make_inputs, {"X": 0, "Y": 0},
+                    dict(batch=batch, channels=c, height=height, width=width, n_convs=n_convs,
+                         wscale_range=tuple(wscale_range)))
+
+
+# --------------------------------------------------------------------------- cfg 3
+def llama_mlp_int4(m: int = 2048, hidden: int = 4096, inter: int = 11008, block: int = 32,
+                   weight_seed: int = 1) -> Workload:
+    """fp16 activations ~N(0,1); uint4 weights ~U(0,15) in blocks of 32 along K.
+
+    Scales fp16 ~U(0.005, 0.02); no zero-point input (the default zero point
+    8 of MatMulNBits applies); accuracy_level 0.  SiLU(gate)*up is expressed
+    as Swish(alpha=1) followed by Mul.
+    """
+    rng = np.random.default_rng(weight_seed)
+
+    def nbits(prefix: str, k: int, n: int) -> dict[str, np.ndarray]:
+        nb = k // block
+        return {
+            f"{prefix}_B": rng.integers(0, 256, (n, nb, block // 2)).astype(np.uint8),
+            f"{prefix}_s": rng.uniform(0.005, 0.02, (n, nb)).astype(np.float16),
+        }
+
+    inits = {**nbits("gate", hidden, inter), **nbits("up", hidden, inter), **nbits("down", inter, hidden)}
+
+    def mm(name, a, out, k, n):
+        return NodeSpec("MatMulNBits", name, (a, f"{name}_B", f"{name}_s"), (out,),
+                        {"bits": 4, "block_size": block, "K": k, "N": n, "accuracy_level": 0},
+                        "com.microsoft")
+
+    nodes = [
+        mm("gate", "A", "G", hidden, inter),
+        mm("up", "A", "U", hidden, inter),
+        NodeSpec("Swish", "silu", ("G",), ("S",), {"alpha": 1.0}),
+        NodeSpec("Mul", "mul", ("S", "U"), ("P",)),
+        mm("down", "P", "Y", inter, hidden),
+    ]
+    values = [TensorSpec(n, "f16", (m, inter)) for n in ("G", "U", "S", "P")]
+    g = GraphSpec(
+        name="llama_mlp_int4",
+        inputs=[TensorSpec("A", "f16", (m, hidden))],
+        outputs=[TensorSpec("Y", "f16", (m, hidden))],
+        nodes=nodes, initializers=inits, values=values,
+        opset_imports=(("", 24), ("com.microsoft", 1)),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        r = np.random.default_rng(seed)
+        return {"A": r.standard_normal((m, hidden)).astype(np.float16)}
+
+    return Workload("llama_mlp_int4", g, make_inputs, {"A": 0, "Y": 0},
+                    dict(m=m, hidden=hidden, inter=inter, block=block))
+
+
+# --------------------------------------------------------------------------- cfg 4
+def attention_fp16(batch: int = 8, heads: int = 32, seq: int = 2048, head_dim: int = 128,
+                   causal: bool = True) -> Workload:
+    shape = (batch, heads, seq, head_dim)
+    g = GraphSpec(
+        name="attention_fp16",
+        inputs=[TensorSpec(n, "f16", shape) for n in ("Q", "K", "V")],
+        outputs=[TensorSpec("Y", "f16", shape)],
+        nodes=[NodeSpec("Attention", "attn", ("Q", "K", "V"), ("Y",),
+                        {"is_causal": 1 if causal else 0})],
+        initializers={},
+        opset_imports=(("", 23),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        r = np.random.default_rng(seed)
+        return {n: r.standard_normal(shape).astype(np.float16) for n in ("Q", "K", "V")}
+
+    return Workload("attention_fp16", g, make_inputs, {"Q": 0, "K": 0, "V": 0, "Y": 0},
+                    dict(batch=batch, heads=heads, seq=seq, head_dim=head_dim, causal=causal))
+
+
+# --------------------------------------------------------------------------- cfg 5
+def lstm_fp32(seq: int = 512, batch: int = 256, input_size: int = 512, hidden: int = 1024,
+              weight_seed: int = 1) -> Workload:
+    rng = np.random.default_rng(weight_seed)
+    w = rng.uniform(-1 / 32, 1 / 32, (1, 4 * hidden, input_size)).astype(np.float32)
+    r = rng.uniform(-1 / 32, 1 / 32, (1, 4 * hidden, hidden)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, (1, 8 * hidden)).astype(np.float32)
+    g = GraphSpec(
+        name="lstm_fp32",
+        inputs=[TensorSpec("X", "f32", (seq, batch, input_size))],
+        outputs=[TensorSpec("Y", "f32", (seq, 1, batch, hidden)),
+                 TensorSpec("Y_h", "f32", (1, batch, hidden)),
+                 TensorSpec("Y_c", "f32", (1, batch, hidden))],
+        nodes=[NodeSpec("LSTM", "lstm", ("X", "W", "R", "B"), ("Y", "Y_h", "Y_c"),
+                        {"hidden_size": hidden})],
+        initializers={"W": w, "R": r, "B": b},
+        opset_imports=(("", 22),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        rr = np.random.default_rng(seed)
+        return {"X": rr.uniform(-1.0, 1.0, (seq, batch, input_size)).astype(np.float32)}
+
+    return Workload("lstm_fp32", g, make_inputs, {"X": 1, "Y": 2, "Y_h": 1, "Y_c": 1},
+                    dict(seq=seq, batch=batch, input_size=input_size, hidden=hidden))
+
+
+BUILDERS = {
+    "mlp_fp32": mlp_fp32,
+    "qconv_stack_int8": qconv_stack_int8,
+    "llama_mlp_int4": llama_mlp_int4,
+    "attention_fp16": attention_fp16,
+    "lstm_fp32": lstm_fp32,
+}

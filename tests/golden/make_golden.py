@@ -1,0 +1,84 @@
+"""Generate the golden input/output vectors in this directory.
+
+Each case builds a small instance of one workload graph, has the REFERENCE
+compiler (imported from its source tree through the test-only onnx shim in
+``oracle/onnx_shim.py``) lower it and emit C, compiles that C with
+``gcc -std=c99 -O2`` and runs it on seeded inputs.  The graph's initializers,
+inputs and the reference outputs are stored as ``<case>.npz``; ``cases.json``
+records the builder arguments.  The fixtures pin both the oracle restatement
+(``oracle/oracle.c``) and the CUDA kernels without needing the reference at
+test time.
+
+Run from the repository root (needs the reference source tree, default
+``/root/reference/src``, override with ``EMX_REFERENCE_SRC``)::
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import json
+import platform
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+from emx_onnx_cgen_b200 import workloads as W  # noqa: E402
+from oracle import refc  # noqa: E402
+
+# (case name, builder, kwargs, input seed)
+CASES = [
+    ("qconv_b2_c64_12x12", "qconv_stack_int8", dict(batch=2, channels=64, height=12, width=12), 0),
+    ("qconv_b1_c64_7x9_lowgain", "qconv_stack_int8",
+     dict(batch=1, channels=64, height=7, width=9, wscale_range=(0.0001, 0.001)), 1),
+    ("qconv_b1_c16_5x5_3conv", "qconv_stack_int8",
+     dict(batch=1, channels=16, height=5, width=5, n_convs=3, wscale_range=(0.0001, 0.001)), 2),
+    ("qconv_b2_c32_16x16_lowgain", "qconv_stack_int8",
+     dict(batch=2, channels=32, height=16, width=16, wscale_range=(0.0001, 0.001)), 3),
+    ("mlp_m4_k32_h64", "mlp_fp32", dict(m=4, k=32, hidden=64), 0),
+    ("mlp_m5_k48_h80", "mlp_fp32", dict(m=5, k=48, hidden=80), 1),
+    ("nbits_m4_k64_n96", "llama_mlp_int4", dict(m=4, hidden=64, inter=96), 0),
+    ("nbits_m3_k128_n160", "llama_mlp_int4", dict(m=3, hidden=128, inter=160), 1),
+    ("attn_b1_h2_t16_d8", "attention_fp16", dict(batch=1, heads=2, seq=16, head_dim=8), 0),
+    ("attn_b1_h2_t64_d128", "attention_fp16", dict(batch=1, heads=2, seq=64, head_dim=128), 1),
+    ("attn_b1_h1_t33_d64", "attention_fp16", dict(batch=1, heads=1, seq=33, head_dim=64), 2),
+    ("lstm_t3_b2_i8_h16", "lstm_fp32", dict(seq=3, batch=2, input_size=8, hidden=16), 0),
+    ("lstm_t5_b3_i16_h32", "lstm_fp32", dict(seq=5, batch=3, input_size=16, hidden=32), 1),
+]
+
+
+def main() -> None:
+    if not refc.reference_available():
+        raise SystemExit(f"reference source not found at {refc.REFERENCE_SRC}")
+    gcc = subprocess.run(["gcc", "--version"], capture_output=True, text=True).stdout.splitlines()[0]
+    libc = " ".join(platform.libc_ver())
+    index = {"generator": "reference generated C, gcc -std=c99 -O2", "gcc": gcc, "libc": libc,
+             "cases": {}}
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, builder, kwargs, seed in CASES:
+            wl = W.BUILDERS[builder](**kwargs)
+            tag = "g_" + name
+            refc.build(wl.graph, tag, Path(tmp))
+            model = refc.RefCModel(tag, Path(tmp))
+            inputs = wl.make_inputs(seed)
+            outputs = model.run(inputs)
+            arrays = {f"init:{k}": v for k, v in wl.graph.initializers.items()}
+            arrays.update({f"in:{k}": v for k, v in inputs.items()})
+            arrays.update({f"out:{k}": v for k, v in outputs.items()})
+            np.savez_compressed(HERE / f"{name}.npz", **arrays)
+            index["cases"][name] = {"builder": builder,
+                                    "kwargs": {k: list(v) if isinstance(v, tuple) else v
+                                               for k, v in kwargs.items()},
+                                    "seed": seed}
+            print(name, {k: v.shape for k, v in outputs.items()})
+    (HERE / "cases.json").write_text(json.dumps(index, indent=1) + "\n")
+
+
+if __name__ == "__main__":
+    main()
