@@ -1,0 +1,79 @@
+// Kernel ids, per-kernel plan-parameter slots and host launchers.
+// The plan emitter (plan.py) writes the same slot numbers; keep both in sync
+// (tests/test_plan.py checks the Python mirror against this header).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "plan_format.h"
+
+namespace emx {
+
+enum KernelId : uint32_t {
+  K_PAD_NHWC = 1,       // NCHW 8-bit -> zero-bordered NHWC (optionally XOR 0x80)
+  K_QCONV_TC = 2,       // QLinearConv implicit GEMM on tcgen05 kind::i8 (+ fused QLinearAdd)
+  K_QCONV_GENERIC = 3,  // QLinearConv, any stride/pad/dilation/group, CUDA cores
+  K_QLINEAR_ADD = 4,    // com.microsoft QLinearAdd, same-shape operands
+  K_GEMM_F32 = 5,       // Gemm fp32, reference accumulation order (+bias, +Relu)
+  K_RELU_F32 = 6,
+  K_NBITS_GEMM = 7,     // MatMulNBits int4 -> fp16 on tcgen05 kind::f16 (+fused epilogues)
+  K_SWISH_F16 = 8,
+  K_MUL_F16 = 9,
+  K_ATTENTION_F16 = 10, // opset-23 Attention, flash tiling on tcgen05
+  K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order
+  K_NBITS_DEQUANT = 12, // int4 blocks -> fp16 weight matrix (prologue of K_NBITS_GEMM)
+};
+
+// ---- K_PAD_NHWC: t[0]=x (NCHW), t[1]=y (padded NHWC)
+enum { PAD_N, PAD_C, PAD_H, PAD_W, PAD_TOP, PAD_LEFT, PAD_HP, PAD_WP, PAD_XOR };
+
+// ---- K_QCONV_TC: t[0]=x (padded NHWC), t[1]=w image, t[2]=epilogue table
+//      (float scale[OC], int32 bias[OC]), t[3]=residual (padded NHWC) or -1, t[4]=y
+enum {
+  QC_N, QC_CIN, QC_OC, QC_KH, QC_KW, QC_HP, QC_WP, QC_OH, QC_OW, QC_A_SIGNED, QC_Y_ZERO,
+  QC_Y_LAYOUT /*0 padded NHWC, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,
+  QC_HAS_ADD, QC_C_ZERO /*conv-side zero in the add*/, QC_R_ZERO, QC_R_XOR, QC_R_SIGNED, QC_R_HP, QC_R_WP,
+  QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED
+};
+enum { QCF_C_SCALE, QCF_R_SCALE, QCF_ADD_SCALE };
+
+// ---- K_QCONV_GENERIC: t[0]=x NCHW, t[1]=w OIHW, t[2]=w_scale f32, t[3]=w_zero i32|-1,
+//      t[4]=bias i32|-1, t[5]=y NCHW
+enum {
+  QG_N, QG_C, QG_H, QG_W, QG_OC, QG_KH, QG_KW, QG_OH, QG_OW, QG_SH, QG_SW, QG_PT, QG_PL, QG_DH, QG_DW,
+  QG_GROUP, QG_X_SIGNED, QG_W_SIGNED, QG_Y_SIGNED, QG_X_ZERO, QG_Y_ZERO, QG_WS_PER_CH, QG_WZ_PER_CH
+};
+enum { QGF_X_SCALE, QGF_Y_SCALE };
+
+// ---- K_QLINEAR_ADD: t[0]=a, t[1]=b, t[2]=y
+enum { QA_COUNT, QA_A_SIGNED, QA_B_SIGNED, QA_Y_SIGNED, QA_A_ZERO, QA_B_ZERO, QA_Y_ZERO, QA_BATCH };
+enum { QAF_A_SCALE, QAF_B_SCALE, QAF_Y_SCALE };
+
+struct LaunchCtx {
+  cudaStream_t stream;
+  int* d_error;     // device error word
+  int64_t batch;    // rows along axis 0 this run (== plan batch unless sliced); 0: plan not batched
+  int num_sms;
+};
+
+// Batch an op processes this run: the run's slice when the plan is batched,
+// else the op's compiled extent.
+inline int64_t eff_batch(const LaunchCtx& c, int64_t compiled) { return c.batch > 0 ? c.batch : compiled; }
+
+// Opaque per-op state prepared once at plan load (tensor maps, chosen variant).
+struct alignas(64) OpState {
+  unsigned char bytes[512];
+};
+
+// Each kernel family: prepare (load time, may fail with a message) + launch.
+typedef int (*PrepareFn)(const PlanOp& op, void* const* ptrs, OpState* st, int device, char* msg, size_t msg_len);
+typedef int (*LaunchFn)(const PlanOp& op, void* const* ptrs, const OpState* st, const LaunchCtx& ctx,
+                        int* launches);
+
+int prepare_qconv_tc(const PlanOp&, void* const*, OpState*, int, char*, size_t);
+int launch_qconv_tc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_pad_nhwc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_qconv_generic(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_qlinear_add(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+
+}  // namespace emx

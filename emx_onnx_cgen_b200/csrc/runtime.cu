@@ -1,0 +1,412 @@
+// C-ABI runtime of libemx_b200.so: plan parsing, device arena, weight upload,
+// host/device I/O staging and in-order kernel dispatch.  See include/emx_b200.h.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/emx_b200.h"
+#include "host_util.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(call, what)                                                                  \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess) return set_error(EMX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e_)); \
+  } while (0)
+
+struct KernelEntry {
+  uint32_t id;
+  emx::PrepareFn prepare;
+  emx::LaunchFn launch;
+  const char* name;
+};
+
+const KernelEntry kKernels[] = {
+    {emx::K_PAD_NHWC, nullptr, emx::launch_pad_nhwc, "pad_nhwc"},
+    {emx::K_QCONV_TC, emx::prepare_qconv_tc, emx::launch_qconv_tc, "qconv_tc"},
+    {emx::K_QCONV_GENERIC, nullptr, emx::launch_qconv_generic, "qconv_generic"},
+    {emx::K_QLINEAR_ADD, nullptr, emx::launch_qlinear_add, "qlinear_add"},
+};
+
+const KernelEntry* find_kernel(uint32_t id) {
+  for (const auto& k : kKernels)
+    if (k.id == id) return &k;
+  return nullptr;
+}
+
+}  // namespace
+
+struct emx_plan {
+  int device = 0;
+  int num_sms = 0;
+  PlanHeader hdr{};
+  std::vector<PlanTensor> tensors;
+  std::vector<uint32_t> inputs, outputs;
+  std::vector<PlanOp> ops;
+  std::vector<emx::OpState> states;
+  std::vector<const KernelEntry*> entries;
+  void* d_weights = nullptr;
+  void* d_arena = nullptr;
+  int* d_error = nullptr;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t last_stream = nullptr;
+  std::vector<void*> ptrs;  // per-tensor device pointer (I/O re-resolved each run)
+  int64_t launches_total = 0;
+  int64_t launches_last = -1;
+  // host outputs pending a device->host copy: (host dst, staging src, bytes)
+  struct Pending { void* host; const void* dev; size_t bytes; };
+  std::vector<Pending> pending;
+  // per-op timing
+  bool profiling = false;
+  bool events_pending = false;
+  std::vector<cudaEvent_t> ev_begin, ev_end;
+  std::vector<double> op_ms;
+  int64_t profiled_runs = 0;
+};
+
+namespace {
+
+size_t dtype_size(uint32_t dt) {
+  switch (dt) {
+    case EMX_U8: case EMX_I8: return 1;
+    case EMX_F16: return 2;
+    case EMX_F32: case EMX_I32: return 4;
+    case EMX_I64: case EMX_F64: return 8;
+    default: return 0;
+  }
+}
+
+int parse_plan(emx_plan* p, const void* blob, size_t len) {
+  const uint8_t* b = static_cast<const uint8_t*>(blob);
+  if (!blob || len < sizeof(PlanHeader)) return set_error(EMX_ERR_PLAN_FORMAT, "plan blob too short (%zu bytes)", len);
+  memcpy(&p->hdr, b, sizeof(PlanHeader));
+  const PlanHeader& h = p->hdr;
+  if (h.magic != EMX_PLAN_MAGIC) return set_error(EMX_ERR_PLAN_FORMAT, "bad plan magic 0x%08x", h.magic);
+  if (h.version != EMX_PLAN_VERSION)
+    return set_error(EMX_ERR_PLAN_FORMAT, "plan version %u, library expects %u", h.version, EMX_PLAN_VERSION);
+  if (h.n_tensors > (1u << 20) || h.n_ops > (1u << 20) || h.n_inputs > h.n_tensors || h.n_outputs > h.n_tensors)
+    return set_error(EMX_ERR_PLAN_FORMAT, "implausible plan counts");
+  const size_t in_slots = (h.n_inputs + 1) & ~1u, out_slots = (h.n_outputs + 1) & ~1u;
+  const size_t need = sizeof(PlanHeader) + (size_t)h.n_tensors * sizeof(PlanTensor) + (in_slots + out_slots) * 4 +
+                      (size_t)h.n_ops * sizeof(PlanOp);
+  if (len != need) return set_error(EMX_ERR_PLAN_FORMAT, "plan blob is %zu bytes, header implies %zu", len, need);
+  size_t off = sizeof(PlanHeader);
+  p->tensors.resize(h.n_tensors);
+  memcpy(p->tensors.data(), b + off, h.n_tensors * sizeof(PlanTensor));
+  off += h.n_tensors * sizeof(PlanTensor);
+  p->inputs.resize(h.n_inputs);
+  memcpy(p->inputs.data(), b + off, h.n_inputs * 4);
+  off += in_slots * 4;
+  p->outputs.resize(h.n_outputs);
+  memcpy(p->outputs.data(), b + off, h.n_outputs * 4);
+  off += out_slots * 4;
+  p->ops.resize(h.n_ops);
+  memcpy(p->ops.data(), b + off, h.n_ops * sizeof(PlanOp));
+  // validate every reference
+  for (size_t i = 0; i < p->tensors.size(); ++i) {
+    const PlanTensor& t = p->tensors[i];
+    const uint64_t limit = t.kind == EMX_T_WEIGHT ? h.weight_bytes : h.arena_bytes;
+    if (t.kind > EMX_T_TEMP || dtype_size(t.dtype) == 0 || t.rank < 0 || t.rank > EMX_MAX_RANK)
+      return set_error(EMX_ERR_PLAN_FORMAT, "tensor %zu: bad kind/dtype/rank", i);
+    if (t.offset > limit || t.nbytes > limit - t.offset)
+      return set_error(EMX_ERR_PLAN_FORMAT, "tensor %zu: [%llu, +%llu) outside its region (%llu bytes)", i,
+                       (unsigned long long)t.offset, (unsigned long long)t.nbytes, (unsigned long long)limit);
+  }
+  for (uint32_t id : p->inputs)
+    if (id >= h.n_tensors || p->tensors[id].kind != EMX_T_INPUT) return set_error(EMX_ERR_PLAN_FORMAT, "bad input id");
+  for (uint32_t id : p->outputs)
+    if (id >= h.n_tensors || p->tensors[id].kind != EMX_T_OUTPUT) return set_error(EMX_ERR_PLAN_FORMAT, "bad output id");
+  p->entries.resize(h.n_ops);
+  for (size_t i = 0; i < p->ops.size(); ++i) {
+    const PlanOp& op = p->ops[i];
+    p->entries[i] = find_kernel(op.kernel);
+    if (!p->entries[i]) return set_error(EMX_ERR_UNSUPPORTED, "op %zu: unknown kernel id %u", i, op.kernel);
+    if (op.n_tensors > EMX_OP_MAX_TENSORS) return set_error(EMX_ERR_PLAN_FORMAT, "op %zu: too many tensors", i);
+    for (uint32_t j = 0; j < op.n_tensors; ++j)
+      if (op.t[j] < -1 || op.t[j] >= (int32_t)h.n_tensors)
+        return set_error(EMX_ERR_PLAN_FORMAT, "op %zu: tensor ref %d out of range", i, op.t[j]);
+  }
+  return EMX_OK;
+}
+
+int load_common(emx_plan* p, const void* plan, size_t plan_len, int device) {
+  int rc = parse_plan(p, plan, plan_len);
+  if (rc) return rc;
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return set_error(EMX_ERR_INVALID_ARGUMENT, "device %d of %d", device, ndev);
+  p->device = device;
+  CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  CUDA_TRY(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+  if (cudaMalloc(&p->d_arena, p->hdr.arena_bytes ? p->hdr.arena_bytes : 256) != cudaSuccess)
+    return set_error(EMX_ERR_OUT_OF_MEMORY, "arena allocation of %llu bytes failed",
+                     (unsigned long long)p->hdr.arena_bytes);
+  if (cudaMalloc(&p->d_weights, p->hdr.weight_bytes ? p->hdr.weight_bytes : 256) != cudaSuccess)
+    return set_error(EMX_ERR_OUT_OF_MEMORY, "weight allocation of %llu bytes failed",
+                     (unsigned long long)p->hdr.weight_bytes);
+  CUDA_TRY(cudaMalloc(&p->d_error, 256), "error word");
+  CUDA_TRY(cudaMemset(p->d_error, 0, 256), "error word");
+  // zero the arena once: zero-bordered layouts rely on borders never being written
+  CUDA_TRY(cudaMemset(p->d_arena, 0, p->hdr.arena_bytes ? p->hdr.arena_bytes : 256), "arena memset");
+  CUDA_TRY(cudaStreamCreateWithFlags(&p->own_stream, cudaStreamNonBlocking), "stream");
+  p->ptrs.assign(p->tensors.size(), nullptr);
+  for (size_t i = 0; i < p->tensors.size(); ++i) {
+    const PlanTensor& t = p->tensors[i];
+    uint8_t* base = static_cast<uint8_t*>(t.kind == EMX_T_WEIGHT ? p->d_weights : p->d_arena);
+    p->ptrs[i] = base + t.offset;
+  }
+  return EMX_OK;
+}
+
+int prepare_ops(emx_plan* p) {
+  p->states.resize(p->ops.size());
+  for (size_t i = 0; i < p->ops.size(); ++i) {
+    if (!p->entries[i]->prepare) continue;
+    char msg[512] = {0};
+    int rc = p->entries[i]->prepare(p->ops[i], p->ptrs.data(), &p->states[i], p->device, msg, sizeof(msg));
+    if (rc) return set_error(rc, "op %zu (%s): %s", i, p->entries[i]->name, msg);
+  }
+  return EMX_OK;
+}
+
+void destroy(emx_plan* p) {
+  if (!p) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(p->device);
+  for (auto e : p->ev_begin) cudaEventDestroy(e);
+  for (auto e : p->ev_end) cudaEventDestroy(e);
+  if (p->own_stream) cudaStreamDestroy(p->own_stream);
+  if (p->d_arena) cudaFree(p->d_arena);
+  if (p->d_weights) cudaFree(p->d_weights);
+  if (p->d_error) cudaFree(p->d_error);
+  cudaSetDevice(cur);
+  delete p;
+}
+
+bool is_device_pointer(const void* ptr) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// bytes of one batch row along axis 0 (tensor must be batched)
+size_t row_bytes(const PlanTensor& t) {
+  if (t.rank < 1 || t.dims[0] <= 0) return 0;
+  return (size_t)(t.nbytes / (uint64_t)t.dims[0]);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* emx_b200_version(void) { return "0.1.0"; }
+
+const char* emx_b200_last_error(void) { return g_last_error.c_str(); }
+
+int emx_b200_plan_load_mem(const void* plan, size_t plan_len, const void* weights, size_t weights_len, int device,
+                           emx_plan_t** out) {
+  if (!out) return set_error(EMX_ERR_INVALID_ARGUMENT, "out is NULL");
+  *out = nullptr;
+  emx_plan* p = new emx_plan();
+  int rc = load_common(p, plan, plan_len, device);
+  if (!rc && weights_len != p->hdr.weight_bytes)
+    rc = set_error(EMX_ERR_WEIGHTS, "weight blob is %zu bytes, plan expects %llu", weights_len,
+                   (unsigned long long)p->hdr.weight_bytes);
+  if (!rc && weights_len) {
+    if (!weights) rc = set_error(EMX_ERR_INVALID_ARGUMENT, "weights is NULL");
+    else if (cudaMemcpy(p->d_weights, weights, weights_len, cudaMemcpyHostToDevice) != cudaSuccess)
+      rc = set_error(EMX_ERR_CUDA, "weight upload failed");
+  }
+  if (!rc) rc = prepare_ops(p);
+  if (rc) {
+    destroy(p);
+    return rc;
+  }
+  g_last_error.clear();
+  *out = p;
+  return EMX_OK;
+}
+
+int emx_b200_plan_load(const void* plan, size_t plan_len, const char* weights_path, int device, emx_plan_t** out) {
+  if (!out) return set_error(EMX_ERR_INVALID_ARGUMENT, "out is NULL");
+  *out = nullptr;
+  if (plan_len < sizeof(PlanHeader) || !plan) return set_error(EMX_ERR_PLAN_FORMAT, "plan blob too short");
+  PlanHeader h;
+  memcpy(&h, plan, sizeof(h));
+  std::vector<uint8_t> buf;
+  if (h.weight_bytes) {
+    if (!weights_path) return set_error(EMX_ERR_WEIGHTS, "plan has %llu weight bytes but no weights path",
+                                        (unsigned long long)h.weight_bytes);
+    FILE* f = fopen(weights_path, "rb");
+    if (!f) return set_error(EMX_ERR_WEIGHTS, "cannot open weights file '%s'", weights_path);
+    buf.resize(h.weight_bytes);
+    size_t got = fread(buf.data(), 1, buf.size(), f);
+    int extra = fgetc(f);
+    fclose(f);
+    if (got != buf.size())
+      return set_error(EMX_ERR_WEIGHTS, "weights file '%s': short read (%zu of %llu bytes)", weights_path, got,
+                       (unsigned long long)h.weight_bytes);
+    if (extra != EOF) return set_error(EMX_ERR_WEIGHTS, "weights file '%s' is longer than the plan expects", weights_path);
+  }
+  return emx_b200_plan_load_mem(plan, plan_len, buf.data(), buf.size(), device, out);
+}
+
+int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs, int64_t batch_begin,
+                 int64_t batch_count, void* stream_) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if ((p->inputs.size() && !inputs) || (p->outputs.size() && !outputs))
+    return set_error(EMX_ERR_INVALID_ARGUMENT, "inputs/outputs array is NULL");
+  const int64_t full = p->hdr.batch;
+  if (batch_count < 0) batch_count = full;
+  if (batch_begin < 0 || batch_count < 0 || (full > 0 && batch_begin + batch_count > full))
+    return set_error(EMX_ERR_INVALID_ARGUMENT, "batch range [%lld, +%lld) outside [0, %lld)", (long long)batch_begin,
+                     (long long)batch_count, (long long)full);
+  const bool sliced = full > 0 && (batch_begin != 0 || batch_count != full);
+  if (sliced && !(p->hdr.flags & EMX_PLAN_BATCHABLE))
+    return set_error(EMX_ERR_INVALID_ARGUMENT, "this plan cannot run a batch slice (batch axis is not axis 0)");
+  if (full > 0 && batch_count == 0) return EMX_OK;
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  cudaStream_t stream = stream_ ? static_cast<cudaStream_t>(stream_) : p->own_stream;
+  p->last_stream = stream;
+  p->pending.clear();
+  for (size_t i = 0; i < p->inputs.size(); ++i) {
+    const PlanTensor& t = p->tensors[p->inputs[i]];
+    const void* src = inputs[i];
+    if (!src) return set_error(EMX_ERR_INVALID_ARGUMENT, "input %zu is NULL", i);
+    size_t off = 0, bytes = t.nbytes;
+    if (full > 0 && t.batch_axis == 0) {
+      off = (size_t)batch_begin * row_bytes(t);
+      bytes = (size_t)batch_count * row_bytes(t);
+    }
+    void* staging = static_cast<uint8_t*>(p->d_arena) + t.offset;
+    if (is_device_pointer(src)) {
+      p->ptrs[p->inputs[i]] = const_cast<uint8_t*>(static_cast<const uint8_t*>(src) + off);
+    } else {
+      CUDA_TRY(cudaMemcpyAsync(staging, static_cast<const uint8_t*>(src) + off, bytes, cudaMemcpyHostToDevice, stream),
+               "input upload");
+      p->ptrs[p->inputs[i]] = staging;
+    }
+  }
+  for (size_t i = 0; i < p->outputs.size(); ++i) {
+    const PlanTensor& t = p->tensors[p->outputs[i]];
+    void* dst = outputs[i];
+    if (!dst) return set_error(EMX_ERR_INVALID_ARGUMENT, "output %zu is NULL", i);
+    size_t off = 0, bytes = t.nbytes;
+    if (full > 0 && t.batch_axis == 0) {
+      off = (size_t)batch_begin * row_bytes(t);
+      bytes = (size_t)batch_count * row_bytes(t);
+    }
+    void* staging = static_cast<uint8_t*>(p->d_arena) + t.offset;
+    if (is_device_pointer(dst)) {
+      p->ptrs[p->outputs[i]] = static_cast<uint8_t*>(dst) + off;
+    } else {
+      p->ptrs[p->outputs[i]] = staging;
+      p->pending.push_back({static_cast<uint8_t*>(dst) + off, staging, bytes});
+    }
+  }
+  emx::LaunchCtx ctx{stream, p->d_error, full > 0 ? batch_count : 0, p->num_sms};
+  int launches = 0;
+  for (size_t i = 0; i < p->ops.size(); ++i) {
+    if (p->profiling) cudaEventRecord(p->ev_begin[i], stream);
+    int rc = p->entries[i]->launch(p->ops[i], p->ptrs.data(), &p->states[i], ctx, &launches);
+    if (p->profiling) cudaEventRecord(p->ev_end[i], stream);
+    if (rc) {
+      cudaError_t e = cudaGetLastError();
+      return set_error(rc == EMX_ERR_CUDA ? EMX_ERR_CUDA : rc, "op %zu (%s) launch failed: %s", i,
+                       p->entries[i]->name, cudaGetErrorString(e));
+    }
+  }
+  for (const auto& pd : p->pending)
+    CUDA_TRY(cudaMemcpyAsync(pd.host, pd.dev, pd.bytes, cudaMemcpyDeviceToHost, stream), "output download");
+  p->launches_total += launches;
+  p->launches_last = launches;
+  p->events_pending = p->profiling;
+  return EMX_OK;
+}
+
+int emx_b200_sync(emx_plan_t* p) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  CUDA_TRY(cudaStreamSynchronize(p->last_stream ? p->last_stream : p->own_stream), "stream synchronize");
+  if (p->events_pending) {
+    for (size_t i = 0; i < p->ops.size(); ++i) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, p->ev_begin[i], p->ev_end[i]) == cudaSuccess) p->op_ms[i] += ms;
+    }
+    ++p->profiled_runs;
+    p->events_pending = false;
+  }
+  int err = 0;
+  CUDA_TRY(cudaMemcpy(&err, p->d_error, sizeof(int), cudaMemcpyDeviceToHost), "error word read");
+  if (err) {
+    cudaMemset(p->d_error, 0, sizeof(int));
+    return set_error(EMX_ERR_DEVICE_TIMEOUT, "device-side wait gave up (code %d)", err);
+  }
+  return EMX_OK;
+}
+
+void emx_b200_plan_free(emx_plan_t* p) { destroy(p); }
+
+int emx_b200_plan_info(const emx_plan_t* p, emx_plan_info_t* info) {
+  if (!p || !info) return set_error(EMX_ERR_INVALID_ARGUMENT, "NULL argument");
+  info->device = p->device;
+  info->n_inputs = (int32_t)p->inputs.size();
+  info->n_outputs = (int32_t)p->outputs.size();
+  info->n_ops = (int32_t)p->ops.size();
+  info->batch = p->hdr.batch;
+  info->arena_bytes = (int64_t)p->hdr.arena_bytes;
+  info->weight_bytes = (int64_t)p->hdr.weight_bytes;
+  info->launches_per_run = p->launches_last;
+  return EMX_OK;
+}
+
+int64_t emx_b200_launch_count(const emx_plan_t* p) { return p ? p->launches_total : -1; }
+
+int emx_b200_set_profiling(emx_plan_t* p, int enable) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  if (enable && p->ev_begin.empty()) {
+    p->ev_begin.resize(p->ops.size());
+    p->ev_end.resize(p->ops.size());
+    for (size_t i = 0; i < p->ops.size(); ++i) {
+      CUDA_TRY(cudaEventCreate(&p->ev_begin[i]), "event");
+      CUDA_TRY(cudaEventCreate(&p->ev_end[i]), "event");
+    }
+  }
+  p->profiling = enable != 0;
+  p->op_ms.assign(p->ops.size(), 0.0);
+  p->profiled_runs = 0;
+  p->events_pending = false;
+  return EMX_OK;
+}
+
+int emx_b200_op_times(const emx_plan_t* p, double* ms, int32_t n_ops, int64_t* runs) {
+  if (!p || !ms || n_ops < (int32_t)p->ops.size()) return set_error(EMX_ERR_INVALID_ARGUMENT, "bad arguments");
+  for (size_t i = 0; i < p->ops.size(); ++i) ms[i] = i < p->op_ms.size() ? p->op_ms[i] : 0.0;
+  if (runs) *runs = p->profiled_runs;
+  return EMX_OK;
+}
+
+}  // extern "C"

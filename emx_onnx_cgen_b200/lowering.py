@@ -1,0 +1,390 @@
+"""Lowering of a ``GraphSpec`` into ``LoweredModel`` objects for the hot-path ops.
+
+The drop-in boundary of this backend is the reference compiler's
+``LoweredModel`` (src/emx_onnx_cgen/codegen/c_emitter.py:333-350), produced by
+``Compiler._lower_model`` (compiler.py:514-606).  ``B200PlanEmitter`` reads
+lowered ops by class name and field name only, so it accepts the reference's
+own objects unchanged.  Where the reference compiler is not installed (the GPU
+hosts that run the tests and the benchmark), this module produces objects with
+the same class names and the same fields for the ops this backend runs:
+
+  QLinearConvOp   ir/ops/nn.py:4734     QLinearAddOp  ir/ops/elementwise.py:1114
+  GemmOp          ir/ops/nn.py:1624     UnaryOp       ir/ops/elementwise.py:538
+  BinaryOp        ir/ops/elementwise.py:23
+  MatMulNBitsOp   ir/ops/nn.py:1035     AttentionOp   ir/ops/nn.py:2478
+  LstmOp          ir/ops/nn.py:8449
+
+Attribute defaults follow the reference's lowerings (lowering/qlinear_conv.py:40,
+qlinear_add.py:31, gemm.py:9, matmul_nbits.py:120, attention.py:363 (scale
+default 1/sqrt(head_size), attention.py:313), lstm.py:335).  The test suite
+checks, wherever the reference is importable, that both lowerings yield
+byte-identical plans.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from enum import Enum
+
+import numpy as np
+
+from .spec import GraphSpec
+
+
+class ScalarType(str, Enum):
+    """Mirror of the reference's ScalarType values used on the hot path."""
+    F32 = "f32"
+    F16 = "f16"
+    F64 = "f64"
+    U8 = "u8"
+    I8 = "i8"
+    I32 = "i32"
+    I64 = "i64"
+    BOOL = "bool"
+
+
+class ScalarFunction(str, Enum):
+    RELU = "relu"
+    SWISH = "swish"
+    SIGMOID = "sigmoid"
+    TANH = "tanh"
+    MUL = "mul"
+    ADD = "add"
+
+
+class UnsupportedOpError(Exception):
+    """Same role as the reference's errors.UnsupportedOpError (errors.py:5)."""
+
+
+@dataclass(frozen=True)
+class ConstTensor:
+    name: str
+    shape: tuple[int, ...]
+    data: np.ndarray
+    dtype: ScalarType
+
+
+@dataclass
+class OpContext:
+    shapes: dict[str, tuple[int, ...]]
+    dtypes: dict[str, ScalarType]
+
+    def shape(self, name: str) -> tuple[int, ...]:
+        return self.shapes[name]
+
+    def dtype(self, name: str) -> ScalarType:
+        return self.dtypes[name]
+
+
+@dataclass(frozen=True)
+class LoweredModel:
+    name: str
+    input_names: tuple[str, ...]
+    input_shapes: tuple[tuple[int, ...], ...]
+    input_dtypes: tuple[ScalarType, ...]
+    output_names: tuple[str, ...]
+    output_shapes: tuple[tuple[int, ...], ...]
+    output_dtypes: tuple[ScalarType, ...]
+    constants: tuple[ConstTensor, ...]
+    ops: tuple[object, ...]
+    op_context: OpContext
+
+
+# ------------------------------------------------------------------ op dataclasses
+@dataclass(frozen=True)
+class QLinearConvOp:
+    input0: str
+    input_scale: str
+    input_zero_point: str
+    weights: str
+    weight_scale: str
+    weight_zero_point: str
+    output_scale: str
+    output_zero_point: str
+    bias: str | None
+    output: str
+    batch: int
+    in_channels: int
+    out_channels: int
+    spatial_rank: int
+    in_spatial: tuple[int, ...]
+    out_spatial: tuple[int, ...]
+    kernel_shape: tuple[int, ...]
+    strides: tuple[int, ...]
+    pads: tuple[int, ...]
+    dilations: tuple[int, ...]
+    group: int
+    input_dtype: ScalarType
+    weight_dtype: ScalarType
+    dtype: ScalarType
+    weight_scale_per_channel: bool
+    weight_zero_per_channel: bool
+
+
+@dataclass(frozen=True)
+class QLinearAddOp:
+    input0: str
+    input0_scale: str
+    input0_zero_point: str
+    input1: str
+    input1_scale: str
+    input1_zero_point: str
+    output_scale: str
+    output_zero_point: str
+    output: str
+    input0_shape: tuple[int, ...]
+    input1_shape: tuple[int, ...]
+    output_shape: tuple[int, ...]
+    input0_dtype: ScalarType
+    input1_dtype: ScalarType
+    dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class GemmOp:
+    input_a: str
+    input_b: str
+    input_c: str | None
+    output: str
+    trans_a: int
+    trans_b: int
+    alpha: float | int
+    beta: float | int
+
+
+@dataclass(frozen=True)
+class UnaryOp:
+    input0: str
+    output: str
+    function: ScalarFunction
+    params: tuple[float, ...] = ()
+
+
+@dataclass(frozen=True)
+class BinaryOp:
+    input0: str
+    input1: str
+    output: str
+    function: ScalarFunction
+
+
+@dataclass(frozen=True)
+class MatMulNBitsOp:
+    input0: str
+    input1: str
+    scales: str
+    zero_points: str | None
+    bias: str | None
+    output: str
+    bits: int
+    block_size: int
+    k: int
+    n: int
+    accuracy_level: int
+    n_blocks_per_col: int
+    blob_size: int
+    input0_shape: tuple[int, ...]
+    output_shape: tuple[int, ...]
+    m: int
+    input0_dtype: ScalarType
+    output_dtype: ScalarType
+    scales_dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class AttentionOp:
+    input_q: str
+    input_k: str
+    input_v: str
+    input_attn_mask: str | None
+    input_past_key: str | None
+    input_past_value: str | None
+    output: str
+    output_present_key: str | None
+    output_present_value: str | None
+    output_qk_matmul: str | None
+    batch: int
+    q_heads: int
+    kv_heads: int
+    q_seq: int
+    kv_seq: int
+    total_seq: int
+    past_seq: int
+    qk_head_size: int
+    v_head_size: int
+    scale: float
+    is_causal: bool
+    softcap: float
+    q_rank: int
+    head_group_size: int
+    dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class LstmOp:
+    input_x: str
+    input_w: str
+    input_r: str
+    input_b: str | None
+    input_sequence_lens: str | None
+    input_initial_h: str | None
+    input_initial_c: str | None
+    input_p: str | None
+    output_y: str | None
+    output_y_h: str | None
+    output_y_c: str | None
+    seq_length: int
+    batch_size: int
+    input_size: int
+    hidden_size: int
+    num_directions: int
+    direction: str
+    layout: int
+    input_forget: int
+    clip: float | None
+    activation_kinds: tuple[int, ...]
+    dtype: ScalarType
+
+
+# ------------------------------------------------------------------ lowering
+def _st(suffix: str) -> ScalarType:
+    return ScalarType(suffix)
+
+
+def lower(spec: GraphSpec) -> LoweredModel:
+    shapes: dict[str, tuple[int, ...]] = {}
+    dtypes: dict[str, ScalarType] = {}
+    for t in (*spec.inputs, *spec.outputs, *spec.values):
+        shapes[t.name] = tuple(t.shape)
+        dtypes[t.name] = _st(t.dtype)
+    consts = []
+    for name, arr in spec.initializers.items():
+        t = spec.tensor(name)
+        shapes[name] = tuple(arr.shape)
+        dtypes[name] = _st(t.dtype)
+        consts.append(ConstTensor(name, tuple(arr.shape), arr, _st(t.dtype)))
+    ops = []
+    for node in spec.nodes:
+        ops.append(_lower_node(node, shapes, dtypes))
+    return LoweredModel(
+        name=spec.name,
+        input_names=tuple(t.name for t in spec.inputs),
+        input_shapes=tuple(tuple(t.shape) for t in spec.inputs),
+        input_dtypes=tuple(_st(t.dtype) for t in spec.inputs),
+        output_names=tuple(t.name for t in spec.outputs),
+        output_shapes=tuple(tuple(t.shape) for t in spec.outputs),
+        output_dtypes=tuple(_st(t.dtype) for t in spec.outputs),
+        constants=tuple(consts),
+        ops=tuple(ops),
+        op_context=OpContext(shapes, dtypes),
+    )
+
+
+def _lower_node(node, shapes, dtypes):
+    a = dict(node.attrs)
+    ins = list(node.inputs)
+    op = node.op_type
+    if op == "QLinearConv":
+        x, w = ins[0], ins[3]
+        n, c, *sp = shapes[x]
+        oc, _, *ks = shapes[w]
+        rank = len(sp)
+        ks = tuple(a.get("kernel_shape", ks))
+        strides = tuple(a.get("strides", [1] * rank))
+        dil = tuple(a.get("dilations", [1] * rank))
+        pads = tuple(a.get("pads", [0] * (2 * rank)))
+        out_sp = tuple((sp[i] + pads[i] + pads[i + rank] - ((ks[i] - 1) * dil[i] + 1)) // strides[i] + 1
+                       for i in range(rank))
+        y = node.outputs[0]
+        shapes[y] = (n, oc, *out_sp)
+        dtypes[y] = dtypes[ins[7]]
+        ws_shape, wz_shape = shapes[ins[4]], shapes[ins[5]]
+        return QLinearConvOp(
+            input0=x, input_scale=ins[1], input_zero_point=ins[2], weights=w, weight_scale=ins[4],
+            weight_zero_point=ins[5], output_scale=ins[6], output_zero_point=ins[7],
+            bias=ins[8] if len(ins) > 8 and ins[8] else None, output=y, batch=n, in_channels=c,
+            out_channels=oc, spatial_rank=rank, in_spatial=tuple(sp), out_spatial=out_sp, kernel_shape=ks,
+            strides=strides, pads=pads, dilations=dil, group=int(a.get("group", 1)),
+            input_dtype=dtypes[x], weight_dtype=dtypes[w], dtype=dtypes[ins[7]],
+            weight_scale_per_channel=int(np.prod(ws_shape)) > 1,
+            weight_zero_per_channel=int(np.prod(wz_shape)) > 1)
+    if op == "QLinearAdd":
+        y = node.outputs[0]
+        shapes[y] = tuple(np.broadcast_shapes(shapes[ins[0]], shapes[ins[3]]))
+        dtypes[y] = dtypes[ins[7]]
+        return QLinearAddOp(
+            input0=ins[0], input0_scale=ins[1], input0_zero_point=ins[2], input1=ins[3], input1_scale=ins[4],
+            input1_zero_point=ins[5], output_scale=ins[6], output_zero_point=ins[7], output=y,
+            input0_shape=shapes[ins[0]], input1_shape=shapes[ins[3]], output_shape=shapes[y],
+            input0_dtype=dtypes[ins[0]], input1_dtype=dtypes[ins[3]], dtype=dtypes[y])
+    if op == "Gemm":
+        ta, tb = int(a.get("transA", 0)), int(a.get("transB", 0))
+        sa, sb = shapes[ins[0]], shapes[ins[1]]
+        m = sa[1] if ta else sa[0]
+        nn_ = sb[0] if tb else sb[1]
+        y = node.outputs[0]
+        shapes[y] = (m, nn_)
+        dtypes[y] = dtypes[ins[0]]
+        return GemmOp(input_a=ins[0], input_b=ins[1], input_c=ins[2] if len(ins) > 2 and ins[2] else None,
+                      output=y, trans_a=ta, trans_b=tb, alpha=float(a.get("alpha", 1.0)),
+                      beta=float(a.get("beta", 1.0)))
+    if op in ("Relu", "Swish", "Sigmoid", "Tanh"):
+        y = node.outputs[0]
+        shapes[y] = shapes[ins[0]]
+        dtypes[y] = dtypes[ins[0]]
+        fn = {"Relu": ScalarFunction.RELU, "Swish": ScalarFunction.SWISH, "Sigmoid": ScalarFunction.SIGMOID,
+              "Tanh": ScalarFunction.TANH}[op]
+        params = (float(a.get("alpha", 1.0)),) if op == "Swish" else ()
+        return UnaryOp(input0=ins[0], output=y, function=fn, params=params)
+    if op in ("Mul", "Add"):
+        y = node.outputs[0]
+        shapes[y] = tuple(np.broadcast_shapes(shapes[ins[0]], shapes[ins[1]]))
+        dtypes[y] = dtypes[ins[0]]
+        return BinaryOp(input0=ins[0], input1=ins[1], output=y,
+                        function=ScalarFunction.MUL if op == "Mul" else ScalarFunction.ADD)
+    if op == "MatMulNBits":
+        k, n = int(a["K"]), int(a["N"])
+        bits, block = int(a.get("bits", 4)), int(a.get("block_size", 32))
+        nb = (k + block - 1) // block
+        xs = shapes[ins[0]]
+        y = node.outputs[0]
+        shapes[y] = (*xs[:-1], n)
+        dtypes[y] = dtypes[ins[0]]
+        return MatMulNBitsOp(
+            input0=ins[0], input1=ins[1], scales=ins[2],
+            zero_points=ins[3] if len(ins) > 3 and ins[3] else None,
+            bias=ins[5] if len(ins) > 5 and ins[5] else None, output=y, bits=bits, block_size=block, k=k, n=n,
+            accuracy_level=int(a.get("accuracy_level", 0)), n_blocks_per_col=nb, blob_size=block * bits // 8,
+            input0_shape=xs, output_shape=shapes[y], m=int(np.prod(xs[:-1])), input0_dtype=dtypes[ins[0]],
+            output_dtype=dtypes[ins[0]], scales_dtype=dtypes[ins[2]])
+    if op == "Attention":
+        b, hq, tq, d = shapes[ins[0]]
+        _, hkv, tkv, _ = shapes[ins[1]]
+        dv = shapes[ins[2]][3]
+        y = node.outputs[0]
+        shapes[y] = (b, hq, tq, dv)
+        dtypes[y] = dtypes[ins[0]]
+        scale = float(a["scale"]) if "scale" in a else 1.0 / math.sqrt(d)
+        return AttentionOp(
+            input_q=ins[0], input_k=ins[1], input_v=ins[2], input_attn_mask=None, input_past_key=None,
+            input_past_value=None, output=y, output_present_key=None, output_present_value=None,
+            output_qk_matmul=None, batch=b, q_heads=hq, kv_heads=hkv, q_seq=tq, kv_seq=tkv, total_seq=tkv,
+            past_seq=0, qk_head_size=d, v_head_size=dv, scale=scale, is_causal=bool(a.get("is_causal", 0)),
+            softcap=float(a.get("softcap", 0.0)), q_rank=4, head_group_size=hq // hkv, dtype=dtypes[ins[0]])
+    if op == "LSTM":
+        t, b, i = shapes[ins[0]]
+        h = int(a["hidden_size"])
+        outs = list(node.outputs) + [""] * (3 - len(node.outputs))
+        for name, shp in zip(outs, [(t, 1, b, h), (1, b, h), (1, b, h)]):
+            if name:
+                shapes[name] = shp
+                dtypes[name] = dtypes[ins[0]]
+        return LstmOp(
+            input_x=ins[0], input_w=ins[1], input_r=ins[2], input_b=ins[3] if len(ins) > 3 and ins[3] else None,
+            input_sequence_lens=None, input_initial_h=None, input_initial_c=None, input_p=None,
+            output_y=outs[0] or None, output_y_h=outs[1] or None, output_y_c=outs[2] or None, seq_length=t,
+            batch_size=b, input_size=i, hidden_size=h, num_directions=1,
+            direction=str(a.get("direction", "forward")), layout=int(a.get("layout", 0)),
+            input_forget=int(a.get("input_forget", 0)), clip=a.get("clip"), activation_kinds=(2, 1, 1),
+            dtype=dtypes[ins[0]])
+    raise UnsupportedOpError(f"{op} has no B200 kernel")

@@ -1,0 +1,543 @@
+"""B200PlanEmitter: LoweredModel -> static launch plan (+ packed weight blob).
+
+This is the new emit target beside the reference's ``CEmitter.emit_model``
+(src/emx_onnx_cgen/codegen/c_emitter.py:1312) and ``collect_weight_data``
+(:4398).  Instead of rendering one C loop nest per lowered op it decides, for
+the same op sequence:
+
+* a kernel per op (or per fused group of ops), in ``LoweredModel.ops`` order;
+* a fixed place for every tensor: weights at offsets in one weight blob
+  (re-packed into the layouts the kernels read, e.g. conv weights as
+  tensor-core operand images), every intermediate at an offset in one device
+  arena sized here, so nothing is allocated at run time;
+* internal layouts between kernels (zero-bordered NHWC activations between
+  tensor-core convolutions) and graph-level fusions (QLinearAdd into the
+  epilogue of the convolution that produces one of its operands).
+
+Ops without a B200 kernel raise ``UnsupportedOpError``: there is no CPU
+fallback.  The emitter only reads op class names and fields, so it accepts the
+reference's own ``LoweredModel`` as well as ``emx_onnx_cgen_b200.lowering``'s.
+
+The binary format is defined in ``csrc/plan_format.h``; kernel ids and
+parameter slots in ``csrc/kernels.h`` (mirrored in ``kernel_ids.py``).
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import kernel_ids as K
+from .lowering import UnsupportedOpError
+
+PLAN_MAGIC = 0x50584D45
+PLAN_VERSION = 1
+MAX_RANK = 8
+OP_MAX_T, OP_MAX_I, OP_MAX_F = 12, 40, 8
+T_WEIGHT, T_INPUT, T_OUTPUT, T_TEMP = 0, 1, 2, 3
+DT = {"f32": 1, "u8": 2, "i8": 3, "i32": 6, "i64": 7, "f16": 10, "f64": 11}
+NP = {"f32": np.float32, "u8": np.uint8, "i8": np.int8, "i32": np.int32, "i64": np.int64,
+      "f16": np.float16, "f64": np.float64}
+ALIGN = 256
+
+_HDR = struct.Struct("<IIIIIIqQQII")
+_TENSOR = struct.Struct("<IIQQii8q")
+_OP = struct.Struct("<II12i40q8d")
+assert _HDR.size == 56 and _TENSOR.size == 96 and _OP.size == 440
+
+
+def _suffix(dt) -> str:
+    return str(getattr(dt, "value", dt))
+
+
+def _name(obj) -> str:
+    return type(obj).__name__
+
+
+def _fn(op) -> str:
+    f = getattr(op, "function", None)
+    return str(getattr(f, "name", f)).upper()
+
+
+@dataclass
+class PlanTensor:
+    kind: int
+    dtype: str
+    offset: int
+    nbytes: int
+    shape: tuple[int, ...]
+    batch_axis: int = -1
+    name: str = ""
+
+
+@dataclass
+class PlanOp:
+    kernel: int
+    tensors: list[int]
+    ip: dict[int, int] = field(default_factory=dict)
+    fp: dict[int, float] = field(default_factory=dict)
+    label: str = ""
+
+
+@dataclass
+class Plan:
+    """A serialisable launch plan: ``plan_bytes`` + ``weight_bytes`` is what
+    ``emx_b200_plan_load_mem`` consumes."""
+    name: str
+    plan_bytes: bytes
+    weight_bytes: bytes
+    input_names: tuple[str, ...]
+    input_shapes: tuple[tuple[int, ...], ...]
+    input_dtypes: tuple[str, ...]
+    output_names: tuple[str, ...]
+    output_shapes: tuple[tuple[int, ...], ...]
+    output_dtypes: tuple[str, ...]
+    batch: int
+    ops: list[PlanOp]
+    tensors: list[PlanTensor]
+    arena_bytes: int
+
+    def describe(self) -> str:
+        lines = [f"plan {self.name}: {len(self.ops)} ops, arena {self.arena_bytes} B, "
+                 f"weights {len(self.weight_bytes)} B, batch {self.batch}"]
+        for op in self.ops:
+            lines.append(f"  {K.NAMES.get(op.kernel, op.kernel):>16}  {op.label}")
+        return "\n".join(lines)
+
+
+class _Builder:
+    def __init__(self):
+        self.tensors: list[PlanTensor] = []
+        self.weights = bytearray()
+        self.arena = 0
+        self.ops: list[PlanOp] = []
+
+    def weight(self, arr: np.ndarray, dtype: str, name: str = "") -> int:
+        arr = np.ascontiguousarray(arr)
+        off = len(self.weights)
+        self.weights += arr.tobytes()
+        pad = (-len(self.weights)) % ALIGN
+        self.weights += b"\0" * pad
+        self.tensors.append(PlanTensor(T_WEIGHT, dtype, off, arr.nbytes, tuple(arr.shape), -1, name))
+        return len(self.tensors) - 1
+
+    def arena_tensor(self, kind: int, dtype: str, shape, nbytes: int | None = None, batch_axis: int = -1,
+                     name: str = "") -> int:
+        shape = tuple(int(s) for s in shape)
+        if nbytes is None:
+            nbytes = int(np.prod(shape, dtype=np.int64)) * np.dtype(NP[dtype]).itemsize
+        off = self.arena
+        self.arena += (nbytes + ALIGN - 1) // ALIGN * ALIGN
+        self.tensors.append(PlanTensor(kind, dtype, off, nbytes, shape, batch_axis, name))
+        return len(self.tensors) - 1
+
+    def op(self, kernel: int, tensors, ip=None, fp=None, label="") -> None:
+        self.ops.append(PlanOp(kernel, list(tensors), dict(ip or {}), dict(fp or {}), label))
+
+    def serialize(self, inputs: list[int], outputs: list[int], batch: int, flags: int) -> bytes:
+        out = bytearray()
+        arena = self.arena + ALIGN
+        out += _HDR.pack(PLAN_MAGIC, PLAN_VERSION, len(self.tensors), len(self.ops), len(inputs), len(outputs),
+                         batch, arena, len(self.weights), flags, 0)
+        for t in self.tensors:
+            dims = list(t.shape)[:MAX_RANK] + [0] * (MAX_RANK - min(len(t.shape), MAX_RANK))
+            out += _TENSOR.pack(t.kind, DT[t.dtype], t.offset, t.nbytes, len(t.shape), t.batch_axis, *dims)
+        for ids in (inputs, outputs):
+            slots = list(ids) + [0] * (len(ids) % 2)
+            out += struct.pack(f"<{len(slots)}I", *slots)
+        for op in self.ops:
+            t = op.tensors + [-1] * (OP_MAX_T - len(op.tensors))
+            ip = [0] * OP_MAX_I
+            for k, v in op.ip.items():
+                ip[k] = int(v)
+            fp = [0.0] * OP_MAX_F
+            for k, v in op.fp.items():
+                fp[k] = float(v)
+            out += _OP.pack(op.kernel, len(op.tensors), *t, *ip, *fp)
+        return bytes(out)
+
+
+@dataclass
+class _Padded:
+    tid: int
+    hp: int
+    wp: int
+    pt: int
+    pl: int
+    xor: int
+
+
+class B200PlanEmitter:
+    """Emit target producing a B200 launch plan from a LoweredModel."""
+
+    def __init__(self, *, use_tensor_cores: bool = True):
+        self.use_tensor_cores = use_tensor_cores
+
+    # ------------------------------------------------------------------ entry
+    def emit_plan(self, model) -> Plan:
+        ctx = model.op_context
+        self._consts = {c.name: np.asarray(c.data, dtype=NP[_suffix(c.dtype)]).reshape(c.shape)
+                        for c in model.constants}
+        self._shape = ctx.shape
+        self._dtype = lambda n: _suffix(ctx.dtype(n))
+        b = _Builder()
+        self._b = b
+        ops = list(model.ops)
+        in_names = tuple(model.input_names)
+        out_names = tuple(model.output_names)
+        in_shapes = tuple(tuple(s) for s in model.input_shapes)
+        out_shapes = tuple(tuple(s) for s in model.output_shapes)
+
+        # batch: common axis-0 extent of every I/O tensor, else not sliceable
+        dims0 = {s[0] for s in (*in_shapes, *out_shapes) if len(s) > 0}
+        batch = dims0.pop() if len(dims0) == 1 else 0
+        flags = 1 if batch > 0 else 0
+
+        self._nchw: dict[str, int] = {}
+        self._padded: dict[str, _Padded] = {}
+        for name, shp in zip(in_names, in_shapes):
+            self._nchw[name] = b.arena_tensor(T_INPUT, self._dtype(name), shp, batch_axis=0 if batch else -1,
+                                              name=name)
+        self._outputs = {}
+        for name, shp in zip(out_names, out_shapes):
+            self._outputs[name] = b.arena_tensor(T_OUTPUT, self._dtype(name), shp,
+                                                 batch_axis=0 if batch else -1, name=name)
+        self._graph_outputs = set(out_names)
+        self._batch = batch
+
+        self._analyse(ops)
+        for i, op in enumerate(ops):
+            if i in self._absorbed:
+                continue
+            handler = getattr(self, "_emit_" + _name(op), None)
+            if handler is None:
+                raise UnsupportedOpError(f"{_name(op)} has no B200 kernel")
+            handler(i, op)
+        for name in out_names:
+            if name not in self._written_outputs:
+                raise UnsupportedOpError(f"graph output {name} is not produced by any op")
+
+        blob = b.serialize([self._nchw[n] for n in in_names], [self._outputs[n] for n in out_names], batch,
+                           flags)
+        return Plan(model.name, blob, bytes(b.weights), in_names, in_shapes,
+                    tuple(_suffix(d) for d in model.input_dtypes), out_names, out_shapes,
+                    tuple(_suffix(d) for d in model.output_dtypes), batch, b.ops, b.tensors, b.arena + ALIGN)
+
+    # ------------------------------------------------------------------ helpers
+    def _const(self, name: str | None, what: str) -> np.ndarray:
+        if name is None:
+            raise UnsupportedOpError(f"{what} missing")
+        if name not in self._consts:
+            raise UnsupportedOpError(f"{what} '{name}' must be an initializer for the B200 plan")
+        return self._consts[name]
+
+    def _scalar(self, name, what):
+        arr = self._const(name, what)
+        if arr.size != 1:
+            raise UnsupportedOpError(f"{what} must be a scalar")
+        return arr.reshape(-1)[0]
+
+    def _dest(self, name: str, dtype: str, shape) -> int:
+        """Tensor id an op should write ``name`` to (graph output or new temp)."""
+        if name in self._graph_outputs:
+            self._written_outputs.add(name)
+            tid = self._outputs[name]
+        else:
+            tid = self._b.arena_tensor(T_TEMP, dtype, shape, name=name)
+        self._nchw[name] = tid
+        return tid
+
+    def _src(self, name: str) -> int:
+        if name in self._nchw:
+            return self._nchw[name]
+        if name in self._consts:
+            arr = self._consts[name]
+            tid = self._b.weight(arr, self._dtype(name), name)
+            self._nchw[name] = tid
+            return tid
+        raise UnsupportedOpError(f"tensor {name} is not available in row-major layout")
+
+    # ------------------------------------------------------------------ analysis
+    def _analyse(self, ops) -> None:
+        self._written_outputs: set[str] = set()
+        self._absorbed: set[int] = set()
+        self._fused_add: dict[int, int] = {}
+        producers: dict[str, int] = {}
+        consumers: dict[str, list[int]] = {}
+        for i, op in enumerate(ops):
+            for nm in self._op_outputs(op):
+                producers[nm] = i
+            for nm in self._op_inputs(op):
+                consumers.setdefault(nm, []).append(i)
+        self._producers, self._consumers = producers, consumers
+
+        # tensor-core eligible convolutions and the activation storage they need
+        self._tc: dict[int, dict] = {}
+        for i, op in enumerate(ops):
+            if _name(op) == "QLinearConvOp":
+                cfg = self._qconv_tc_config(op)
+                if cfg is not None:
+                    self._tc[i] = cfg
+        # fuse QLinearAdd into a tensor-core conv producing one operand
+        for j, op in enumerate(ops):
+            if _name(op) != "QLinearAddOp":
+                continue
+            if tuple(op.input0_shape) != tuple(op.input1_shape):
+                continue
+            for side, other in ((op.input0, op.input1), (op.input1, op.input0)):
+                i = producers.get(side)
+                if i is None or i not in self._tc or i in self._fused_add:
+                    continue
+                if len(consumers.get(side, [])) != 1 or side in self._graph_outputs:
+                    continue
+                if self._dtype(other) not in ("u8", "i8") or self._dtype(op.output) not in ("u8", "i8"):
+                    continue
+                self._fused_add[i] = j
+                self._absorbed.add(j)
+                break
+        # padded-storage requirements (xor, pads) per tensor from tensor-core consumers
+        self._need_pad: dict[str, tuple[int, int, int, int]] = {}  # name -> (pt, pl, pb, pr) + xor
+        self._need_xor: dict[str, int] = {}
+        changed = True
+        while changed:
+            changed = False
+            self._need_pad.clear()
+            self._need_xor.clear()
+            for i, cfg in list(self._tc.items()):
+                op = ops[i]
+                name = op.input0
+                pads = cfg["pads"]
+                if name in self._need_pad and (self._need_pad[name] != pads or self._need_xor[name] != cfg["xor"]):
+                    del self._tc[i]
+                    self._fused_add.pop(i, None)
+                    changed = True
+                    break
+                self._need_pad[name] = pads
+                self._need_xor[name] = cfg["xor"]
+        self._absorbed = set(self._fused_add.values())
+        for i, j in self._fused_add.items():
+            add = ops[j]
+            conv_out = ops[i].output
+            resid = add.input1 if add.input0 == conv_out else add.input0
+            if resid not in self._need_pad:
+                self._need_pad[resid] = (0, 0, 0, 0)
+                self._need_xor[resid] = 0
+        # which produced tensors must (also) exist row-major
+        self._need_rowmajor: set[str] = set(self._graph_outputs)
+        tc_inputs = {ops[i].input0 for i in self._tc}
+        resid_inputs = set()
+        for i, j in self._fused_add.items():
+            add = ops[j]
+            conv_out = ops[i].output
+            resid_inputs.add(add.input1 if add.input0 == conv_out else add.input0)
+        for name, cons in consumers.items():
+            for c in cons:
+                if c in self._absorbed:
+                    continue
+                if c in self._tc and ops[c].input0 == name:
+                    continue
+                self._need_rowmajor.add(name)
+        self._ops = ops
+        del tc_inputs, resid_inputs
+
+    @staticmethod
+    def _op_inputs(op):
+        fields = {
+            "QLinearConvOp": ("input0",), "QLinearAddOp": ("input0", "input1"),
+            "GemmOp": ("input_a", "input_b", "input_c"), "UnaryOp": ("input0",), "BinaryOp": ("input0", "input1"),
+            "MatMulNBitsOp": ("input0",), "AttentionOp": ("input_q", "input_k", "input_v"),
+            "LstmOp": ("input_x",),
+        }.get(_name(op), ())
+        return [getattr(op, f) for f in fields if getattr(op, f, None)]
+
+    @staticmethod
+    def _op_outputs(op):
+        fields = {"LstmOp": ("output_y", "output_y_h", "output_y_c")}.get(_name(op), ("output",))
+        return [getattr(op, f) for f in fields if getattr(op, f, None)]
+
+    # ------------------------------------------------------------------ QLinearConv
+    TC_VARIANTS = {(32, 32), (32, 64), (64, 32), (64, 64), (64, 128), (128, 64), (128, 128)}
+
+    def _qconv_tc_config(self, op):
+        if not self.use_tensor_cores:
+            return None
+        if op.spatial_rank != 2 or tuple(op.strides) != (1, 1) or tuple(op.dilations) != (1, 1) or op.group != 1:
+            return None
+        if (op.in_channels, op.out_channels) not in self.TC_VARIANTS:
+            return None
+        if _suffix(op.weight_dtype) != "i8" or _suffix(op.dtype) not in ("u8", "i8"):
+            return None
+        try:
+            zx = int(self._scalar(op.input_zero_point, "x_zero_point"))
+            wz = self._const(op.weight_zero_point, "w_zero_point")
+            self._const(op.weight_scale, "w_scale")
+            self._scalar(op.input_scale, "x_scale")
+            self._scalar(op.output_scale, "y_scale")
+            self._scalar(op.output_zero_point, "y_zero_point")
+            if op.bias is not None:
+                self._const(op.bias, "bias")
+        except UnsupportedOpError:
+            return None
+        if np.any(wz != 0):
+            return None
+        xdt = _suffix(op.input_dtype)
+        if xdt == "u8" and zx == 128:
+            xor, a_signed = 0x80, 1
+        elif xdt == "u8" and zx == 0:
+            xor, a_signed = 0, 0
+        elif xdt == "i8" and zx == 0:
+            xor, a_signed = 0, 1
+        else:
+            return None
+        kh, kw = op.kernel_shape
+        if kh * kw * op.in_channels * op.out_channels > 160 * 1024 or 128 + kw - 1 > 256:
+            return None
+        pt, pl, pb, pr = op.pads
+        return {"xor": xor, "a_signed": a_signed, "pads": (pt, pl, pb, pr)}
+
+    def _padded_of(self, name: str) -> _Padded:
+        """Zero-bordered NHWC copy of ``name`` (created by a pad op if the
+        producer did not write it directly)."""
+        if name in self._padded:
+            return self._padded[name]
+        pt, pl, pb, pr = self._need_pad[name]
+        xor = self._need_xor[name]
+        n, c, h, w = self._shape(name)
+        hp, wp = h + pt + pb, w + pl + pr
+        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (n, hp, wp, c), name=name + ":nhwc")
+        src = self._src(name)
+        self._b.op(K.K_PAD_NHWC, [src, tid],
+                   {K.PAD_N: n, K.PAD_C: c, K.PAD_H: h, K.PAD_W: w, K.PAD_TOP: pt, K.PAD_LEFT: pl,
+                    K.PAD_HP: hp, K.PAD_WP: wp, K.PAD_XOR: xor}, label=f"{name} -> NHWC")
+        pd = _Padded(tid, hp, wp, pt, pl, xor)
+        self._padded[name] = pd
+        return pd
+
+    def _new_padded(self, name: str) -> _Padded:
+        pt, pl, pb, pr = self._need_pad[name]
+        n, c, h, w = self._shape(name)
+        hp, wp = h + pt + pb, w + pl + pr
+        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (n, hp, wp, c), name=name + ":nhwc")
+        pd = _Padded(tid, hp, wp, pt, pl, self._need_xor[name])
+        self._padded[name] = pd
+        return pd
+
+    def _emit_QLinearConvOp(self, i, op):
+        if i in self._tc:
+            return self._emit_qconv_tc(i, op, self._tc[i])
+        return self._emit_qconv_generic(op)
+
+    def _emit_qconv_generic(self, op):
+        if op.spatial_rank != 2:
+            raise UnsupportedOpError("QLinearConv: only 2-D convolutions have a B200 kernel")
+        xs = np.float32(self._scalar(op.input_scale, "x_scale"))
+        ys = np.float32(self._scalar(op.output_scale, "y_scale"))
+        zx = int(self._scalar(op.input_zero_point, "x_zero_point"))
+        zy = int(self._scalar(op.output_zero_point, "y_zero_point"))
+        w = self._const(op.weights, "weights")
+        ws = self._const(op.weight_scale, "w_scale").astype(np.float32).reshape(-1)
+        wz = self._const(op.weight_zero_point, "w_zero_point").astype(np.int32).reshape(-1)
+        t_w = self._b.weight(w, _suffix(op.weight_dtype), op.weights)
+        t_ws = self._b.weight(ws, "f32")
+        t_wz = self._b.weight(wz, "i32")
+        t_b = -1
+        if op.bias is not None:
+            t_b = self._b.weight(self._const(op.bias, "bias").astype(np.int32), "i32")
+        x = self._src(op.input0)
+        n, c, h, wd = self._shape(op.input0)
+        oh, ow = op.out_spatial
+        y = self._dest(op.output, _suffix(op.dtype), (n, op.out_channels, oh, ow))
+        kh, kw = op.kernel_shape
+        self._b.op(K.K_QCONV_GENERIC, [x, t_w, t_ws, t_wz, t_b, y], {
+            K.QG_N: n, K.QG_C: c, K.QG_H: h, K.QG_W: wd, K.QG_OC: op.out_channels, K.QG_KH: kh, K.QG_KW: kw,
+            K.QG_OH: oh, K.QG_OW: ow, K.QG_SH: op.strides[0], K.QG_SW: op.strides[1], K.QG_PT: op.pads[0],
+            K.QG_PL: op.pads[1], K.QG_DH: op.dilations[0], K.QG_DW: op.dilations[1], K.QG_GROUP: op.group,
+            K.QG_X_SIGNED: int(_suffix(op.input_dtype) == "i8"), K.QG_W_SIGNED: int(_suffix(op.weight_dtype) == "i8"),
+            K.QG_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QG_X_ZERO: zx, K.QG_Y_ZERO: zy,
+            K.QG_WS_PER_CH: int(ws.size > 1), K.QG_WZ_PER_CH: int(wz.size > 1)},
+            {K.QGF_X_SCALE: float(xs), K.QGF_Y_SCALE: float(ys)}, label=f"{op.output} (generic)")
+
+    def _emit_qconv_tc(self, i, op, cfg):
+        xs = np.float32(self._scalar(op.input_scale, "x_scale"))
+        ys = np.float32(self._scalar(op.output_scale, "y_scale"))
+        zy = int(self._scalar(op.output_zero_point, "y_zero_point"))
+        w = self._const(op.weights, "weights").astype(np.int8)
+        oc, cin, kh, kw = w.shape
+        ws = self._const(op.weight_scale, "w_scale").astype(np.float32).reshape(-1)
+        ws = np.broadcast_to(ws, (oc,)).astype(np.float32)
+        # per-channel requant scale exactly as the reference's float expression: (xs * ws) / ys
+        scale = (np.float32(xs) * ws).astype(np.float32) / np.float32(ys)
+        scale = scale.astype(np.float32)
+        bias = (self._const(op.bias, "bias").astype(np.int32) if op.bias is not None
+                else np.zeros(oc, np.int32))
+        epi = np.concatenate([scale.view(np.uint8), bias.view(np.uint8)])
+        # weight image: [tap][chunk of 16 in-channels][oc][16 bytes]
+        img = w.transpose(2, 3, 1, 0).reshape(kh * kw, cin // 16, 16, oc).transpose(0, 1, 3, 2)
+        t_w = self._b.weight(np.ascontiguousarray(img), "i8", op.weights + ":tc")
+        t_e = self._b.weight(epi, "u8", op.weights + ":epi")
+        xin = self._padded_of(op.input0)
+        n, _, h, wd = self._shape(op.input0)
+        oh, ow = op.out_spatial
+        ip = {K.QC_N: n, K.QC_CIN: cin, K.QC_OC: oc, K.QC_KH: kh, K.QC_KW: kw, K.QC_HP: xin.hp, K.QC_WP: xin.wp,
+              K.QC_OH: oh, K.QC_OW: ow, K.QC_A_SIGNED: cfg["a_signed"], K.QC_Y_ZERO: zy,
+              K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8")}
+        fp = {}
+        t_r = -1
+        out_name = op.output
+        out_dtype = _suffix(op.dtype)
+        label = f"{op.output}"
+        if i in self._fused_add:
+            add = self._ops[self._fused_add[i]]
+            conv_side0 = add.input0 == op.output
+            resid = add.input1 if conv_side0 else add.input0
+            c_s = add.input0_scale if conv_side0 else add.input1_scale
+            c_z = add.input0_zero_point if conv_side0 else add.input1_zero_point
+            r_s = add.input1_scale if conv_side0 else add.input0_scale
+            r_z = add.input1_zero_point if conv_side0 else add.input0_zero_point
+            rp = self._padded_of(resid)
+            t_r = rp.tid
+            ip.update({K.QC_HAS_ADD: 1, K.QC_C_ZERO: int(self._scalar(c_z, "add zero")),
+                       K.QC_R_ZERO: int(self._scalar(r_z, "add zero")), K.QC_R_XOR: rp.xor,
+                       K.QC_R_SIGNED: int(self._dtype(resid) == "i8"), K.QC_R_HP: rp.hp, K.QC_R_WP: rp.wp,
+                       K.QC_R_PT: rp.pt, K.QC_R_PL: rp.pl,
+                       K.QC_ADD_ZERO: int(self._scalar(add.output_zero_point, "add zero")),
+                       K.QC_ADD_SIGNED: int(_suffix(add.dtype) == "i8")})
+            fp = {K.QCF_C_SCALE: float(np.float32(self._scalar(c_s, "add scale"))),
+                  K.QCF_R_SCALE: float(np.float32(self._scalar(r_s, "add scale"))),
+                  K.QCF_ADD_SCALE: float(np.float32(self._scalar(add.output_scale, "add scale")))}
+            out_name = add.output
+            out_dtype = _suffix(add.dtype)
+            label += f" + {add.output} (fused QLinearAdd)"
+        padded_out = out_name in self._need_pad and out_name not in self._need_rowmajor
+        if padded_out:
+            yp = self._new_padded(out_name)
+            ip.update({K.QC_Y_LAYOUT: 0, K.QC_Y_XOR: yp.xor, K.QC_Y_HP: yp.hp, K.QC_Y_WP: yp.wp,
+                       K.QC_Y_PT: yp.pt, K.QC_Y_PL: yp.pl})
+            t_y = yp.tid
+        else:
+            t_y = self._dest(out_name, out_dtype, (n, oc, oh, ow))
+            ip.update({K.QC_Y_LAYOUT: 1})
+        self._b.op(K.K_QCONV_TC, [xin.tid, t_w, t_e, t_r, t_y], ip, fp, label=label + " (tcgen05 i8)")
+        if padded_out is False and out_name in self._need_pad:
+            self._padded_of(out_name)  # consumers also need the NHWC copy
+
+    # ------------------------------------------------------------------ QLinearAdd (standalone)
+    def _emit_QLinearAddOp(self, i, op):
+        if tuple(op.input0_shape) != tuple(op.input1_shape):
+            raise UnsupportedOpError("QLinearAdd: broadcasting operands have no B200 kernel")
+        a, b_ = self._src(op.input0), self._src(op.input1)
+        y = self._dest(op.output, _suffix(op.dtype), op.output_shape)
+        count = int(np.prod(op.output_shape))
+        batched = self._batch > 0 and len(op.output_shape) > 0 and op.output_shape[0] == self._batch
+        self._b.op(K.K_QLINEAR_ADD, [a, b_, y], {
+            K.QA_COUNT: count, K.QA_A_SIGNED: int(_suffix(op.input0_dtype) == "i8"),
+            K.QA_B_SIGNED: int(_suffix(op.input1_dtype) == "i8"), K.QA_Y_SIGNED: int(_suffix(op.dtype) == "i8"),
+            K.QA_A_ZERO: int(self._scalar(op.input0_zero_point, "a_zero")),
+            K.QA_B_ZERO: int(self._scalar(op.input1_zero_point, "b_zero")),
+            K.QA_Y_ZERO: int(self._scalar(op.output_zero_point, "y_zero")),
+            K.QA_BATCH: self._batch if batched else 0},
+            {K.QAF_A_SCALE: float(np.float32(self._scalar(op.input0_scale, "a_scale"))),
+             K.QAF_B_SCALE: float(np.float32(self._scalar(op.input1_scale, "b_scale"))),
+             K.QAF_Y_SCALE: float(np.float32(self._scalar(op.output_scale, "y_scale")))},
+            label=op.output)

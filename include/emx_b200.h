@@ -1,0 +1,119 @@
+/*
+ * emx_b200.h -- C ABI of the B200 execution backend for emx-onnx-cgen's
+ * lowered-operator hot path (libemx_b200.so).
+ *
+ * The reference compiler ends its pipeline in a generated C translation unit
+ * whose runtime ABI is
+ *
+ *     _Bool <model>_load(const char *weights_path);
+ *     void  <model>(const T in0[restrict ...], ..., T out0[restrict ...], ...);
+ *
+ * (reference: docs/output-format.md:132-193, emitted by
+ * src/emx_onnx_cgen/codegen/c_emitter.py:4272-4317 (loader) and :2297
+ * (model wrapper)).  This library replaces that runtime: a launch plan
+ * produced from the same LoweredModel by emx_onnx_cgen_b200.plan
+ * (B200PlanEmitter) is loaded once per device, weights go to HBM once, and
+ * each run executes the plan's kernels on a CUDA stream.
+ *
+ * Conventions
+ *   - Every entry point returns an emx_status (0 = EMX_OK); the message of the
+ *     last failure on the calling thread is emx_b200_last_error().
+ *   - Caller owns input/output buffers (row-major, the ONNX shapes recorded
+ *     in the plan).  The library owns its device arena and the weights.
+ *   - One plan handle serves one device and is used by one host thread at a
+ *     time, the same single-threaded contract as the generated C
+ *     (README.md:23 of the reference); multi-GPU = one handle per device.
+ *   - No allocation happens after emx_b200_plan_load: the arena holding every
+ *     intermediate tensor is sized by the plan.
+ */
+#ifndef EMX_B200_H
+#define EMX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct emx_plan emx_plan_t;
+
+typedef enum emx_status {
+    EMX_OK = 0,
+    EMX_ERR_INVALID_ARGUMENT = 1, /* null pointer, batch range, bad device id   */
+    EMX_ERR_PLAN_FORMAT = 2,      /* corrupt / truncated / wrong-version plan    */
+    EMX_ERR_WEIGHTS = 3,          /* weights file missing, short read, size      */
+    EMX_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed           */
+    EMX_ERR_UNSUPPORTED = 5,      /* kernel id / shape the library cannot run    */
+    EMX_ERR_DEVICE_TIMEOUT = 6,   /* a bounded device-side wait gave up          */
+    EMX_ERR_OUT_OF_MEMORY = 7     /* arena or weight allocation failed           */
+} emx_status;
+
+/* Library version, "major.minor.patch". */
+const char *emx_b200_version(void);
+
+/* Message of the last failed call on this thread ("" if none).  Replaces the
+ * generated C's silent early return on allocation failure
+ * (c_emitter.py:2785-2788) and its `_Bool` loader result. */
+const char *emx_b200_last_error(void);
+
+/* Parse a plan blob, allocate the device arena on `device`, upload weights
+ * read from `weights_path` (raw little-endian blob written next to the plan).
+ * Replaces `_Bool <model>_load(const char *path)` (c_emitter.py:4272-4317). */
+int emx_b200_plan_load(const void *plan, size_t plan_len, const char *weights_path,
+                       int device, emx_plan_t **out);
+
+/* Same as emx_b200_plan_load with the weight blob already in host memory. */
+int emx_b200_plan_load_mem(const void *plan, size_t plan_len, const void *weights,
+                           size_t weights_len, int device, emx_plan_t **out);
+
+/* Run the plan.  inputs[i]/outputs[i] follow the graph's input/output order
+ * (the parameter order of the generated `<model>(...)`, c_emitter.py:2297)
+ * and may be host or device pointers (detected per pointer).  Host buffers
+ * are staged through the arena with cudaMemcpyAsync on `stream`.
+ * [batch_begin, batch_begin + batch_count) selects rows along axis 0 of every
+ * batched input/output (batch_count = -1: the plan's full batch); the
+ * pointers address the full tensors.  `stream` is a cudaStream_t (NULL: the
+ * plan's own stream).  Returns after enqueueing device work; host outputs
+ * are complete when emx_b200_sync returns. */
+int emx_b200_run(emx_plan_t *plan, const void *const *inputs, void *const *outputs,
+                 int64_t batch_begin, int64_t batch_count, void *stream);
+
+/* Wait for the plan's last run; reports device-side timeouts
+ * (EMX_ERR_DEVICE_TIMEOUT) and asynchronous CUDA errors. */
+int emx_b200_sync(emx_plan_t *plan);
+
+/* Release device memory and the handle (NULL is accepted). */
+void emx_b200_plan_free(emx_plan_t *plan);
+
+/* Introspection (for drivers and tests). */
+typedef struct emx_plan_info {
+    int32_t device;
+    int32_t n_inputs;
+    int32_t n_outputs;
+    int32_t n_ops;
+    int64_t batch;             /* full batch along axis 0 (0 if not batched) */
+    int64_t arena_bytes;
+    int64_t weight_bytes;
+    int64_t launches_per_run;  /* kernels this library launches per full run */
+} emx_plan_info_t;
+
+int emx_b200_plan_info(const emx_plan_t *plan, emx_plan_info_t *info);
+
+/* Number of this library's kernel launches since load (all runs). */
+int64_t emx_b200_launch_count(const emx_plan_t *plan);
+
+/* Per-op device timing: when enabled, every op's launches are bracketed by
+ * CUDA events on the run stream and emx_b200_sync accumulates the elapsed
+ * time per op.  Off by default (no events are recorded). */
+int emx_b200_set_profiling(emx_plan_t *plan, int enable);
+
+/* Accumulated milliseconds per op (n_ops entries) and the number of runs they
+ * cover, since profiling was last enabled. */
+int emx_b200_op_times(const emx_plan_t *plan, double *ms, int32_t n_ops, int64_t *runs);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMX_B200_H */

@@ -1,0 +1,64 @@
+"""Host-side plan emission (no GPU): plan format, kernel-id mirror, boundary
+parity with the reference's own LoweredModel, unsupported-op behaviour."""
+import struct
+
+import numpy as np
+import pytest
+
+from emx_onnx_cgen_b200 import kernel_ids as K, lowering, workloads as W
+from emx_onnx_cgen_b200.plan import B200PlanEmitter, _HDR, PLAN_MAGIC
+from emx_onnx_cgen_b200.spec import GraphSpec, NodeSpec, TensorSpec
+from oracle import refc
+
+SMALL = {
+    "qconv": lambda: W.qconv_stack_int8(batch=2, height=12, width=12),
+    "qconv_c16": lambda: W.qconv_stack_int8(batch=1, channels=16, height=5, width=5, n_convs=3),
+}
+
+
+def test_kernel_ids_parsed_from_header():
+    assert K.K_QCONV_TC == 2 and K.K_PAD_NHWC == 1
+    assert K.QC_ADD_SIGNED > K.QC_N
+    assert K.NAMES[K.K_QCONV_TC] == "qconv_tc"
+
+
+@pytest.mark.parametrize("key", sorted(SMALL))
+def test_plan_matches_reference_lowering(key):
+    if not refc.reference_available():
+        pytest.skip("reference source tree not present")
+    wl = SMALL[key]()
+    mine = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    _, ref_lowered = refc.lower(wl.graph)
+    theirs = B200PlanEmitter().emit_plan(ref_lowered)
+    assert mine.plan_bytes == theirs.plan_bytes
+    assert mine.weight_bytes == theirs.weight_bytes
+
+
+def test_qconv_stack_plan_shape():
+    plan = B200PlanEmitter().emit_plan(lowering.lower(W.qconv_stack_int8().graph))
+    kinds = [K.NAMES[o.kernel] for o in plan.ops]
+    assert kinds == ["pad_nhwc", "qconv_tc", "qconv_tc", "qconv_tc", "qconv_tc"]
+    hdr = _HDR.unpack_from(plan.plan_bytes)
+    assert hdr[0] == PLAN_MAGIC and hdr[6] == 32
+    assert len(plan.plan_bytes) == 56 + 96 * len(plan.tensors) + 2 * 8 + 440 * len(plan.ops)
+
+
+def test_unsupported_op_raises():
+    g = GraphSpec("bad", [TensorSpec("X", "f32", (2, 2))], [TensorSpec("Y", "f32", (2, 2))],
+                  [NodeSpec("Cos", "c", ("X",), ("Y",))], {})
+    with pytest.raises(lowering.UnsupportedOpError):
+        B200PlanEmitter().emit_plan(lowering.lower(g))
+
+
+def test_weight_image_layout():
+    """Tensor-core weight image: [tap][16-channel chunk][oc][16 bytes]."""
+    wl = W.qconv_stack_int8(batch=1, channels=32, height=4, width=4, n_convs=1)
+    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    conv = next(o for o in plan.ops if o.kernel == K.K_QCONV_TC)
+    t = plan.tensors[conv.tensors[1]]
+    img = np.frombuffer(plan.weight_bytes[t.offset:t.offset + t.nbytes], np.int8).reshape(9, 2, 32, 16)
+    w = wl.graph.initializers["w0"]
+    for tap in (0, 4, 8):
+        kh, kw = divmod(tap, 3)
+        for chunk in range(2):
+            assert np.array_equal(img[tap, chunk], w[:, chunk * 16:(chunk + 1) * 16, kh, kw])
