@@ -177,7 +177,7 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
         times.append(step())
         if steps is not None and len(times) >= steps:
             break
-        if steps is None and time.perf_counter() - t_start >= seconds:
+        if seconds and time.perf_counter() - t_start >= seconds:
             break
     return times, threads * dom["ref_rows"], threads
 
@@ -188,7 +188,10 @@ def reference_arm(args) -> None:
     if rank != 0:
         return
     wl, dom = workload_spec(args.workload)
-    times, rows, threads = cpu_reference_sample(dom, 0, steps=args.steps, warmup=args.warmup)
+    # one step = one row-slice per host thread; the run stops after K steps or
+    # ~150 s of CPU time, whichever comes first (the line reports the steps run)
+    times, rows, threads = cpu_reference_sample(dom, 150.0, steps=args.steps, warmup=min(args.warmup, 1))
+    args.steps = len(times)
     sec = sum(times) / len(times)
     value = rows / dom["full_rows"] / sec
     line = {
@@ -229,8 +232,12 @@ def ours_arm(args) -> None:
     wl, dom = workload_spec(args.workload)
     plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
     sess = Session(plan, device=local)
-    stream = torch.cuda.current_stream()
+    # a real (non-legacy) stream: its handle is what the library launches on and
+    # what the timing events are recorded on
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
+    assert sptr != 0
 
     x_np = wl.make_inputs(rank)
     host_in = [torch.from_numpy(np.ascontiguousarray(x_np[n])).pin_memory() for n in plan.input_names]
@@ -270,15 +277,23 @@ def ours_arm(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        sess.run_ptrs(in_d, out_d, stream=sptr)
-        sess.run_ptrs(in_h, out_h, stream=sptr)
-    sess.sync()
-    launches_before = sess.launch_count()
-    barrier()
     with ClockSampler(local) as clk:
+        # warm-up: at least W steps and at least ~1 s of back-to-back work so the
+        # SM clock has ramped before the timed region
+        t0 = time.perf_counter()
+        done = 0
+        while done < args.warmup or time.perf_counter() - t0 < 1.0:
+            flush.fill_(3)
+            sess.run_ptrs(in_d, out_d, stream=sptr)
+            sess.run_ptrs(in_h, out_h, stream=sptr)
+            done += 1
+            if done % 16 == 0:
+                sess.sync()
+        sess.sync()
+        launches_before = sess.launch_count()
+        barrier()
         ms = timed(in_d, out_d, args.steps)
-    launches = sess.launch_count() - launches_before
+        launches = sess.launch_count() - launches_before
     barrier()
     ms_e2e = timed(in_h, out_h, args.steps)
     barrier()
@@ -360,7 +375,7 @@ def _ncu_traffic(kernel: str, workload: str):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qconv_stack_int8")

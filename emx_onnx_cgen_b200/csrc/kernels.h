@@ -10,7 +10,7 @@
 namespace emx {
 
 enum KernelId : uint32_t {
-  K_PAD_NHWC = 1,       // NCHW 8-bit -> zero-bordered NHWC (optionally XOR 0x80)
+  K_PAD_NHWC = 1,       // NCHW 8-bit -> zero-bordered chunk-planar NHWC (optionally XOR 0x80)
   K_QCONV_TC = 2,       // QLinearConv implicit GEMM on tcgen05 kind::i8 (+ fused QLinearAdd)
   K_QCONV_GENERIC = 3,  // QLinearConv, any stride/pad/dilation/group, CUDA cores
   K_QLINEAR_ADD = 4,    // com.microsoft QLinearAdd, same-shape operands
@@ -24,16 +24,20 @@ enum KernelId : uint32_t {
   K_NBITS_DEQUANT = 12, // int4 blocks -> fp16 weight matrix (prologue of K_NBITS_GEMM)
 };
 
-// ---- K_PAD_NHWC: t[0]=x (NCHW), t[1]=y (padded NHWC)
-enum { PAD_N, PAD_C, PAD_H, PAD_W, PAD_TOP, PAD_LEFT, PAD_HP, PAD_WP, PAD_XOR };
+// Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
+// row = n*Hp*Wp + hp*Wp + wp, `*_ROWS` rows allocated per plane (>= N*Hp*Wp
+// plus a tail the conv windows may read).
 
-// ---- K_QCONV_TC: t[0]=x (padded NHWC), t[1]=w image, t[2]=epilogue table
-//      (float scale[OC], int32 bias[OC]), t[3]=residual (padded NHWC) or -1, t[4]=y
+// ---- K_PAD_NHWC: t[0]=x (NCHW), t[1]=y (planar)
+enum { PAD_N, PAD_C, PAD_H, PAD_W, PAD_TOP, PAD_LEFT, PAD_HP, PAD_WP, PAD_XOR, PAD_ROWS };
+
+// ---- K_QCONV_TC: t[0]=x (planar), t[1]=w image, t[2]=epilogue table
+//      (float scale[OC], int32 bias[OC]), t[3]=residual (planar) or -1, t[4]=y
 enum {
   QC_N, QC_CIN, QC_OC, QC_KH, QC_KW, QC_HP, QC_WP, QC_OH, QC_OW, QC_A_SIGNED, QC_Y_ZERO,
-  QC_Y_LAYOUT /*0 padded NHWC, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,
+  QC_Y_LAYOUT /*0 planar, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,
   QC_HAS_ADD, QC_C_ZERO /*conv-side zero in the add*/, QC_R_ZERO, QC_R_XOR, QC_R_SIGNED, QC_R_HP, QC_R_WP,
-  QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED
+  QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED, QC_X_ROWS, QC_Y_ROWS, QC_R_ROWS
 };
 enum { QCF_C_SCALE, QCF_R_SCALE, QCF_ADD_SCALE };
 
@@ -49,6 +53,14 @@ enum { QGF_X_SCALE, QGF_Y_SCALE };
 enum { QA_COUNT, QA_A_SIGNED, QA_B_SIGNED, QA_Y_SIGNED, QA_A_ZERO, QA_B_ZERO, QA_Y_ZERO, QA_BATCH };
 enum { QAF_A_SCALE, QAF_B_SCALE, QAF_Y_SCALE };
 
+// ---- K_GEMM_F32: t[0]=A, t[1]=B, t[2]=bias|-1, t[3]=Y
+enum { GM_M, GM_N, GM_K, GM_TRANS_A, GM_TRANS_B, GM_BIAS_MODE, GM_RELU };
+enum { GMF_ALPHA, GMF_BETA };
+
+// ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), last=y
+enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
+enum { EWF_ALPHA };
+
 struct LaunchCtx {
   cudaStream_t stream;
   int* d_error;     // device error word
@@ -56,9 +68,17 @@ struct LaunchCtx {
   int num_sms;
 };
 
-// Batch an op processes this run: the run's slice when the plan is batched,
-// else the op's compiled extent.
-inline int64_t eff_batch(const LaunchCtx& c, int64_t compiled) { return c.batch > 0 ? c.batch : compiled; }
+// Last integer slot of every op: 1 when the op's leading (batch) extent
+// follows the run's batch slice.  The plan emitter sets it only on ops whose
+// leading extent is the plan batch, and marks a plan sliceable only if every
+// op that touches activations has it.
+constexpr int IP_BATCHED = EMX_OP_MAX_IPARAMS - 1;
+
+// Batch an op processes this run: the run's slice for batched ops of a
+// batched plan, else the op's compiled extent.
+inline int64_t eff_batch(const LaunchCtx& c, const PlanOp& op, int64_t compiled) {
+  return (c.batch > 0 && op.ip[IP_BATCHED]) ? c.batch : compiled;
+}
 
 // Opaque per-op state prepared once at plan load (tensor maps, chosen variant).
 struct alignas(64) OpState {
@@ -75,5 +95,7 @@ int launch_qconv_tc(const PlanOp&, void* const*, const OpState*, const LaunchCtx
 int launch_pad_nhwc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qconv_generic(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qlinear_add(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_gemm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

@@ -1,4 +1,5 @@
-// QLinearConv / QLinearAdd kernels (int8 ResNet-style stacks).
+// QLinearConv (+ fused QLinearAdd) on tcgen05 kind::i8, for the int8
+// ResNet-style stacks: stride 1, dilation 1, group 1, C in {32,64,128}.
 //
 // Reference arithmetic (src/emx_onnx_cgen/templates/qlinear_conv_op.c.j2:1-45,
 // qlinear_add_op.c.j2:1-21, ir/ops/nn.py:4875-4951):
@@ -6,90 +7,90 @@
 //   scale = ((float)xs * (float)ws[oc]) / (float)ys
 //   y     = clamp((float)(nearbyint((double)((float)acc * scale)) + zy))
 //   add   = clamp(nearbyintf(((float)(a-za)*sa + (float)(b-zb)*sb) / ys + zy))
-// Integer accumulation is exact in any order, so the tensor-core kernel is
-// bit-exact as long as the epilogue repeats the float steps one rounding at a
-// time (__fmul_rn/__fadd_rn/__fdiv_rn: no FMA contraction, IEEE division).
+// Integer accumulation is exact in any order, so the tensor cores reproduce
+// acc exactly; the epilogue repeats the float steps one rounding at a time
+// (qmath.cuh).
 //
-// Tensor-core path (K_QCONV_TC), stride 1 / dilation 1 / group 1 convolutions:
-//   * activations live in a zero-bordered NHWC layout [N][Hp][Wp][C] (Hp, Wp
-//     include the conv's pads).  Output pixel (oh, ow) of image n is the
-//     "pitched" row q = n*Hp*Wp + oh*Wp + ow; tap (kh, kw) then reads padded
-//     row q + kh*Wp + kw.  A tile of 128 consecutive pitched rows therefore
-//     needs, per kh, one contiguous window of 128+KW-1 input rows, and the KW
-//     taps of that kh are the same window shifted by kw rows.  Rows that fall
-//     on the pad columns / pad rows produce discarded outputs.
-//   * the window is fetched by TMA as C/16 planes of [rows][16 bytes] (one 2-D
-//     tile load per 16-byte channel chunk), which is exactly the SWIZZLE_NONE
-//     K-major canonical layout with SBO = 128 (8 rows x 16 B) and LBO = plane
-//     pitch; the kw shift is a 16*kw byte offset of the descriptor start.
-//   * zero padding must mean "real zero": when the activation zero point is
-//     128 on uint8 storage the producer stores x ^ 0x80 (= x - 128 as int8)
-//     and the MMA runs s8 x s8; when it is 0 the MMA runs u8 x s8 on the raw
-//     bytes.  Other zero points use the generic kernel.
+// Activation layout between these kernels: "chunk-planar, zero-bordered":
+// [C/16 planes][rows][16 bytes], row = n*Hp*Wp + hp*Wp + wp over the image
+// padded by the conv's pads (Hp = H+pads, Wp = W+pads), plus a tail of spare
+// rows per plane.  Border rows are zero and never written.
+//   * Output pixel (oh, ow) of image n is the "pitched" row q = n*Hp*Wp +
+//     oh*Wp + ow; tap (kh, kw) reads input row q + kh*Wp + kw.  A tile of 128
+//     consecutive pitched rows needs, per kh, the window of 128+KW-1
+//     consecutive rows starting at q0 + kh*Wp; its KW taps are that window
+//     shifted by kw rows.  Pitched rows on pad columns / pad rows give outputs
+//     that are discarded.
+//   * In each 16-byte plane the window is contiguous, so one bulk copy per
+//     plane (cp.async.bulk, no tensor map, no multicast) lands it in shared
+//     memory as [plane][rows][16 B]: exactly the SWIZZLE_NONE K-major
+//     canonical layout with SBO = 128 (8 rows x 16 B) and LBO = plane pitch.
+//     The kw shift is a 16*kw-byte offset of the descriptor start address.
+//   * zero padding must mean "real zero": for zero point 128 on uint8 storage
+//     the producer stores x ^ 0x80 (= x - 128 as int8) and the MMA runs
+//     s8 x s8; for zero point 0 the MMA runs on the raw bytes (u8 or s8).
 //   * weights (all taps, [tap][C/16][OC][16 B]) stay in shared memory for the
-//     CTA's lifetime; the int32 accumulator (128 x OC) is double-buffered in
-//     TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
-//   * warp roles: warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM owner,
-//     warps 4-7 epilogue (TMEM lane quarter = warp % 4).
-#include <cuda_fp16.h>
-
+//     CTA's lifetime; the int32 accumulator tile (128 x OC) is double-buffered
+//     in TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   * warps: 0 producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-11 epilogue
+//     (two warps per TMEM lane quarter, each taking half of the OC columns).
 #include "host_util.h"
 #include "kernels.h"
+#include "qmath.cuh"
 #include "tc100.cuh"
 
 namespace emx {
 
-// ------------------------------------------------------------------ epilogue math
-__device__ __forceinline__ int requant(int32_t acc, float scale, float zero, bool is_signed) {
-  float v = __fmul_rn(__int2float_rn(acc), scale);
-  float r = __fadd_rn(rintf(v), zero);
-  r = fmaxf(r, is_signed ? -128.0f : 0.0f);
-  r = fminf(r, is_signed ? 127.0f : 255.0f);
-  return (int)r;
-}
-
-__device__ __forceinline__ int qadd(int a, int za, float sa, int b, int zb, float sb, float ys, float yz,
-                                    bool is_signed) {
-  float ar = __fmul_rn(__int2float_rn(a - za), sa);
-  float br = __fmul_rn(__int2float_rn(b - zb), sb);
-  float s = __fadd_rn(__fdiv_rn(__fadd_rn(ar, br), ys), yz);
-  float r = rintf(s);
-  r = fmaxf(r, is_signed ? -128.0f : 0.0f);
-  r = fminf(r, is_signed ? 127.0f : 255.0f);
-  return (int)r;
-}
-
-__device__ __forceinline__ int load_8bit(uint32_t byte, bool is_signed) {
-  return is_signed ? (int)(int8_t)(uint8_t)byte : (int)(uint8_t)byte;
-}
-
-// ------------------------------------------------------------------ tcgen05 conv
 struct QConvTcParams {
+  const uint8_t* x;
   const uint8_t* w_img;
   const float* scale;
   const int32_t* bias;
   const uint8_t* resid;
   uint8_t* y;
   int* err;
+  uint64_t x_pitch, y_pitch, r_pitch;  // bytes between 16-channel planes
+  int64_t x_rows;                      // rows allocated per input plane
   int batch, kh, kw, hp, wp, oh, ow;
   int rows_box, stages, n_tiles;
   uint32_t idesc, b_bytes, stage_bytes, plane_bytes;
-  float y_zero;
-  int y_layout, y_xor, y_hp, y_wp, y_pt, y_pl, y_signed;
-  int has_add;
-  float c_scale, r_scale, add_scale, add_zero;
-  int c_zero, r_zero, r_xor, r_signed, r_hp, r_wp, r_pt, r_pl, add_signed;
+  float y_lo, y_hi, y_m_minus_zero;
+  int y_layout, y_xor, y_hp, y_wp, y_pt, y_pl;
+  int has_add, fast_div;
+  float c_scale, r_scale, add_scale, add_inv_scale, add_zero, c_zero, r_zero, add_lo, add_hi;
+  int r_xor, r_signed, r_hp, r_wp, r_pt, r_pl;
 };
 
-constexpr int QC_THREADS = 256;
+constexpr int QC_EPI_WARPS = 8;
+constexpr int QC_THREADS = 128 + 32 * QC_EPI_WARPS;
 constexpr int QC_TILE_M = 128;
 
+template <int OC, int HALF>
+__device__ __forceinline__ void qc_epilogue_store(const QConvTcParams& p, const uint32_t (&out)[HALF / 4], int col0,
+                                                  int n, int oh, int ow, int64_t q) {
+  if (p.y_layout == 0) {
+    const int64_t ypix = ((int64_t)n * p.y_hp + oh + p.y_pt) * p.y_wp + ow + p.y_pl;
+#pragma unroll
+    for (int c = 0; c < HALF / 16; ++c) {
+      uint4* dst = reinterpret_cast<uint4*>(p.y + (uint64_t)(col0 / 16 + c) * p.y_pitch + (uint64_t)ypix * 16);
+      *dst = make_uint4(out[4 * c + 0], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+    }
+  } else {
+    const int64_t plane = (int64_t)p.oh * p.ow;
+    uint8_t* yb = p.y + ((int64_t)n * OC + col0) * plane + (int64_t)oh * p.ow + ow;
+#pragma unroll
+    for (int c = 0; c < HALF; ++c) yb[(int64_t)c * plane] = (uint8_t)(out[c >> 2] >> (8 * (c & 3)));
+  }
+  (void)q;
+}
+
 template <int CIN, int OC>
-__global__ void __launch_bounds__(QC_THREADS, 1)
-    qconv_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const QConvTcParams p) {
-  constexpr int CHUNKS = CIN / 16;  // 16-byte channel chunks per pixel
+__global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcParams p) {
+  constexpr int CHUNKS = CIN / 16;  // 16-byte channel planes per pixel
   constexpr int KSTEPS = CIN / 32;  // kind::i8 MMAs (K = 32) per tap
+  constexpr int HALF = OC / 2;      // columns per epilogue warp
   constexpr uint32_t TMEM_COLS = (2 * OC < 32) ? 32 : 2 * OC;
+  static_assert(HALF % 16 == 0, "OC must be a multiple of 32");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_b = smem;
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf[a], 1);
-      mbar_init(&acce[a], 128);
+      mbar_init(&acce[a], 32 * QC_EPI_WARPS);
     }
     mbar_init(bbar, 1);
     mbar_init(drain, 1);
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
     tmem_relinquish();
   }
   if (warp >= 4) {
-    for (int i = threadIdx.x - 128; i < OC; i += 128) {
+    for (int i = threadIdx.x - 128; i < OC; i += 32 * QC_EPI_WARPS) {
       s_scale[i] = p.scale[i];
       s_bias[i] = p.bias[i];
     }
@@ -147,20 +148,27 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      uint32_t issued = 0;  // bit s: stage s has a window in flight or landed, parity in `parity_of`
-      uint32_t parity_of = 0;
+      uint32_t issued = 0, parity_of = 0;  // per stage: window issued, and in which phase
+      const uint32_t win_bytes = (uint32_t)p.rows_box * 16u;
       for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-        const int q0 = tile * QC_TILE_M;
+        const int64_t q0 = (int64_t)tile * QC_TILE_M;
         for (int kh = 0; kh < p.kh; ++kh) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
+          const int64_t row0 = q0 + (int64_t)kh * p.wp;
           uint8_t* dst = s_a + (size_t)stage * p.stage_bytes;
-          mbar_arrive_expect_tx(&full[stage], p.stage_bytes);
+          if (row0 + p.rows_box > p.x_rows) {  // plan guarantees this never happens; do not read past the plane
+            record_error(p.err, DEV_BAD_CONFIG);
+            mbar_arrive(&full[stage]);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], p.stage_bytes);
 #pragma unroll
-          for (int c = 0; c < CHUNKS; ++c)
-            tma_load_2d(dst + (size_t)c * p.plane_bytes, &tmap_x, &full[stage], c * 16, q0 + kh * p.wp);
+            for (int c = 0; c < CHUNKS; ++c)
+              bulk_load(dst + (size_t)c * p.plane_bytes, p.x + (uint64_t)c * p.x_pitch + (uint64_t)row0 * 16u,
+                        win_bytes, &full[stage]);
+          }
           issued |= 1u << stage;
           parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
@@ -169,8 +177,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
           }
         }
       }
-      // error path: let every window this thread issued land before the CTA exits
-      if (!ok) {
+      if (!ok) {  // error path: let every window this thread issued land before the CTA exits
         for (int s2 = 0; s2 < p.stages; ++s2)
           if (issued & (1u << s2)) (void)mbar_wait(&full[s2], (parity_of >> s2) & 1u, nullptr, 0);
       }
@@ -230,8 +237,9 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
   } else if (warp >= 4) {
     // ---------------- epilogue: TMEM -> registers -> requant (+ QLinearAdd) -> global
     const int quarter = warp & 3;
+    const int col0 = ((warp - 4) >> 2) * HALF;
     const int row = quarter * 32 + lane;
-    const int hpwp = p.hp * p.wp;
+    const int64_t hpwp = (int64_t)p.hp * p.wp;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++it) {
       __syncwarp();
@@ -239,60 +247,67 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
       bool ok = mbar_wait(&accf[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      uint32_t v[OC];
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * OC);
+      uint32_t v[HALF];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * OC + col0);
 #pragma unroll
-      for (int c = 0; c < OC / 16; ++c) tmem_ld16(taddr + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[c * 16]));
+      for (int c = 0; c < HALF / 16; ++c)
+        tmem_ld16(taddr + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[c * 16]));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&acce[acc]);
 
-      const int q = tile * QC_TILE_M + row;
-      const int n = q / hpwp;
-      const int rem = q - n * hpwp;
+      const int64_t q = (int64_t)tile * QC_TILE_M + row;
+      const int n = (int)(q / hpwp);
+      const int rem = (int)(q - (int64_t)n * hpwp);
       const int oh = rem / p.wp;
       const int ow = rem - oh * p.wp;
       if (n >= p.batch || oh >= p.oh || ow >= p.ow) continue;
 
-      uint32_t rbytes[OC / 4];
-      if (p.has_add) {
-        const size_t rpix = ((size_t)n * p.r_hp + oh + p.r_pt) * p.r_wp + ow + p.r_pl;
-        const uint4* rp = reinterpret_cast<const uint4*>(p.resid + rpix * OC);
+      uint32_t out[HALF / 4];
 #pragma unroll
-        for (int c = 0; c < OC / 16; ++c) {
-          uint4 t = rp[c];
-          rbytes[4 * c + 0] = t.x;
-          rbytes[4 * c + 1] = t.y;
-          rbytes[4 * c + 2] = t.z;
-          rbytes[4 * c + 3] = t.w;
+      for (int j = 0; j < HALF / 4; ++j) out[j] = 0;
+      if (!p.has_add) {
+#pragma unroll
+        for (int c = 0; c < HALF; ++c) {
+          const float r = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero, p.y_lo,
+                                       p.y_hi);
+          out[c >> 2] |= (float_to_byte(r) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
         }
-      }
-      uint32_t out[OC / 4];
-#pragma unroll
-      for (int j = 0; j < OC / 4; ++j) out[j] = 0;
-#pragma unroll
-      for (int oc = 0; oc < OC; ++oc) {
-        const int32_t a = (int32_t)v[oc] + s_bias[oc];
-        int yv = requant(a, s_scale[oc], p.y_zero, p.y_signed);
-        if (p.has_add) {
-          const uint32_t rb = ((rbytes[oc >> 2] >> (8 * (oc & 3))) & 0xFFu) ^ (uint32_t)p.r_xor;
-          yv = qadd(yv, p.c_zero, p.c_scale, load_8bit(rb, p.r_signed), p.r_zero, p.r_scale, p.add_scale,
-                    p.add_zero, p.add_signed);
-        }
-        out[oc >> 2] |= (((uint32_t)yv & 0xFFu) ^ (uint32_t)p.y_xor) << (8 * (oc & 3));
-      }
-      if (p.y_layout == 0) {
-        const size_t ypix = ((size_t)n * p.y_hp + oh + p.y_pt) * p.y_wp + ow + p.y_pl;
-        uint4* yp = reinterpret_cast<uint4*>(p.y + ypix * OC);
-#pragma unroll
-        for (int c = 0; c < OC / 16; ++c)
-          yp[c] = make_uint4(out[4 * c + 0], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
       } else {
-        const size_t plane = (size_t)p.oh * p.ow;
-        uint8_t* yb = p.y + (size_t)n * OC * plane + (size_t)oh * p.ow + ow;
+        const int64_t rpix = ((int64_t)n * p.r_hp + oh + p.r_pt) * p.r_wp + ow + p.r_pl;
+        uint32_t rb[HALF / 4];
 #pragma unroll
-        for (int oc = 0; oc < OC; ++oc) yb[(size_t)oc * plane] = (uint8_t)(out[oc >> 2] >> (8 * (oc & 3)));
+        for (int c = 0; c < HALF / 16; ++c) {
+          const uint4 t =
+              *reinterpret_cast<const uint4*>(p.resid + (uint64_t)(col0 / 16 + c) * p.r_pitch + (uint64_t)rpix * 16);
+          rb[4 * c + 0] = t.x;
+          rb[4 * c + 1] = t.y;
+          rb[4 * c + 2] = t.z;
+          rb[4 * c + 3] = t.w;
+        }
+        if (p.fast_div) {
+#pragma unroll
+          for (int c = 0; c < HALF; ++c) {
+            const float cv = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero,
+                                          p.y_lo, p.y_hi);
+            const int r = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
+            const float a = qadd_fast<true>(cv, p.c_zero, p.c_scale, r, p.r_zero, p.r_scale, p.add_scale,
+                                            p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
+            out[c >> 2] |= (float_to_byte(a) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < HALF; ++c) {
+            const float cv = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero,
+                                          p.y_lo, p.y_hi);
+            const int r = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
+            const float a = qadd_fast<false>(cv, p.c_zero, p.c_scale, r, p.r_zero, p.r_scale, p.add_scale,
+                                             p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
+            out[c >> 2] |= (float_to_byte(a) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
+          }
+        }
       }
+      qc_epilogue_store<OC, HALF>(p, out, col0, n, oh, ow, q);
     }
   }
 
@@ -304,18 +319,34 @@ __global__ void __launch_bounds__(QC_THREADS, 1)
   }
 }
 
+// Exhaustive check, for one fused QLinearAdd, that the refined-reciprocal
+// division gives the same output byte as __fdiv_rn for every (conv value,
+// residual byte) pair.  mismatch[0] counts differing pairs.
+__global__ void qadd_fastdiv_check_kernel(QConvTcParams p, int* mismatch) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 65536) return;
+  const int a8 = i >> 8, r8 = i & 255;
+  const float cv = p.y_lo < 0.0f ? (float)(int8_t)a8 : (float)a8;  // conv output value (already clamped)
+  const int r = load_8bit((uint32_t)r8, p.r_signed);
+  const float f = qadd_fast<true>(cv, p.c_zero, p.c_scale, r, p.r_zero, p.r_scale, p.add_scale, p.add_inv_scale,
+                                  p.add_zero, p.add_lo, p.add_hi);
+  const int e = qadd_exact((int)cv, (int)p.c_zero, p.c_scale, r, (int)p.r_zero, p.r_scale, p.add_scale, p.add_zero,
+                           p.add_lo < 0.0f);
+  if ((int)f != e) atomicAdd(mismatch, 1);
+}
+
 // ------------------------------------------------------------------ host side
 struct QConvTcState {
-  CUtensorMap tmap;  // 128 bytes, 64-aligned
-  int variant;       // index into the instantiation table
+  int variant;
   int stages;
   int rows_box;
+  int fast_div;
   uint32_t stage_bytes, plane_bytes, b_bytes;
   size_t smem_bytes;
 };
 static_assert(sizeof(QConvTcState) <= sizeof(OpState), "state fits");
 
-typedef void (*QcKernel)(const CUtensorMap, const QConvTcParams);
+typedef void (*QcKernel)(const QConvTcParams);
 struct QcVariant {
   int cin, oc;
   QcKernel fn;
@@ -336,6 +367,64 @@ static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_byte
   return s;
 }
 
+static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, const QConvTcState* st,
+                        int64_t batch) {
+  const int oc = (int)op.ip[QC_OC];
+  p.x = (const uint8_t*)ptrs[op.t[0]];
+  p.w_img = (const uint8_t*)ptrs[op.t[1]];
+  p.scale = (const float*)ptrs[op.t[2]];
+  p.bias = (const int32_t*)((const float*)ptrs[op.t[2]] + oc);
+  p.resid = op.t[3] >= 0 ? (const uint8_t*)ptrs[op.t[3]] : nullptr;
+  p.y = (uint8_t*)ptrs[op.t[4]];
+  p.x_rows = op.ip[QC_X_ROWS];
+  p.x_pitch = (uint64_t)op.ip[QC_X_ROWS] * 16u;
+  p.y_pitch = (uint64_t)op.ip[QC_Y_ROWS] * 16u;
+  p.r_pitch = (uint64_t)op.ip[QC_R_ROWS] * 16u;
+  p.batch = (int)batch;
+  p.kh = (int)op.ip[QC_KH];
+  p.kw = (int)op.ip[QC_KW];
+  p.hp = (int)op.ip[QC_HP];
+  p.wp = (int)op.ip[QC_WP];
+  p.oh = (int)op.ip[QC_OH];
+  p.ow = (int)op.ip[QC_OW];
+  p.rows_box = st->rows_box;
+  p.stages = st->stages;
+  const int64_t q_end = (batch - 1) * p.hp * p.wp + (int64_t)(p.oh - 1) * p.wp + p.ow;  // one past last valid
+  p.n_tiles = batch > 0 ? (int)((q_end + QC_TILE_M - 1) / QC_TILE_M) : 0;
+  p.idesc = make_idesc(2u, op.ip[QC_A_SIGNED] ? 1u : 0u, 1u, 128u, (uint32_t)oc);
+  p.b_bytes = st->b_bytes;
+  p.stage_bytes = st->stage_bytes;
+  p.plane_bytes = st->plane_bytes;
+  const bool ys = op.ip[QC_Y_SIGNED] != 0;
+  p.y_lo = ys ? -128.0f : 0.0f;
+  p.y_hi = ys ? 127.0f : 255.0f;
+  p.y_m_minus_zero = kMagic - (float)op.ip[QC_Y_ZERO];
+  p.y_layout = (int)op.ip[QC_Y_LAYOUT];
+  p.y_xor = (int)op.ip[QC_Y_XOR];
+  p.y_hp = (int)op.ip[QC_Y_HP];
+  p.y_wp = (int)op.ip[QC_Y_WP];
+  p.y_pt = (int)op.ip[QC_Y_PT];
+  p.y_pl = (int)op.ip[QC_Y_PL];
+  p.has_add = (int)op.ip[QC_HAS_ADD];
+  p.fast_div = st->fast_div;
+  p.c_scale = (float)op.fp[QCF_C_SCALE];
+  p.r_scale = (float)op.fp[QCF_R_SCALE];
+  p.add_scale = (float)op.fp[QCF_ADD_SCALE];
+  p.add_inv_scale = p.has_add ? 1.0f / p.add_scale : 0.0f;
+  p.add_zero = (float)op.ip[QC_ADD_ZERO];
+  p.c_zero = (float)op.ip[QC_C_ZERO];
+  p.r_zero = (float)op.ip[QC_R_ZERO];
+  const bool as = op.ip[QC_ADD_SIGNED] != 0;
+  p.add_lo = as ? -128.0f : 0.0f;
+  p.add_hi = as ? 127.0f : 255.0f;
+  p.r_xor = (int)op.ip[QC_R_XOR];
+  p.r_signed = (int)op.ip[QC_R_SIGNED];
+  p.r_hp = (int)op.ip[QC_R_HP];
+  p.r_wp = (int)op.ip[QC_R_WP];
+  p.r_pt = (int)op.ip[QC_R_PT];
+  p.r_pl = (int)op.ip[QC_R_PL];
+}
+
 int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int device, char* msg, size_t n) {
   QConvTcState* st = reinterpret_cast<QConvTcState*>(st_);
   const int cin = (int)op.ip[QC_CIN], oc = (int)op.ip[QC_OC];
@@ -345,226 +434,95 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
   if (st->variant < 0) return fail(msg, n, 5, "QLinearConv tensor-core path: no variant for C=%d OC=%d", cin, oc);
   const int kw = (int)op.ip[QC_KW], kh = (int)op.ip[QC_KH];
   st->rows_box = (int)align_up((size_t)(QC_TILE_M + kw - 1), 8);
-  if (st->rows_box > 256) return fail(msg, n, 5, "kernel width %d too large for one TMA box", kw);
   st->plane_bytes = (uint32_t)st->rows_box * 16u;
   st->stage_bytes = st->plane_bytes * (uint32_t)(cin / 16);
   st->b_bytes = (uint32_t)(kh * kw * cin * oc);
+  // every window the kernel can request must stay inside the input planes
+  const int64_t rows_needed =
+      op.ip[QC_N] * op.ip[QC_HP] * op.ip[QC_WP] + (int64_t)(kh - 1) * op.ip[QC_WP] + st->rows_box;
+  if (op.ip[QC_X_ROWS] < rows_needed)
+    return fail(msg, n, 2, "input planes have %lld rows, windows need %lld", (long long)op.ip[QC_X_ROWS],
+                (long long)rows_needed);
   const size_t budget = 200 * 1024;
   int stages = 9;
   while (stages > 2 && qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc) > budget) --stages;
   st->stages = stages;
   st->smem_bytes = qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc);
-  if (st->smem_bytes > 227 * 1024) return fail(msg, n, 5, "QLinearConv tensor-core path needs %zu B smem", st->smem_bytes);
-  const int64_t rows = op.ip[QC_N] * op.ip[QC_HP] * op.ip[QC_WP];
-  int rc = make_tmap_2d(&st->tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ptrs[op.t[0]], (uint64_t)cin, (uint64_t)rows,
-                        (uint64_t)cin, 16, (uint32_t)st->rows_box, CU_TENSOR_MAP_SWIZZLE_NONE, msg, n);
-  if (rc) return rc;
+  if (st->smem_bytes > 227 * 1024)
+    return fail(msg, n, 5, "QLinearConv tensor-core path needs %zu B smem", st->smem_bytes);
   cudaError_t e = cudaFuncSetAttribute(kQcVariants[st->variant].fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)st->smem_bytes);
   if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  st->fast_div = 0;
+  if (op.ip[QC_HAS_ADD]) {
+    QConvTcParams p{};
+    fill_params(p, op, ptrs, st, op.ip[QC_N]);
+    int* d_mis = nullptr;
+    int mis = -1;
+    if (cudaMalloc(&d_mis, sizeof(int)) != cudaSuccess) return fail(msg, n, 7, "check buffer");
+    cudaMemset(d_mis, 0, sizeof(int));
+    qadd_fastdiv_check_kernel<<<256, 256>>>(p, d_mis);
+    e = cudaMemcpy(&mis, d_mis, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d_mis);
+    if (e != cudaSuccess) return fail(msg, n, 4, "fast-division check: %s", cudaGetErrorString(e));
+    st->fast_div = mis == 0 ? 1 : 0;
+  }
   (void)device;
   return 0;
 }
 
 int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, const LaunchCtx& ctx, int* launches) {
   const QConvTcState* st = reinterpret_cast<const QConvTcState*>(st_);
-  const int oc = (int)op.ip[QC_OC];
   QConvTcParams p{};
-  p.w_img = (const uint8_t*)ptrs[op.t[1]];
-  p.scale = (const float*)ptrs[op.t[2]];
-  p.bias = (const int32_t*)((const float*)ptrs[op.t[2]] + oc);
-  p.resid = op.t[3] >= 0 ? (const uint8_t*)ptrs[op.t[3]] : nullptr;
-  p.y = (uint8_t*)ptrs[op.t[4]];
+  fill_params(p, op, ptrs, st, eff_batch(ctx, op, op.ip[QC_N]));
   p.err = ctx.d_error;
-  p.batch = (int)eff_batch(ctx, op.ip[QC_N]);
-  p.kh = (int)op.ip[QC_KH];
-  p.kw = (int)op.ip[QC_KW];
-  p.hp = (int)op.ip[QC_HP];
-  p.wp = (int)op.ip[QC_WP];
-  p.oh = (int)op.ip[QC_OH];
-  p.ow = (int)op.ip[QC_OW];
-  p.rows_box = st->rows_box;
-  p.stages = st->stages;
-  const int64_t q_last = ((int64_t)p.batch - 1) * p.hp * p.wp + (int64_t)(p.oh - 1) * p.wp + p.ow;  // one past last valid
-  p.n_tiles = (int)((q_last + QC_TILE_M - 1) / QC_TILE_M);
-  p.idesc = make_idesc(2u, op.ip[QC_A_SIGNED] ? 1u : 0u, 1u, 128u, (uint32_t)oc);
-  p.b_bytes = st->b_bytes;
-  p.stage_bytes = st->stage_bytes;
-  p.plane_bytes = st->plane_bytes;
-  p.y_zero = (float)op.ip[QC_Y_ZERO];
-  p.y_layout = (int)op.ip[QC_Y_LAYOUT];
-  p.y_xor = (int)op.ip[QC_Y_XOR];
-  p.y_hp = (int)op.ip[QC_Y_HP];
-  p.y_wp = (int)op.ip[QC_Y_WP];
-  p.y_pt = (int)op.ip[QC_Y_PT];
-  p.y_pl = (int)op.ip[QC_Y_PL];
-  p.y_signed = (int)op.ip[QC_Y_SIGNED];
-  p.has_add = (int)op.ip[QC_HAS_ADD];
-  p.c_scale = (float)op.fp[QCF_C_SCALE];
-  p.r_scale = (float)op.fp[QCF_R_SCALE];
-  p.add_scale = (float)op.fp[QCF_ADD_SCALE];
-  p.add_zero = (float)op.ip[QC_ADD_ZERO];
-  p.c_zero = (int)op.ip[QC_C_ZERO];
-  p.r_zero = (int)op.ip[QC_R_ZERO];
-  p.r_xor = (int)op.ip[QC_R_XOR];
-  p.r_signed = (int)op.ip[QC_R_SIGNED];
-  p.r_hp = (int)op.ip[QC_R_HP];
-  p.r_wp = (int)op.ip[QC_R_WP];
-  p.r_pt = (int)op.ip[QC_R_PT];
-  p.r_pl = (int)op.ip[QC_R_PL];
-  p.add_signed = (int)op.ip[QC_ADD_SIGNED];
   if (p.n_tiles <= 0) return 0;
   const int grid = p.n_tiles < ctx.num_sms ? p.n_tiles : ctx.num_sms;
-  kQcVariants[st->variant].fn<<<grid, QC_THREADS, st->smem_bytes, ctx.stream>>>(st->tmap, p);
+  kQcVariants[st->variant].fn<<<grid, QC_THREADS, st->smem_bytes, ctx.stream>>>(p);
   ++*launches;
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : 4;
+  return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 
-// ------------------------------------------------------------------ NCHW -> padded NHWC
-// One block per (image, input row).  Coalesced row reads, coalesced pixel writes.
-__global__ void pad_nhwc_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int c, int h, int w, int pt,
-                                int pl, int hp, int wp, uint32_t xr) {
-  extern __shared__ uint8_t s[];
+// ------------------------------------------------------------------ NCHW -> chunk-planar zero-bordered
+// One block per (image, input row): the row's C x W bytes are staged in shared
+// memory, then written as 16-byte chunks, one per (plane, pixel); consecutive
+// threads write consecutive pixels of one plane (coalesced 16-byte stores).
+__global__ void pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int c, int h, int w,
+                                  int pt, int pl, int hp, int wp, uint64_t plane_pitch, uint32_t xr) {
+  extern __shared__ uint8_t s[];  // [c][w + 4]
   const int row = blockIdx.x, n = blockIdx.y;
+  const int ws = w + 4;
   const uint8_t* src = x + ((size_t)n * c * h + row) * w;
   for (int i = threadIdx.x; i < c * w; i += blockDim.x) {
     const int ch = i / w, col = i - ch * w;
-    s[col * c + ch] = src[(size_t)ch * h * w + col] ^ (uint8_t)xr;
+    s[ch * ws + col] = src[(size_t)ch * h * w + col];
   }
   __syncthreads();
-  uint8_t* dst = y + (((size_t)n * hp + row + pt) * wp + pl) * c;
-  if ((c & 15) == 0) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(s);
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-    for (int i = threadIdx.x; i < c * w / 16; i += blockDim.x) d4[i] = s4[i];
-  } else {
-    for (int i = threadIdx.x; i < c * w; i += blockDim.x) dst[i] = s[i];
+  const int planes = c / 16;
+  const int64_t row0 = ((int64_t)n * hp + row + pt) * wp + pl;
+  const uint32_t x4 = xr * 0x01010101u;
+  for (int i = threadIdx.x; i < planes * w; i += blockDim.x) {
+    const int j = i / w, col = i - j * w;
+    uint32_t wd[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int cb = 16 * j + 4 * q;
+      wd[q] = ((uint32_t)s[(cb + 0) * ws + col] | ((uint32_t)s[(cb + 1) * ws + col] << 8) |
+               ((uint32_t)s[(cb + 2) * ws + col] << 16) | ((uint32_t)s[(cb + 3) * ws + col] << 24)) ^ x4;
+    }
+    *reinterpret_cast<uint4*>(y + (uint64_t)j * plane_pitch + (uint64_t)(row0 + col) * 16) =
+        make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
 }
 
 int launch_pad_nhwc(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int c = (int)op.ip[PAD_C], h = (int)op.ip[PAD_H], w = (int)op.ip[PAD_W];
-  const size_t smem = (size_t)c * w;
-  if (smem > 48 * 1024) return 5;
-  dim3 grid((unsigned)h, (unsigned)eff_batch(ctx, op.ip[PAD_N]));
-  pad_nhwc_kernel<<<grid, 256, smem, ctx.stream>>>((const uint8_t*)ptrs[op.t[0]], (uint8_t*)ptrs[op.t[1]], c, h, w,
-                                                   (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT], (int)op.ip[PAD_HP],
-                                                   (int)op.ip[PAD_WP], (uint32_t)op.ip[PAD_XOR]);
-  ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
-}
-
-// ------------------------------------------------------------------ generic QLinearConv
-// One thread per output element, the reference loop nest verbatim (in-bounds
-// taps only, per-channel weight zero points, groups, strides, dilations).
-struct QConvGenericParams {
-  const uint8_t* x;
-  const uint8_t* w;
-  const float* ws;
-  const int32_t* wz;
-  const int32_t* bias;
-  uint8_t* y;
-  int n, c, h, wd, oc, kh, kw, oh, ow, sh, sw, pt, pl, dh, dw, group;
-  int x_signed, w_signed, y_signed, x_zero, y_zero, ws_pc, wz_pc;
-  float xs, ys;
-};
-
-__global__ void qconv_generic_kernel(const QConvGenericParams p) {
-  const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;
-  const int gic = p.c / p.group, goc = p.oc / p.group;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int ow = (int)(idx % p.ow);
-    const int oh = (int)((idx / p.ow) % p.oh);
-    const int ocg = (int)((idx / ((int64_t)p.ow * p.oh)) % p.oc);
-    const int n = (int)(idx / ((int64_t)p.ow * p.oh * p.oc));
-    const int g = ocg / goc;
-    const float scale = __fdiv_rn(__fmul_rn(p.xs, p.ws[p.ws_pc ? ocg : 0]), p.ys);
-    const int32_t wzero = p.wz ? p.wz[p.wz_pc ? ocg : 0] : 0;
-    int32_t acc = p.bias ? p.bias[ocg] : 0;
-    for (int ic = 0; ic < gic; ++ic) {
-      const int icg = g * gic + ic;
-      for (int a = 0; a < p.kh; ++a) {
-        const int ih = oh * p.sh + a * p.dh - p.pt;
-        if (ih < 0 || ih >= p.h) continue;
-        for (int b = 0; b < p.kw; ++b) {
-          const int iw = ow * p.sw + b * p.dw - p.pl;
-          if (iw < 0 || iw >= p.wd) continue;
-          const uint8_t xb = p.x[(((size_t)n * p.c + icg) * p.h + ih) * p.wd + iw];
-          const uint8_t wb = p.w[(((size_t)ocg * gic + ic) * p.kh + a) * p.kw + b];
-          const int32_t xv = load_8bit(xb, p.x_signed) - p.x_zero;
-          const int32_t wv = load_8bit(wb, p.w_signed) - wzero;
-          acc += xv * wv;
-        }
-      }
-    }
-    p.y[idx] = (uint8_t)requant(acc, scale, (float)p.y_zero, p.y_signed);
-  }
-}
-
-int launch_qconv_generic(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
-  QConvGenericParams p{};
-  p.x = (const uint8_t*)ptrs[op.t[0]];
-  p.w = (const uint8_t*)ptrs[op.t[1]];
-  p.ws = (const float*)ptrs[op.t[2]];
-  p.wz = op.t[3] >= 0 ? (const int32_t*)ptrs[op.t[3]] : nullptr;
-  p.bias = op.t[4] >= 0 ? (const int32_t*)ptrs[op.t[4]] : nullptr;
-  p.y = (uint8_t*)ptrs[op.t[5]];
-  p.n = (int)eff_batch(ctx, op.ip[QG_N]);
-  p.c = (int)op.ip[QG_C];
-  p.h = (int)op.ip[QG_H];
-  p.wd = (int)op.ip[QG_W];
-  p.oc = (int)op.ip[QG_OC];
-  p.kh = (int)op.ip[QG_KH];
-  p.kw = (int)op.ip[QG_KW];
-  p.oh = (int)op.ip[QG_OH];
-  p.ow = (int)op.ip[QG_OW];
-  p.sh = (int)op.ip[QG_SH];
-  p.sw = (int)op.ip[QG_SW];
-  p.pt = (int)op.ip[QG_PT];
-  p.pl = (int)op.ip[QG_PL];
-  p.dh = (int)op.ip[QG_DH];
-  p.dw = (int)op.ip[QG_DW];
-  p.group = (int)op.ip[QG_GROUP];
-  p.x_signed = (int)op.ip[QG_X_SIGNED];
-  p.w_signed = (int)op.ip[QG_W_SIGNED];
-  p.y_signed = (int)op.ip[QG_Y_SIGNED];
-  p.x_zero = (int)op.ip[QG_X_ZERO];
-  p.y_zero = (int)op.ip[QG_Y_ZERO];
-  p.ws_pc = (int)op.ip[QG_WS_PER_CH];
-  p.wz_pc = (int)op.ip[QG_WZ_PER_CH];
-  p.xs = (float)op.fp[QGF_X_SCALE];
-  p.ys = (float)op.fp[QGF_Y_SCALE];
-  const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;
-  if (total == 0) return 0;
-  const int64_t blocks64 = (total + 255) / 256;
-  const int blocks = (int)(blocks64 < 65535 * 16 ? blocks64 : 65535 * 16);
-  qconv_generic_kernel<<<blocks, 256, 0, ctx.stream>>>(p);
-  ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
-}
-
-// ------------------------------------------------------------------ QLinearAdd (same shape)
-__global__ void qlinear_add_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b,
-                                   uint8_t* __restrict__ y, int64_t count, int as, int bs, int ys_signed, int az,
-                                   int bz, float sa, float sb, float sy, float yz) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
-    y[i] = (uint8_t)qadd(load_8bit(a[i], as), az, sa, load_8bit(b[i], bs), bz, sb, sy, yz, ys_signed);
-  }
-}
-
-int launch_qlinear_add(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
-  const int64_t full_batch = op.ip[QA_BATCH] > 0 ? op.ip[QA_BATCH] : 1;
-  const int64_t count = op.ip[QA_COUNT] / full_batch * (op.ip[QA_BATCH] > 0 ? eff_batch(ctx, full_batch) : 1);
-  if (count == 0) return 0;
-  const int64_t blocks64 = (count + 255) / 256;
-  const int blocks = (int)(blocks64 < 148 * 64 ? blocks64 : 148 * 64);
-  qlinear_add_kernel<<<blocks, 256, 0, ctx.stream>>>(
-      (const uint8_t*)ptrs[op.t[0]], (const uint8_t*)ptrs[op.t[1]], (uint8_t*)ptrs[op.t[2]], count,
-      (int)op.ip[QA_A_SIGNED], (int)op.ip[QA_B_SIGNED], (int)op.ip[QA_Y_SIGNED], (int)op.ip[QA_A_ZERO],
-      (int)op.ip[QA_B_ZERO], (float)op.fp[QAF_A_SCALE], (float)op.fp[QAF_B_SCALE], (float)op.fp[QAF_Y_SCALE],
-      (float)op.ip[QA_Y_ZERO]);
+  const size_t smem = (size_t)c * (w + 4);
+  if (smem > 48 * 1024 || c % 16) return 5;
+  dim3 grid((unsigned)h, (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));
+  pad_planar_kernel<<<grid, 256, smem, ctx.stream>>>(
+      (const uint8_t*)ptrs[op.t[0]], (uint8_t*)ptrs[op.t[1]], c, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
+      (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint64_t)op.ip[PAD_ROWS] * 16u, (uint32_t)op.ip[PAD_XOR]);
   ++*launches;
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

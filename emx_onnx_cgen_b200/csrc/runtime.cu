@@ -44,6 +44,8 @@ const KernelEntry kKernels[] = {
     {emx::K_QCONV_TC, emx::prepare_qconv_tc, emx::launch_qconv_tc, "qconv_tc"},
     {emx::K_QCONV_GENERIC, nullptr, emx::launch_qconv_generic, "qconv_generic"},
     {emx::K_QLINEAR_ADD, nullptr, emx::launch_qlinear_add, "qlinear_add"},
+    {emx::K_GEMM_F32, nullptr, emx::launch_gemm_f32, "gemm_f32"},
+    {emx::K_RELU_F32, nullptr, emx::launch_relu_f32, "relu_f32"},
 };
 
 const KernelEntry* find_kernel(uint32_t id) {

@@ -35,4 +35,5 @@ def _parse(text: str) -> dict[str, int]:
 
 ENUMS = _parse(_HEADER.read_text())
 globals().update(ENUMS)
+IP_BATCHED_SLOT = 39  # kernels.h: IP_BATCHED = EMX_OP_MAX_IPARAMS - 1
 NAMES = {v: k[2:].lower() for k, v in ENUMS.items() if k.startswith("K_")}

@@ -112,6 +112,7 @@ class _Builder:
         self.weights = bytearray()
         self.arena = 0
         self.ops: list[PlanOp] = []
+        self.all_batched = True
 
     def weight(self, arr: np.ndarray, dtype: str, name: str = "") -> int:
         arr = np.ascontiguousarray(arr)
@@ -132,8 +133,12 @@ class _Builder:
         self.tensors.append(PlanTensor(kind, dtype, off, nbytes, shape, batch_axis, name))
         return len(self.tensors) - 1
 
-    def op(self, kernel: int, tensors, ip=None, fp=None, label="") -> None:
-        self.ops.append(PlanOp(kernel, list(tensors), dict(ip or {}), dict(fp or {}), label))
+    def op(self, kernel: int, tensors, ip=None, fp=None, label="", batched: bool = False) -> None:
+        ip = dict(ip or {})
+        ip[K.IP_BATCHED_SLOT] = 1 if batched else 0
+        self.ops.append(PlanOp(kernel, list(tensors), ip, dict(fp or {}), label))
+        if not batched:
+            self.all_batched = False
 
     def serialize(self, inputs: list[int], outputs: list[int], batch: int, flags: int) -> bytes:
         out = bytearray()
@@ -166,6 +171,7 @@ class _Padded:
     pt: int
     pl: int
     xor: int
+    rows: int
 
 
 class B200PlanEmitter:
@@ -217,6 +223,13 @@ class B200PlanEmitter:
         for name in out_names:
             if name not in self._written_outputs:
                 raise UnsupportedOpError(f"graph output {name} is not produced by any op")
+        if batch > 0 and not b.all_batched:
+            # some op's leading extent is not the batch: the plan runs whole only
+            batch, flags = 0, 0
+            for t in b.tensors:
+                t.batch_axis = -1
+            for op in b.ops:
+                op.ip[K.IP_BATCHED_SLOT] = 0
 
         blob = b.serialize([self._nchw[n] for n in in_names], [self._outputs[n] for n in out_names], batch,
                            flags)
@@ -339,6 +352,22 @@ class B200PlanEmitter:
                     continue
                 self._need_rowmajor.add(name)
         self._ops = ops
+        # tensors whose axis 0 follows the plan batch
+        self._batched_names: set[str] = set()
+        if self._batch > 0:
+            self._batched_names.update(n for n in self._nchw)  # graph inputs
+            for op in ops:
+                ins = self._op_inputs(op)
+                if not ins or ins[0] not in self._batched_names:
+                    continue
+                if _name(op) == "GemmOp" and int(op.trans_a):
+                    continue
+                if _name(op) == "LstmOp":
+                    continue
+                for o in self._op_outputs(op):
+                    shp = tuple(self._shape(o))
+                    if shp and shp[0] == self._batch:
+                        self._batched_names.add(o)
         del tc_inputs, resid_inputs
 
     @staticmethod
@@ -397,29 +426,29 @@ class B200PlanEmitter:
         return {"xor": xor, "a_signed": a_signed, "pads": (pt, pl, pb, pr)}
 
     def _padded_of(self, name: str) -> _Padded:
-        """Zero-bordered NHWC copy of ``name`` (created by a pad op if the
-        producer did not write it directly)."""
+        """Zero-bordered chunk-planar copy of ``name`` (created by a pad op if
+        the producer did not write it directly)."""
         if name in self._padded:
             return self._padded[name]
-        pt, pl, pb, pr = self._need_pad[name]
-        xor = self._need_xor[name]
+        pd = self._new_padded(name)
         n, c, h, w = self._shape(name)
-        hp, wp = h + pt + pb, w + pl + pr
-        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (n, hp, wp, c), name=name + ":nhwc")
         src = self._src(name)
-        self._b.op(K.K_PAD_NHWC, [src, tid],
-                   {K.PAD_N: n, K.PAD_C: c, K.PAD_H: h, K.PAD_W: w, K.PAD_TOP: pt, K.PAD_LEFT: pl,
-                    K.PAD_HP: hp, K.PAD_WP: wp, K.PAD_XOR: xor}, label=f"{name} -> NHWC")
-        pd = _Padded(tid, hp, wp, pt, pl, xor)
-        self._padded[name] = pd
+        self._b.op(K.K_PAD_NHWC, [src, pd.tid],
+                   {K.PAD_N: n, K.PAD_C: c, K.PAD_H: h, K.PAD_W: w, K.PAD_TOP: pd.pt, K.PAD_LEFT: pd.pl,
+                    K.PAD_HP: pd.hp, K.PAD_WP: pd.wp, K.PAD_XOR: pd.xor, K.PAD_ROWS: pd.rows},
+                   label=f"{name} -> planar", batched=n == self._batch)
         return pd
 
     def _new_padded(self, name: str) -> _Padded:
+        """Allocate the chunk-planar zero-bordered tensor [C/16][rows][16 B];
+        rows = N*Hp*Wp + a tail that covers the last conv windows (up to 9
+        kernel rows of Wp plus a 256-row window)."""
         pt, pl, pb, pr = self._need_pad[name]
         n, c, h, w = self._shape(name)
         hp, wp = h + pt + pb, w + pl + pr
-        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (n, hp, wp, c), name=name + ":nhwc")
-        pd = _Padded(tid, hp, wp, pt, pl, self._need_xor[name])
+        rows = n * hp * wp + 9 * wp + 264
+        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (c // 16, rows, 16), name=name + ":planar")
+        pd = _Padded(tid, hp, wp, pt, pl, self._need_xor[name], rows)
         self._padded[name] = pd
         return pd
 
@@ -456,7 +485,8 @@ class B200PlanEmitter:
             K.QG_X_SIGNED: int(_suffix(op.input_dtype) == "i8"), K.QG_W_SIGNED: int(_suffix(op.weight_dtype) == "i8"),
             K.QG_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QG_X_ZERO: zx, K.QG_Y_ZERO: zy,
             K.QG_WS_PER_CH: int(ws.size > 1), K.QG_WZ_PER_CH: int(wz.size > 1)},
-            {K.QGF_X_SCALE: float(xs), K.QGF_Y_SCALE: float(ys)}, label=f"{op.output} (generic)")
+            {K.QGF_X_SCALE: float(xs), K.QGF_Y_SCALE: float(ys)}, label=f"{op.output} (generic)",
+            batched=n == self._batch)
 
     def _emit_qconv_tc(self, i, op, cfg):
         xs = np.float32(self._scalar(op.input_scale, "x_scale"))
@@ -481,7 +511,7 @@ class B200PlanEmitter:
         oh, ow = op.out_spatial
         ip = {K.QC_N: n, K.QC_CIN: cin, K.QC_OC: oc, K.QC_KH: kh, K.QC_KW: kw, K.QC_HP: xin.hp, K.QC_WP: xin.wp,
               K.QC_OH: oh, K.QC_OW: ow, K.QC_A_SIGNED: cfg["a_signed"], K.QC_Y_ZERO: zy,
-              K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8")}
+              K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QC_X_ROWS: xin.rows}
         fp = {}
         t_r = -1
         out_name = op.output
@@ -500,7 +530,7 @@ class B200PlanEmitter:
             ip.update({K.QC_HAS_ADD: 1, K.QC_C_ZERO: int(self._scalar(c_z, "add zero")),
                        K.QC_R_ZERO: int(self._scalar(r_z, "add zero")), K.QC_R_XOR: rp.xor,
                        K.QC_R_SIGNED: int(self._dtype(resid) == "i8"), K.QC_R_HP: rp.hp, K.QC_R_WP: rp.wp,
-                       K.QC_R_PT: rp.pt, K.QC_R_PL: rp.pl,
+                       K.QC_R_PT: rp.pt, K.QC_R_PL: rp.pl, K.QC_R_ROWS: rp.rows,
                        K.QC_ADD_ZERO: int(self._scalar(add.output_zero_point, "add zero")),
                        K.QC_ADD_SIGNED: int(_suffix(add.dtype) == "i8")})
             fp = {K.QCF_C_SCALE: float(np.float32(self._scalar(c_s, "add scale"))),
@@ -513,12 +543,13 @@ class B200PlanEmitter:
         if padded_out:
             yp = self._new_padded(out_name)
             ip.update({K.QC_Y_LAYOUT: 0, K.QC_Y_XOR: yp.xor, K.QC_Y_HP: yp.hp, K.QC_Y_WP: yp.wp,
-                       K.QC_Y_PT: yp.pt, K.QC_Y_PL: yp.pl})
+                       K.QC_Y_PT: yp.pt, K.QC_Y_PL: yp.pl, K.QC_Y_ROWS: yp.rows})
             t_y = yp.tid
         else:
             t_y = self._dest(out_name, out_dtype, (n, oc, oh, ow))
             ip.update({K.QC_Y_LAYOUT: 1})
-        self._b.op(K.K_QCONV_TC, [xin.tid, t_w, t_e, t_r, t_y], ip, fp, label=label + " (tcgen05 i8)")
+        self._b.op(K.K_QCONV_TC, [xin.tid, t_w, t_e, t_r, t_y], ip, fp, label=label + " (tcgen05 i8)",
+                   batched=n == self._batch)
         if padded_out is False and out_name in self._need_pad:
             self._padded_of(out_name)  # consumers also need the NHWC copy
 
@@ -540,4 +571,71 @@ class B200PlanEmitter:
             {K.QAF_A_SCALE: float(np.float32(self._scalar(op.input0_scale, "a_scale"))),
              K.QAF_B_SCALE: float(np.float32(self._scalar(op.input1_scale, "b_scale"))),
              K.QAF_Y_SCALE: float(np.float32(self._scalar(op.output_scale, "y_scale")))},
-            label=op.output)
+            label=op.output, batched=batched)
+
+    # ------------------------------------------------------------------ Gemm (+ Relu)
+    def _fused_relu_of(self, i, op):
+        """Index of a Relu that only consumes this op's output (fused into its epilogue)."""
+        out = op.output
+        cons = self._consumers.get(out, [])
+        if out in self._graph_outputs or len(cons) != 1:
+            return None
+        c = self._ops[cons[0]]
+        if _name(c) == "UnaryOp" and _fn(c) == "RELU" and c.input0 == out:
+            return cons[0]
+        return None
+
+    def _emit_GemmOp(self, i, op):
+        if self._dtype(op.input_a) != "f32" or self._dtype(op.input_b) != "f32":
+            raise UnsupportedOpError("Gemm: only fp32 has a B200 kernel")
+        sa, sb = self._shape(op.input_a), self._shape(op.input_b)
+        ta, tb = int(op.trans_a), int(op.trans_b)
+        m, k = (sa[1], sa[0]) if ta else (sa[0], sa[1])
+        n = sb[0] if tb else sb[1]
+        a, b_ = self._src(op.input_a), self._src(op.input_b)
+        t_c, mode = -1, 0
+        if op.input_c is not None:
+            cs = tuple(self._shape(op.input_c))
+            size = int(np.prod(cs)) if cs else 1
+            if size == 1:
+                mode = 1
+            elif len(cs) == 1:
+                mode = 2 if cs[0] == n else 3
+            elif cs == (1, n):
+                mode = 2
+            elif cs == (m, 1):
+                mode = 3
+            else:
+                mode = 4
+            t_c = self._src(op.input_c)
+        relu_i = self._fused_relu_of(i, op)
+        out = op.output
+        if relu_i is not None:
+            self._absorbed.add(relu_i)
+            out = self._ops[relu_i].output
+        y = self._dest(out, "f32", (m, n))
+        self._b.op(K.K_GEMM_F32, [a, b_, t_c, y], {
+            K.GM_M: m, K.GM_N: n, K.GM_K: k, K.GM_TRANS_A: ta, K.GM_TRANS_B: tb, K.GM_BIAS_MODE: mode,
+            K.GM_RELU: int(relu_i is not None)},
+            {K.GMF_ALPHA: float(np.float32(op.alpha)), K.GMF_BETA: float(np.float32(op.beta))},
+            label=f"{op.output}" + (f" + Relu -> {out}" if relu_i is not None else "") + " (fp32, reference order)",
+            batched=(not ta) and m == self._batch and self._is_batched(op.input_a))
+
+    def _is_batched(self, name: str) -> bool:
+        """Whether tensor ``name``'s axis 0 follows the plan batch (graph input or
+        produced from one by batched ops)."""
+        return name in self._batched_names
+
+    def _emit_UnaryOp(self, i, op):
+        fn = _fn(op)
+        dt = self._dtype(op.input0)
+        shape = tuple(self._shape(op.input0))
+        x = self._src(op.input0)
+        y = self._dest(op.output, dt, shape)
+        count = int(np.prod(shape))
+        rows = shape[0] if shape and shape[0] == self._batch and self._is_batched(op.input0) else 0
+        ip = {K.EW_COUNT: count, K.EW_ROWS: rows}
+        if fn == "RELU" and dt == "f32":
+            self._b.op(K.K_RELU_F32, [x, y], ip, label=op.output, batched=rows > 0)
+        else:
+            raise UnsupportedOpError(f"Unary {fn} on {dt} has no B200 kernel")

@@ -21,7 +21,15 @@ def plan_for(workload, **kw):
 
 
 def assert_bitexact(got: np.ndarray, ref: np.ndarray, what: str = ""):
+    """Identical bits, except that any NaN equals any NaN (x86 and the GPU
+    produce different NaN payloads; the reference's ULP metric treats NaN/NaN
+    as equal, shared/ulp.py:26-50)."""
     assert got.shape == ref.shape and got.dtype == ref.dtype, (got.shape, ref.shape, got.dtype, ref.dtype)
+    if got.dtype.kind == "f":
+        gn, rn = np.isnan(got), np.isnan(ref)
+        assert np.array_equal(gn, rn), f"{what}: NaN positions differ"
+        got = np.where(gn, 0, got).astype(got.dtype)
+        ref = np.where(rn, 0, ref).astype(ref.dtype)
     if not np.array_equal(got.view(np.uint8), ref.view(np.uint8)):
         diff = np.argwhere(got != ref)
         raise AssertionError(f"{what}: {len(diff)} of {got.size} elements differ; first at {diff[:5].tolist()}: "
