@@ -12,6 +12,7 @@
 // FADD), i.e. half the FFMA peak; HBM traffic (weights once) is far below it.
 #include "host_util.h"
 #include "kernels.h"
+#include "tc100.cuh"
 
 namespace emx {
 
@@ -36,6 +37,8 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const G
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  pdl_wait();
+  pdl_launch_dependents();
 
   float acc[RM][RN];
 #pragma unroll
@@ -162,13 +165,15 @@ int launch_gemm_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
     }
   }
   dim3 grid((unsigned)((p.n + v->bn - 1) / v->bn), (unsigned)((p.m + v->bm - 1) / v->bm));
-  v->fn<<<grid, v->threads, 0, ctx.stream>>>(p);
+  cudaError_t e = launch_pdl(v->fn, grid, dim3(v->threads), 0, ctx.stream, p);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 // ------------------------------------------------------------------ Relu (standalone)
 __global__ void relu_f32_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float a = x[i];
     y[i] = a > 0.0f ? a : 0.0f;
@@ -180,9 +185,10 @@ int launch_relu_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   const int64_t n = op.ip[EW_COUNT] / (op.ip[EW_ROWS] > 0 ? op.ip[EW_ROWS] : 1) * rows;
   if (n == 0) return 0;
   const int blocks = (int)((n + 255) / 256 < 148 * 32 ? (n + 255) / 256 : 148 * 32);
-  relu_f32_kernel<<<blocks, 256, 0, ctx.stream>>>((const float*)ptrs[op.t[0]], (float*)ptrs[op.t[1]], n);
+  cudaError_t e = launch_pdl(relu_f32_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const float*)ptrs[op.t[0]],
+                             (float*)ptrs[op.t[1]], n);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 }  // namespace emx

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "plan_format.h"
 
 namespace emx {
@@ -80,6 +82,25 @@ inline int64_t eff_batch(const LaunchCtx& c, const PlanOp& op, int64_t compiled)
   return (c.batch > 0 && op.ip[IP_BATCHED]) ? c.batch : compiled;
 }
 
+// Launch with programmatic stream serialisation allowed (see pdl_wait() in
+// tc100.cuh): every kernel of the library goes through this helper and waits
+// on its predecessor inside the kernel.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Opaque per-op state prepared once at plan load (tensor maps, chosen variant).
 struct alignas(64) OpState {
   unsigned char bytes[512];
@@ -96,6 +117,7 @@ int launch_pad_nhwc(const PlanOp&, void* const*, const OpState*, const LaunchCtx
 int launch_qconv_generic(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qlinear_add(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_gemm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+void launch_hold(const int* flag, int seq, int* err, cudaStream_t stream);
 int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

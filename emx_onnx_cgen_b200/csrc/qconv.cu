@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
         const uint32_t n = min(16384u, p.b_bytes - off);
         bulk_load(s_b + off, p.w_img + off, n, bbar);
       }
+      pdl_wait();  // activations come from the preceding kernel
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -240,6 +242,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
     const int col0 = ((warp - 4) >> 2) * HALF;
     const int row = quarter * 32 + lane;
     const int64_t hpwp = (int64_t)p.hp * p.wp;
+    pdl_wait();  // residual reads and output writes follow the preceding kernel
     int it = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++it) {
       __syncwarp();
@@ -478,9 +481,9 @@ int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, con
   p.err = ctx.d_error;
   if (p.n_tiles <= 0) return 0;
   const int grid = p.n_tiles < ctx.num_sms ? p.n_tiles : ctx.num_sms;
-  kQcVariants[st->variant].fn<<<grid, QC_THREADS, st->smem_bytes, ctx.stream>>>(p);
+  cudaError_t e = launch_pdl(kQcVariants[st->variant].fn, dim3(grid), dim3(QC_THREADS), st->smem_bytes, ctx.stream, p);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 // ------------------------------------------------------------------ NCHW -> chunk-planar zero-bordered
@@ -491,6 +494,8 @@ __global__ void pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __rest
                                   int pt, int pl, int hp, int wp, uint64_t plane_pitch, uint32_t xr) {
   extern __shared__ uint8_t s[];  // [c][w + 4]
   const int row = blockIdx.x, n = blockIdx.y;
+  pdl_wait();
+  pdl_launch_dependents();
   const int ws = w + 4;
   const uint8_t* src = x + ((size_t)n * c * h + row) * w;
   for (int i = threadIdx.x; i < c * w; i += blockDim.x) {
@@ -520,11 +525,12 @@ int launch_pad_nhwc(const PlanOp& op, void* const* ptrs, const OpState*, const L
   const size_t smem = (size_t)c * (w + 4);
   if (smem > 48 * 1024 || c % 16) return 5;
   dim3 grid((unsigned)h, (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));
-  pad_planar_kernel<<<grid, 256, smem, ctx.stream>>>(
-      (const uint8_t*)ptrs[op.t[0]], (uint8_t*)ptrs[op.t[1]], c, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
-      (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint64_t)op.ip[PAD_ROWS] * 16u, (uint32_t)op.ip[PAD_XOR]);
+  cudaError_t e = launch_pdl(pad_planar_kernel, grid, dim3(256), smem, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
+                             (uint8_t*)ptrs[op.t[1]], c, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
+                             (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint64_t)op.ip[PAD_ROWS] * 16u,
+                             (uint32_t)op.ip[PAD_XOR]);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 }  // namespace emx

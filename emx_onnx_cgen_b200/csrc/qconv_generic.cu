@@ -6,6 +6,7 @@
 #include "host_util.h"
 #include "kernels.h"
 #include "qmath.cuh"
+#include "tc100.cuh"
 
 namespace emx {
 
@@ -25,6 +26,8 @@ struct QConvGenericParams {
 };
 
 __global__ void qconv_generic_kernel(const QConvGenericParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;
   const int gic = p.c / p.group, goc = p.oc / p.group;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -94,15 +97,17 @@ int launch_qconv_generic(const PlanOp& op, void* const* ptrs, const OpState*, co
   if (total == 0) return 0;
   const int64_t blocks64 = (total + 255) / 256;
   const int blocks = (int)(blocks64 < 65535 * 16 ? blocks64 : 65535 * 16);
-  qconv_generic_kernel<<<blocks, 256, 0, ctx.stream>>>(p);
+  cudaError_t e = launch_pdl(qconv_generic_kernel, dim3(blocks), dim3(256), 0, ctx.stream, p);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 // ------------------------------------------------------------------ QLinearAdd (same shape)
 __global__ void qlinear_add_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b,
                                    uint8_t* __restrict__ y, int64_t count, int as, int bs, int ys_signed, int az,
                                    int bz, float sa, float sb, float sy, float yz) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
     y[i] = (uint8_t)qadd_exact(load_8bit(a[i], as), az, sa, load_8bit(b[i], bs), bz, sb, sy, yz, ys_signed);
   }
@@ -114,13 +119,13 @@ int launch_qlinear_add(const PlanOp& op, void* const* ptrs, const OpState*, cons
   if (count == 0) return 0;
   const int64_t blocks64 = (count + 255) / 256;
   const int blocks = (int)(blocks64 < 148 * 64 ? blocks64 : 148 * 64);
-  qlinear_add_kernel<<<blocks, 256, 0, ctx.stream>>>(
-      (const uint8_t*)ptrs[op.t[0]], (const uint8_t*)ptrs[op.t[1]], (uint8_t*)ptrs[op.t[2]], count,
-      (int)op.ip[QA_A_SIGNED], (int)op.ip[QA_B_SIGNED], (int)op.ip[QA_Y_SIGNED], (int)op.ip[QA_A_ZERO],
-      (int)op.ip[QA_B_ZERO], (float)op.fp[QAF_A_SCALE], (float)op.fp[QAF_B_SCALE], (float)op.fp[QAF_Y_SCALE],
-      (float)op.ip[QA_Y_ZERO]);
+  cudaError_t e = launch_pdl(
+      qlinear_add_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
+      (const uint8_t*)ptrs[op.t[1]], (uint8_t*)ptrs[op.t[2]], count, (int)op.ip[QA_A_SIGNED], (int)op.ip[QA_B_SIGNED],
+      (int)op.ip[QA_Y_SIGNED], (int)op.ip[QA_A_ZERO], (int)op.ip[QA_B_ZERO], (float)op.fp[QAF_A_SCALE],
+      (float)op.fp[QAF_B_SCALE], (float)op.fp[QAF_Y_SCALE], (float)op.ip[QA_Y_ZERO]);
   ++*launches;
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return e == cudaSuccess ? 0 : 4;
 }
 
 }  // namespace emx

@@ -82,6 +82,22 @@ struct emx_plan {
   std::vector<cudaEvent_t> ev_begin, ev_end;
   std::vector<double> op_ms;
   int64_t profiled_runs = 0;
+  // CUDA graphs of the op sequence, keyed by the resolved I/O pointers
+  struct GraphEntry {
+    std::vector<void*> key;
+    int64_t batch = 0;
+    bool profiling = false;
+    int launches = 0;
+    uint64_t last_use = 0;
+    cudaGraphExec_t exec = nullptr;
+  };
+  bool use_graphs = true;
+  std::vector<GraphEntry> graphs;
+  uint64_t graph_clock = 0;
+  // host-mapped release flag for the profiling hold kernel
+  int* h_hold = nullptr;
+  int* d_hold = nullptr;
+  int hold_seq = 0;
 };
 
 namespace {
@@ -194,6 +210,8 @@ void destroy(emx_plan* p) {
   int cur = 0;
   cudaGetDevice(&cur);
   cudaSetDevice(p->device);
+  for (auto& g : p->graphs) cudaGraphExecDestroy(g.exec);
+  if (p->h_hold) cudaFreeHost(p->h_hold);
   for (auto e : p->ev_begin) cudaEventDestroy(e);
   for (auto e : p->ev_end) cudaEventDestroy(e);
   if (p->own_stream) cudaStreamDestroy(p->own_stream);
@@ -202,6 +220,83 @@ void destroy(emx_plan* p) {
   if (p->d_error) cudaFree(p->d_error);
   cudaSetDevice(cur);
   delete p;
+}
+
+// Enqueue every op of the plan on `stream`.  In profiling mode each op is
+// bracketed by timing events and the whole sequence sits behind a hold kernel
+// that spins (at most ~1 s) on a host-mapped flag until the host has
+// enqueued everything, so the GPU then runs the ops back to back and the
+// events measure kernels rather than host launch gaps.
+int launch_ops(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches) {
+  emx::LaunchCtx ctx{stream, p->d_error, run_batch, p->num_sms};
+  const int seq = ++p->hold_seq;
+  if (p->profiling) emx::launch_hold(p->d_hold, seq, p->d_error, stream);
+  for (size_t i = 0; i < p->ops.size(); ++i) {
+    if (p->profiling) cudaEventRecord(p->ev_begin[i], stream);
+    int rc = p->entries[i]->launch(p->ops[i], p->ptrs.data(), &p->states[i], ctx, launches);
+    if (p->profiling) cudaEventRecord(p->ev_end[i], stream);
+    if (rc) {
+      if (p->profiling) *(volatile int*)p->h_hold = seq;
+      cudaError_t e = cudaGetLastError();
+      return set_error(rc == EMX_ERR_CUDA ? EMX_ERR_CUDA : rc, "op %zu (%s) launch failed: %s", i,
+                       p->entries[i]->name, cudaGetErrorString(e));
+    }
+  }
+  if (p->profiling) {
+    __sync_synchronize();
+    *(volatile int*)p->h_hold = seq;
+  }
+  return EMX_OK;
+}
+
+// The plan's kernels as one CUDA graph per (I/O pointers, batch, profiling):
+// captured once on the plan's private stream, replayed with one
+// cudaGraphLaunch on the caller's stream.  Host<->device staging copies stay
+// outside the graph (they may involve pageable host memory).
+int run_graph(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches) {
+  std::vector<void*> key;
+  key.reserve(p->inputs.size() + p->outputs.size());
+  for (uint32_t id : p->inputs) key.push_back(p->ptrs[id]);
+  for (uint32_t id : p->outputs) key.push_back(p->ptrs[id]);
+  ++p->graph_clock;
+  for (auto& g : p->graphs) {
+    if (g.batch == run_batch && g.profiling == p->profiling && g.key == key) {
+      g.last_use = p->graph_clock;
+      *launches += g.launches;
+      CUDA_TRY(cudaGraphLaunch(g.exec, stream), "cudaGraphLaunch");
+      return EMX_OK;
+    }
+  }
+  cudaGraph_t graph = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(p->own_stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+  int n = 0;
+  int rc = launch_ops(p, run_batch, p->own_stream, &n);
+  cudaError_t e = cudaStreamEndCapture(p->own_stream, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return set_error(EMX_ERR_CUDA, "end capture: %s", cudaGetErrorString(e));
+  emx_plan::GraphEntry entry;
+  entry.key = key;
+  entry.batch = run_batch;
+  entry.profiling = p->profiling;
+  entry.launches = n;
+  entry.last_use = p->graph_clock;
+  e = cudaGraphInstantiate(&entry.exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return set_error(EMX_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  if (p->graphs.size() >= 8) {  // evict the least recently used
+    size_t lru = 0;
+    for (size_t i = 1; i < p->graphs.size(); ++i)
+      if (p->graphs[i].last_use < p->graphs[lru].last_use) lru = i;
+    cudaGraphExecDestroy(p->graphs[lru].exec);
+    p->graphs.erase(p->graphs.begin() + lru);
+  }
+  p->graphs.push_back(entry);
+  *launches += n;
+  CUDA_TRY(cudaGraphLaunch(entry.exec, stream), "cudaGraphLaunch");
+  return EMX_OK;
 }
 
 bool is_device_pointer(const void* ptr) {
@@ -328,17 +423,14 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
       p->pending.push_back({static_cast<uint8_t*>(dst) + off, staging, bytes});
     }
   }
-  emx::LaunchCtx ctx{stream, p->d_error, full > 0 ? batch_count : 0, p->num_sms};
+  const int64_t run_batch = full > 0 ? batch_count : 0;
   int launches = 0;
-  for (size_t i = 0; i < p->ops.size(); ++i) {
-    if (p->profiling) cudaEventRecord(p->ev_begin[i], stream);
-    int rc = p->entries[i]->launch(p->ops[i], p->ptrs.data(), &p->states[i], ctx, &launches);
-    if (p->profiling) cudaEventRecord(p->ev_end[i], stream);
-    if (rc) {
-      cudaError_t e = cudaGetLastError();
-      return set_error(rc == EMX_ERR_CUDA ? EMX_ERR_CUDA : rc, "op %zu (%s) launch failed: %s", i,
-                       p->entries[i]->name, cudaGetErrorString(e));
-    }
+  if (p->use_graphs && !p->profiling) {
+    int rc = run_graph(p, run_batch, stream, &launches);
+    if (rc) return rc;
+  } else {
+    int rc = launch_ops(p, run_batch, stream, &launches);
+    if (rc) return rc;
   }
   for (const auto& pd : p->pending)
     CUDA_TRY(cudaMemcpyAsync(pd.host, pd.dev, pd.bytes, cudaMemcpyDeviceToHost, stream), "output download");
@@ -386,9 +478,21 @@ int emx_b200_plan_info(const emx_plan_t* p, emx_plan_info_t* info) {
 
 int64_t emx_b200_launch_count(const emx_plan_t* p) { return p ? p->launches_total : -1; }
 
+int emx_b200_set_graphs(emx_plan_t* p, int enable) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  p->use_graphs = enable != 0;
+  return EMX_OK;
+}
+
 int emx_b200_set_profiling(emx_plan_t* p, int enable) {
   if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
   CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  if (enable && !p->h_hold) {
+    CUDA_TRY(cudaHostAlloc((void**)&p->h_hold, sizeof(int), cudaHostAllocMapped), "hold flag");
+    *p->h_hold = 0;
+    p->hold_seq = 0;
+    CUDA_TRY(cudaHostGetDevicePointer((void**)&p->d_hold, p->h_hold, 0), "hold flag device pointer");
+  }
   if (enable && p->ev_begin.empty()) {
     p->ev_begin.resize(p->ops.size());
     p->ev_end.resize(p->ops.size());

@@ -220,6 +220,17 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialisation allowed, so the next kernel may start
+// its independent prologue while this one drains.  pdl_wait() blocks until the
+// preceding grid has completed and its memory is visible: it must come before
+// the first read of a predecessor's output and the first write of anything a
+// predecessor may still read.  pdl_launch_dependents() lets the next grid be
+// scheduled (its CTAs then wait in their own pdl_wait()).  Both are no-ops
+// when the kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -24,7 +24,7 @@ STATUS_NAMES = {0: "EMX_OK", 1: "EMX_ERR_INVALID_ARGUMENT", 2: "EMX_ERR_PLAN_FOR
 
 EXPORTED = ("emx_b200_version", "emx_b200_last_error", "emx_b200_plan_load", "emx_b200_plan_load_mem",
             "emx_b200_run", "emx_b200_sync", "emx_b200_plan_free", "emx_b200_plan_info",
-            "emx_b200_launch_count", "emx_b200_set_profiling", "emx_b200_op_times")
+            "emx_b200_launch_count", "emx_b200_set_profiling", "emx_b200_op_times", "emx_b200_set_graphs")
 
 
 class EmxError(RuntimeError):
@@ -65,6 +65,8 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.emx_b200_launch_count.argtypes = [vp]
         lib.emx_b200_launch_count.restype = i64
         lib.emx_b200_set_profiling.argtypes = [vp, i32]
+        lib.emx_b200_set_graphs.argtypes = [vp, i32]
+        lib.emx_b200_set_graphs.restype = i32
         lib.emx_b200_op_times.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
                                           ctypes.POINTER(i64)]
         for name in ("emx_b200_plan_load", "emx_b200_plan_load_mem", "emx_b200_run", "emx_b200_sync",
@@ -133,6 +135,9 @@ class Session:
         inf = PlanInfo()
         _check(self.lib.emx_b200_plan_info(self.handle, ctypes.byref(inf)))
         return inf
+
+    def set_graphs(self, enable: bool) -> None:
+        _check(self.lib.emx_b200_set_graphs(self.handle, 1 if enable else 0))
 
     def set_profiling(self, enable: bool) -> None:
         _check(self.lib.emx_b200_set_profiling(self.handle, 1 if enable else 0))

@@ -112,6 +112,12 @@ int emx_b200_set_profiling(emx_plan_t *plan, int enable);
  * cover, since profiling was last enabled. */
 int emx_b200_op_times(const emx_plan_t *plan, double *ms, int32_t n_ops, int64_t *runs);
 
+/* CUDA-graph replay of the op sequence (default on): the first run with a
+ * given set of input/output addresses and batch captures the plan's kernels
+ * into a graph, later runs with the same addresses replay it with one launch.
+ * Off: every run launches the kernels one by one. */
+int emx_b200_set_graphs(emx_plan_t *plan, int enable);
+
 #ifdef __cplusplus
 }
 #endif
