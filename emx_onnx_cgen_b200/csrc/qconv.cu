@@ -11,29 +11,38 @@
 // acc exactly; the epilogue repeats the float steps one rounding at a time
 // (qmath.cuh).
 //
-// Activation layout between these kernels: "chunk-planar, zero-bordered":
-// [C/16 planes][rows][16 bytes], row = n*Hp*Wp + hp*Wp + wp over the image
-// padded by the conv's pads (Hp = H+pads, Wp = W+pads), plus a tail of spare
-// rows per plane.  Border rows are zero and never written.
+// Activation layout between these kernels: "swizzled NHWC, zero-bordered":
+// [rows][C bytes], row = n*Hp*Wp + hp*Wp + wp over the image padded by the
+// conv's pads (Hp = H+pads, Wp = W+pads), plus a tail of spare rows.  Inside a
+// row the 16-byte channel chunks are permuted by the tensor-core swizzle of a
+// C-byte row (swz_chunk in tc100.cuh).  Border rows are zero, never written.
 //   * Output pixel (oh, ow) of image n is the "pitched" row q = n*Hp*Wp +
 //     oh*Wp + ow; tap (kh, kw) reads input row q + kh*Wp + kw.  A tile of 128
-//     consecutive pitched rows needs, per kh, the window of 128+KW-1
-//     consecutive rows starting at q0 + kh*Wp; its KW taps are that window
-//     shifted by kw rows.  Pitched rows on pad columns / pad rows give outputs
-//     that are discarded.
-//   * In each 16-byte plane the window is contiguous, so one bulk copy per
-//     plane (cp.async.bulk, no tensor map, no multicast) lands it in shared
-//     memory as [plane][rows][16 B]: exactly the SWIZZLE_NONE K-major
-//     canonical layout with SBO = 128 (8 rows x 16 B) and LBO = plane pitch.
-//     The kw shift is a 16*kw-byte offset of the descriptor start address.
+//     consecutive pitched rows therefore reads, for all taps together, the
+//     window of 128 + (KH-1)*Wp + KW-1 consecutive rows starting at q0; tap
+//     (kh, kw) is the 128-row slice starting kh*Wp + kw rows into it.
+//     Pitched rows on pad columns / pad rows give outputs that are discarded.
+//   * That window is contiguous: one bulk copy per tile (cp.async.bulk, no
+//     tensor map, no multicast) lands it in shared memory already in the
+//     swizzled K-major canonical layout (tile starts are multiples of 8 rows
+//     and stages are 1024-byte aligned, so the swizzle phase carries over); a
+//     tap is a (kh*Wp+kw)*C byte offset of the descriptor start, with the
+//     descriptor's base offset carrying the shifted phase.  Bulk copies here
+//     have a round trip of ~2 us, so throughput comes from keeping ~120 KB of
+//     windows in flight per SM (8 stages of one tile each).  The swizzle keeps
+//     the tensor cores' operand reads conflict-free (without it each MMA
+//     waited ~5x its math time on shared memory).
+//   * each CTA takes a contiguous range of tiles (neighbouring windows share
+//     most rows, which stay hot in L2).
 //   * zero padding must mean "real zero": for zero point 128 on uint8 storage
 //     the producer stores x ^ 0x80 (= x - 128 as int8) and the MMA runs
 //     s8 x s8; for zero point 0 the MMA runs on the raw bytes (u8 or s8).
 //   * weights (all taps, [tap][C/16][OC][16 B]) stay in shared memory for the
 //     CTA's lifetime; the int32 accumulator tile (128 x OC) is double-buffered
 //     in TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
-//   * warps: 0 producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-11 epilogue
-//     (two warps per TMEM lane quarter, each taking half of the OC columns).
+//   * warps: 0 producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-19 epilogue
+//     (four warps per TMEM lane quarter, each taking a quarter of the OC
+//     columns).
 #include "host_util.h"
 #include "kernels.h"
 #include "qmath.cuh"
@@ -49,11 +58,11 @@ struct QConvTcParams {
   const uint8_t* resid;
   uint8_t* y;
   int* err;
-  uint64_t x_pitch, y_pitch, r_pitch;  // bytes between 16-channel planes
-  int64_t x_rows;                      // rows allocated per input plane
+  int64_t x_rows;  // rows allocated in the input
+  uint64_t hpwp_mul, wp_mul;  // ceil(2^40 / (Hp*Wp)), ceil(2^40 / Wp)
   int batch, kh, kw, hp, wp, oh, ow;
-  int rows_box, stages, n_tiles;
-  uint32_t idesc, b_bytes, stage_bytes, plane_bytes;
+  int win_rows, stages, n_tiles;
+  uint32_t idesc, b_bytes, stage_bytes, win_bytes;
   float y_lo, y_hi, y_m_minus_zero;
   int y_layout, y_xor, y_hp, y_wp, y_pt, y_pl;
   int has_add, fast_div;
@@ -61,36 +70,78 @@ struct QConvTcParams {
   int r_xor, r_signed, r_hp, r_wp, r_pt, r_pl;
 };
 
-constexpr int QC_EPI_WARPS = 8;
-constexpr int QC_THREADS = 128 + 32 * QC_EPI_WARPS;
+// Warp roles: warp 0 producer, warps 1..2 MMA issuers (one partial
+// accumulator each: one issuing thread completes a tcgen05.mma every ~150
+// cycles whatever its N, so with N = OC = 64 two issuers keep more of the
+// tensor core busy), warps 4..19 epilogue.
+constexpr int QC_MMA_WARPS = 2;
+constexpr int QC_EPI_WARP0 = 4;
+constexpr int QC_EPI_WARPS = 16;
+constexpr int QC_THREADS = 32 * (QC_EPI_WARP0 + QC_EPI_WARPS);
 constexpr int QC_TILE_M = 128;
 
-template <int OC, int HALF>
-__device__ __forceinline__ void qc_epilogue_store(const QConvTcParams& p, const uint32_t (&out)[HALF / 4], int col0,
-                                                  int n, int oh, int ow, int64_t q) {
+// bytes of a clamped integer-valued float (see float_to_byte): gather the low
+// byte of four bit patterns into one word.
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d) {
+  const uint32_t ba = (uint32_t)__float_as_int(__fadd_rn(a, kMagic));
+  const uint32_t bb = (uint32_t)__float_as_int(__fadd_rn(b, kMagic));
+  const uint32_t bc = (uint32_t)__float_as_int(__fadd_rn(c, kMagic));
+  const uint32_t bd = (uint32_t)__float_as_int(__fadd_rn(d, kMagic));
+  return __byte_perm(__byte_perm(ba, bb, 0x0040), __byte_perm(bc, bd, 0x0040), 0x5410);
+}
+
+// Store G output bytes (G/4 words) of one pixel.
+template <int OC, int G>
+__device__ __forceinline__ void qc_store(const QConvTcParams& p, const uint32_t (&out)[G / 4], int col0, int n, int oh,
+                                         int ow) {
   if (p.y_layout == 0) {
     const int64_t ypix = ((int64_t)n * p.y_hp + oh + p.y_pt) * p.y_wp + ow + p.y_pl;
+    uint8_t* row = p.y + (uint64_t)ypix * OC;
+    if constexpr (G == 8) {
+      *reinterpret_cast<uint2*>(row + 16 * swz_chunk(ypix, col0 / 16, OC) + (col0 % 16)) = make_uint2(out[0], out[1]);
+    } else {
 #pragma unroll
-    for (int c = 0; c < HALF / 16; ++c) {
-      uint4* dst = reinterpret_cast<uint4*>(p.y + (uint64_t)(col0 / 16 + c) * p.y_pitch + (uint64_t)ypix * 16);
-      *dst = make_uint4(out[4 * c + 0], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+      for (int c = 0; c < G / 16; ++c)
+        *reinterpret_cast<uint4*>(row + 16 * swz_chunk(ypix, col0 / 16 + c, OC)) =
+            make_uint4(out[4 * c + 0], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
     }
   } else {
     const int64_t plane = (int64_t)p.oh * p.ow;
     uint8_t* yb = p.y + ((int64_t)n * OC + col0) * plane + (int64_t)oh * p.ow + ow;
 #pragma unroll
-    for (int c = 0; c < HALF; ++c) yb[(int64_t)c * plane] = (uint8_t)(out[c >> 2] >> (8 * (c & 3)));
+    for (int c = 0; c < G; ++c) yb[(int64_t)c * plane] = (uint8_t)(out[c >> 2] >> (8 * (c & 3)));
   }
-  (void)q;
+}
+
+template <int OC, int G>
+__device__ __forceinline__ void qc_load_resid(const QConvTcParams& p, uint32_t (&rb)[G / 4], int col0, int n, int oh,
+                                              int ow) {
+  const int64_t rpix = ((int64_t)n * p.r_hp + oh + p.r_pt) * p.r_wp + ow + p.r_pl;
+  const uint8_t* row = p.resid + (uint64_t)rpix * OC;
+  if constexpr (G == 8) {
+    const uint2 t = *reinterpret_cast<const uint2*>(row + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
+    rb[0] = t.x;
+    rb[1] = t.y;
+  } else {
+#pragma unroll
+    for (int c = 0; c < G / 16; ++c) {
+      const uint4 t = *reinterpret_cast<const uint4*>(row + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
+      rb[4 * c + 0] = t.x;
+      rb[4 * c + 1] = t.y;
+      rb[4 * c + 2] = t.z;
+      rb[4 * c + 3] = t.w;
+    }
+  }
 }
 
 template <int CIN, int OC>
 __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcParams p) {
-  constexpr int CHUNKS = CIN / 16;  // 16-byte channel planes per pixel
   constexpr int KSTEPS = CIN / 32;  // kind::i8 MMAs (K = 32) per tap
-  constexpr int HALF = OC / 2;      // columns per epilogue warp
-  constexpr uint32_t TMEM_COLS = (2 * OC < 32) ? 32 : 2 * OC;
-  static_assert(HALF % 16 == 0, "OC must be a multiple of 32");
+  constexpr int G = OC / 4;         // columns per epilogue warp
+  // partial accumulators (= issuing warps) per tile: 2 tiles x P x OC <= 512 TMEM columns
+  constexpr int P = QC_MMA_WARPS;
+  constexpr uint32_t TMEM_COLS = 512;
+  static_assert(G % 8 == 0, "OC must be a multiple of 32");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_b = smem;
@@ -103,31 +154,36 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
   uint64_t* accf = bars + 2 * p.stages;
   uint64_t* acce = accf + 2;
   uint64_t* bbar = acce + 2;
-  uint64_t* drain = bbar + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = bbar + 1;  // one per MMA warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + QC_MMA_WARPS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int n_mma = p.kh * p.kw * KSTEPS;   // MMAs per tile
+  const int PE = n_mma < P ? n_mma : P;     // partials (and issuing warps) in use
+  // contiguous tile range of this CTA
+  const int t_begin = (int)((int64_t)blockIdx.x * p.n_tiles / gridDim.x);
+  const int t_end = (int)((int64_t)(blockIdx.x + 1) * p.n_tiles / gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], PE);  // one commit per MMA warp
     }
     for (int a = 0; a < 2; ++a) {
-      mbar_init(&accf[a], 1);
-      mbar_init(&acce[a], 32 * QC_EPI_WARPS);
+      mbar_init(&accf[a], PE);
+      mbar_init(&acce[a], QC_EPI_WARPS);  // one arrive per epilogue warp
     }
     mbar_init(bbar, 1);
-    mbar_init(drain, 1);
+    for (int w = 0; w < QC_MMA_WARPS; ++w) mbar_init(&drain[w], 1);
     fence_barrier_init();
   }
-  if (warp == 2) {
+  if (warp == 1) {
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= 4) {
-    for (int i = threadIdx.x - 128; i < OC; i += 32 * QC_EPI_WARPS) {
+  if (warp >= QC_EPI_WARP0) {
+    for (int i = threadIdx.x - 32 * QC_EPI_WARP0; i < OC; i += 32 * QC_EPI_WARPS) {
       s_scale[i] = p.scale[i];
       s_bias[i] = p.bias[i];
     }
@@ -140,7 +196,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: weights once, then one window per (tile, kh)
+      // ---------------- producer: weights once, then one window per tile
       mbar_arrive_expect_tx(bbar, p.b_bytes);
       for (uint32_t off = 0; off < p.b_bytes; off += 16384u) {
         const uint32_t n = min(16384u, p.b_bytes - off);
@@ -151,32 +207,25 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued = 0, parity_of = 0;  // per stage: window issued, and in which phase
-      const uint32_t win_bytes = (uint32_t)p.rows_box * 16u;
-      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-        const int64_t q0 = (int64_t)tile * QC_TILE_M;
-        for (int kh = 0; kh < p.kh; ++kh) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
-          }
-          const int64_t row0 = q0 + (int64_t)kh * p.wp;
-          uint8_t* dst = s_a + (size_t)stage * p.stage_bytes;
-          if (row0 + p.rows_box > p.x_rows) {  // plan guarantees this never happens; do not read past the plane
-            record_error(p.err, DEV_BAD_CONFIG);
-            mbar_arrive(&full[stage]);
-          } else {
-            mbar_arrive_expect_tx(&full[stage], p.stage_bytes);
-#pragma unroll
-            for (int c = 0; c < CHUNKS; ++c)
-              bulk_load(dst + (size_t)c * p.plane_bytes, p.x + (uint64_t)c * p.x_pitch + (uint64_t)row0 * 16u,
-                        win_bytes, &full[stage]);
-          }
-          issued |= 1u << stage;
-          parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
-          if (++stage == p.stages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+      for (int tile = t_begin; tile < t_end; ++tile) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        const int64_t row0 = (int64_t)tile * QC_TILE_M;
+        uint8_t* dst = s_a + (size_t)stage * p.stage_bytes;
+        if (row0 + p.win_rows > p.x_rows) {  // the plan guarantees this never happens; never read past a plane
+          record_error(p.err, DEV_BAD_CONFIG);
+          mbar_arrive(&full[stage]);
+        } else {
+          mbar_arrive_expect_tx(&full[stage], p.win_bytes);
+          bulk_load(dst, p.x + (uint64_t)row0 * CIN, p.win_bytes, &full[stage]);
+        }
+        issued |= 1u << stage;
+        parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
       if (!ok) {  // error path: let every window this thread issued land before the CTA exits
@@ -184,139 +233,145 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
           if (issued & (1u << s2)) (void)mbar_wait(&full[s2], (parity_of >> s2) & 1u, nullptr, 0);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp >= 1 && warp <= PE) {
     if (lane == 0) {
-      // ---------------- MMA issuer
+      // ---------------- MMA issuers: warp 1+j issues MMAs k = j, j+P, j+2P, ...
+      // of every tile into partial accumulator j
+      const int my = warp - 1;
       bool ok = mbar_wait(bbar, 0, p.err, DEV_TIMEOUT_MMA);
       tc_fence_after();
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      const uint32_t b_plane = OC * 16u;
       const uint32_t a_base = smem_u32(s_a);
       const uint32_t b_base = smem_u32(s_b);
-      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x, ++it) {
+      for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
         const int acc = it & 1;
         if (!mbar_wait(&acce[acc], ((it >> 1) & 1) ^ 1u, p.err, DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * OC);
-        for (int kh = 0; kh < p.kh; ++kh) {
-          if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_stage = a_base + (uint32_t)stage * p.stage_bytes;
-          for (int kw = 0; kw < p.kw; ++kw) {
-            const int tap = kh * p.kw + kw;
-#pragma unroll
-            for (int s = 0; s < KSTEPS; ++s) {
-              const uint64_t adesc =
-                  smem_desc_k_noswizzle(a_stage + (uint32_t)kw * 16u + (uint32_t)(2 * s) * p.plane_bytes,
-                                        p.plane_bytes, 128u);
-              const uint64_t bdesc = smem_desc_k_noswizzle(
-                  b_base + ((uint32_t)(tap * CHUNKS + 2 * s)) * b_plane, b_plane, 128u);
-              mma_i8(d_tmem, adesc, bdesc, p.idesc, (kh | kw | s) != 0 ? 1u : 0u);
-            }
-          }
-          tc_commit(&empty[stage]);
-          if (++stage == p.stages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
+        tc_fence_after();
+        // MMA number k of the tile accumulates into partial k % P (integer
+        // partial sums are exact in any order; the epilogue adds the P
+        // partials), issued by warp 1 + k % P.
+        const uint32_t d_tmem = tmem_base + (uint32_t)((acc * P + my) * OC);
+        const uint32_t a_stage = a_base + (uint32_t)stage * p.stage_bytes;
+        for (int k = my; k < n_mma; k += PE) {
+          const int tap = k / KSTEPS, s = k - tap * KSTEPS;
+          const int kh = tap / p.kw, kw = tap - kh * p.kw;
+          const uint32_t a_tap = a_stage + (uint32_t)(kh * p.wp + kw) * CIN;
+          const uint32_t b_tap = b_base + (uint32_t)tap * (OC * CIN);
+          const uint64_t adesc = smem_desc_k_swizzled(a_tap + 32u * s, CIN);
+          const uint64_t bdesc = smem_desc_k_swizzled(b_tap + 32u * s, CIN);
+          mma_i8(d_tmem, adesc, bdesc, p.idesc, k >= PE ? 1u : 0u);
+        }
+        tc_commit(&empty[stage]);
         tc_commit(&accf[acc]);
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
       if (!ok) {  // error path: wait for this thread's MMAs before TMEM is released
-        tc_commit(drain);
-        (void)mbar_wait(drain, 0, nullptr, 0);
+        tc_commit(&drain[my]);
+        (void)mbar_wait(&drain[my], 0, nullptr, 0);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= QC_EPI_WARP0) {
     // ---------------- epilogue: TMEM -> registers -> requant (+ QLinearAdd) -> global
     const int quarter = warp & 3;
-    const int col0 = ((warp - 4) >> 2) * HALF;
+    const int col0 = ((warp - QC_EPI_WARP0) >> 2) * G;
     const int row = quarter * 32 + lane;
     const int64_t hpwp = (int64_t)p.hp * p.wp;
+    const uint32_t yx4 = (uint32_t)p.y_xor * 0x01010101u;
     pdl_wait();  // residual reads and output writes follow the preceding kernel
     int it = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++it) {
+    for (int tile = t_begin; tile < t_end; ++tile, ++it) {
       __syncwarp();
       const int acc = it & 1;
       bool ok = mbar_wait(&accf[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      uint32_t v[HALF];
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * OC + col0);
+      uint32_t pv[P][G];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * P * OC + col0);
 #pragma unroll
-      for (int c = 0; c < HALF / 16; ++c)
-        tmem_ld16(taddr + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[c * 16]));
+      for (int pp = 0; pp < P; ++pp) {
+        if constexpr (G == 8) {
+          tmem_ld8(taddr + pp * OC, pv[pp]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < G / 16; ++c)
+            tmem_ld16(taddr + pp * OC + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&pv[pp][c * 16]));
+        }
+      }
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&acce[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[acc]);
+      uint32_t v[G];
+#pragma unroll
+      for (int c = 0; c < G; ++c) {
+        int32_t s = (int32_t)pv[0][c];
+#pragma unroll
+        for (int pp = 1; pp < P; ++pp)
+          if (pp < PE) s += (int32_t)pv[pp][c];
+        v[c] = (uint32_t)s;
+      }
 
-      const int64_t q = (int64_t)tile * QC_TILE_M + row;
-      const int n = (int)(q / hpwp);
-      const int rem = (int)(q - (int64_t)n * hpwp);
-      const int oh = rem / p.wp;
+      // pixel of pitched row q: divisions by Hp*Wp and Wp as multiply-shift
+      // with host-computed ceil(2^40 / d) (exact for q * d < 2^40, checked on the host)
+      const uint32_t q = (uint32_t)tile * QC_TILE_M + (uint32_t)row;
+      const int n = (int)(((uint64_t)q * p.hpwp_mul) >> 40);
+      const int rem = (int)(q - (uint32_t)n * (uint32_t)hpwp);
+      const int oh = (int)(((uint64_t)(uint32_t)rem * p.wp_mul) >> 40);
       const int ow = rem - oh * p.wp;
       if (n >= p.batch || oh >= p.oh || ow >= p.ow) continue;
 
-      uint32_t out[HALF / 4];
+      float r[G];
 #pragma unroll
-      for (int j = 0; j < HALF / 4; ++j) out[j] = 0;
-      if (!p.has_add) {
-#pragma unroll
-        for (int c = 0; c < HALF; ++c) {
-          const float r = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero, p.y_lo,
-                                       p.y_hi);
-          out[c >> 2] |= (float_to_byte(r) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
-        }
-      } else {
-        const int64_t rpix = ((int64_t)n * p.r_hp + oh + p.r_pt) * p.r_wp + ow + p.r_pl;
-        uint32_t rb[HALF / 4];
-#pragma unroll
-        for (int c = 0; c < HALF / 16; ++c) {
-          const uint4 t =
-              *reinterpret_cast<const uint4*>(p.resid + (uint64_t)(col0 / 16 + c) * p.r_pitch + (uint64_t)rpix * 16);
-          rb[4 * c + 0] = t.x;
-          rb[4 * c + 1] = t.y;
-          rb[4 * c + 2] = t.z;
-          rb[4 * c + 3] = t.w;
-        }
+      for (int c4 = 0; c4 < G / 4; ++c4) {
+        const float4 sc = *reinterpret_cast<const float4*>(&s_scale[col0 + 4 * c4]);
+        const int4 bi = *reinterpret_cast<const int4*>(&s_bias[col0 + 4 * c4]);
+        r[4 * c4 + 0] = requant_fast((int32_t)v[4 * c4 + 0] + bi.x, sc.x, p.y_m_minus_zero, p.y_lo, p.y_hi);
+        r[4 * c4 + 1] = requant_fast((int32_t)v[4 * c4 + 1] + bi.y, sc.y, p.y_m_minus_zero, p.y_lo, p.y_hi);
+        r[4 * c4 + 2] = requant_fast((int32_t)v[4 * c4 + 2] + bi.z, sc.z, p.y_m_minus_zero, p.y_lo, p.y_hi);
+        r[4 * c4 + 3] = requant_fast((int32_t)v[4 * c4 + 3] + bi.w, sc.w, p.y_m_minus_zero, p.y_lo, p.y_hi);
+      }
+      if (p.has_add) {
+        uint32_t rb[G / 4];
+        qc_load_resid<OC, G>(p, rb, col0, n, oh, ow);
         if (p.fast_div) {
 #pragma unroll
-          for (int c = 0; c < HALF; ++c) {
-            const float cv = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero,
-                                          p.y_lo, p.y_hi);
-            const int r = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
-            const float a = qadd_fast<true>(cv, p.c_zero, p.c_scale, r, p.r_zero, p.r_scale, p.add_scale,
-                                            p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
-            out[c >> 2] |= (float_to_byte(a) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
+          for (int c = 0; c < G; ++c) {
+            const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
+            r[c] = qadd_fast<true>(r[c], p.c_zero, p.c_scale, rv, p.r_zero, p.r_scale, p.add_scale, p.add_inv_scale,
+                                   p.add_zero, p.add_lo, p.add_hi);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < HALF; ++c) {
-            const float cv = requant_fast((int32_t)v[c] + s_bias[col0 + c], s_scale[col0 + c], p.y_m_minus_zero,
-                                          p.y_lo, p.y_hi);
-            const int r = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
-            const float a = qadd_fast<false>(cv, p.c_zero, p.c_scale, r, p.r_zero, p.r_scale, p.add_scale,
-                                             p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
-            out[c >> 2] |= (float_to_byte(a) ^ (uint32_t)p.y_xor) << (8 * (c & 3));
+          for (int c = 0; c < G; ++c) {
+            const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
+            r[c] = qadd_fast<false>(r[c], p.c_zero, p.c_scale, rv, p.r_zero, p.r_scale, p.add_scale,
+                                    p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
           }
         }
       }
-      qc_epilogue_store<OC, HALF>(p, out, col0, n, oh, ow, q);
+      uint32_t out[G / 4];
+#pragma unroll
+      for (int c4 = 0; c4 < G / 4; ++c4)
+        out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
+      qc_store<OC, G>(p, out, col0, n, oh, ow);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
@@ -342,9 +397,9 @@ __global__ void qadd_fastdiv_check_kernel(QConvTcParams p, int* mismatch) {
 struct QConvTcState {
   int variant;
   int stages;
-  int rows_box;
+  int win_rows;
   int fast_div;
-  uint32_t stage_bytes, plane_bytes, b_bytes;
+  uint32_t stage_bytes, win_bytes, b_bytes;
   size_t smem_bytes;
 };
 static_assert(sizeof(QConvTcState) <= sizeof(OpState), "state fits");
@@ -366,7 +421,7 @@ static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_byte
   s += align_up(b_bytes, 1024);
   s += (size_t)stages * stage_bytes;
   s += (size_t)oc * 8;
-  s += (size_t)(2 * stages + 6) * 8 + 16;
+  s += (size_t)(2 * stages + 5 + QC_MMA_WARPS) * 8 + 16;
   return s;
 }
 
@@ -380,9 +435,6 @@ static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, c
   p.resid = op.t[3] >= 0 ? (const uint8_t*)ptrs[op.t[3]] : nullptr;
   p.y = (uint8_t*)ptrs[op.t[4]];
   p.x_rows = op.ip[QC_X_ROWS];
-  p.x_pitch = (uint64_t)op.ip[QC_X_ROWS] * 16u;
-  p.y_pitch = (uint64_t)op.ip[QC_Y_ROWS] * 16u;
-  p.r_pitch = (uint64_t)op.ip[QC_R_ROWS] * 16u;
   p.batch = (int)batch;
   p.kh = (int)op.ip[QC_KH];
   p.kw = (int)op.ip[QC_KW];
@@ -390,14 +442,17 @@ static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, c
   p.wp = (int)op.ip[QC_WP];
   p.oh = (int)op.ip[QC_OH];
   p.ow = (int)op.ip[QC_OW];
-  p.rows_box = st->rows_box;
+  p.win_rows = st->win_rows;
   p.stages = st->stages;
+  const uint64_t hpwp = (uint64_t)p.hp * (uint64_t)p.wp;
+  p.hpwp_mul = ((1ull << 40) + hpwp - 1) / hpwp;
+  p.wp_mul = ((1ull << 40) + (uint64_t)p.wp - 1) / (uint64_t)p.wp;
   const int64_t q_end = (batch - 1) * p.hp * p.wp + (int64_t)(p.oh - 1) * p.wp + p.ow;  // one past last valid
   p.n_tiles = batch > 0 ? (int)((q_end + QC_TILE_M - 1) / QC_TILE_M) : 0;
   p.idesc = make_idesc(2u, op.ip[QC_A_SIGNED] ? 1u : 0u, 1u, 128u, (uint32_t)oc);
   p.b_bytes = st->b_bytes;
   p.stage_bytes = st->stage_bytes;
-  p.plane_bytes = st->plane_bytes;
+  p.win_bytes = st->win_bytes;
   const bool ys = op.ip[QC_Y_SIGNED] != 0;
   p.y_lo = ys ? -128.0f : 0.0f;
   p.y_hi = ys ? 127.0f : 255.0f;
@@ -436,18 +491,24 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
     if (kQcVariants[i].cin == cin && kQcVariants[i].oc == oc) st->variant = i;
   if (st->variant < 0) return fail(msg, n, 5, "QLinearConv tensor-core path: no variant for C=%d OC=%d", cin, oc);
   const int kw = (int)op.ip[QC_KW], kh = (int)op.ip[QC_KH];
-  st->rows_box = (int)align_up((size_t)(QC_TILE_M + kw - 1), 8);
-  st->plane_bytes = (uint32_t)st->rows_box * 16u;
-  st->stage_bytes = st->plane_bytes * (uint32_t)(cin / 16);
+  const int64_t wp = op.ip[QC_WP];
+  st->win_rows = (int)align_up((size_t)(QC_TILE_M + (kh - 1) * wp + kw - 1), 8);
+  st->win_bytes = (uint32_t)st->win_rows * (uint32_t)cin;
+  st->stage_bytes = (uint32_t)align_up(st->win_bytes, 1024);  // stages keep the 1024-byte swizzle alignment
   st->b_bytes = (uint32_t)(kh * kw * cin * oc);
+  // pitched-row arithmetic: 32-bit rows and exact multiply-shift division (q * Hp*Wp < 2^40)
+  const int64_t hpwp = op.ip[QC_HP] * wp;
+  const int64_t q_max = op.ip[QC_N] * hpwp + QC_TILE_M;
+  if (q_max >= (1ll << 31) || (double)q_max * (double)hpwp >= (double)(1ull << 40))
+    return fail(msg, n, 5, "QLinearConv tensor-core path: %lld pitched rows too many for one launch",
+                (long long)q_max);
   // every window the kernel can request must stay inside the input planes
-  const int64_t rows_needed =
-      op.ip[QC_N] * op.ip[QC_HP] * op.ip[QC_WP] + (int64_t)(kh - 1) * op.ip[QC_WP] + st->rows_box;
+  const int64_t rows_needed = op.ip[QC_N] * op.ip[QC_HP] * wp + st->win_rows;
   if (op.ip[QC_X_ROWS] < rows_needed)
     return fail(msg, n, 2, "input planes have %lld rows, windows need %lld", (long long)op.ip[QC_X_ROWS],
                 (long long)rows_needed);
-  const size_t budget = 200 * 1024;
-  int stages = 9;
+  const size_t budget = 210 * 1024;
+  int stages = 8;
   while (stages > 2 && qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc) > budget) --stages;
   st->stages = stages;
   st->smem_bytes = qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc);
@@ -487,20 +548,30 @@ int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, con
 }
 
 // ------------------------------------------------------------------ NCHW -> chunk-planar zero-bordered
-// One block per (image, input row): the row's C x W bytes are staged in shared
-// memory, then written as 16-byte chunks, one per (plane, pixel); consecutive
-// threads write consecutive pixels of one plane (coalesced 16-byte stores).
+// One block per (image, input row).  Phase 1 reads the row's C channel rows of
+// W bytes with 4-byte loads into shared memory [C][W+4]; phase 2 writes one
+// 16-byte chunk per (chunk, pixel) at its swizzled position in the pixel's
+// C-byte row.
 __global__ void pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int c, int h, int w,
-                                  int pt, int pl, int hp, int wp, uint64_t plane_pitch, uint32_t xr) {
-  extern __shared__ uint8_t s[];  // [c][w + 4]
+                                  int pt, int pl, int hp, int wp, uint32_t xr) {
+  extern __shared__ __align__(16) uint8_t s[];  // [c][ws]
   const int row = blockIdx.x, n = blockIdx.y;
+  const int ws = w + 4;
   pdl_wait();
   pdl_launch_dependents();
-  const int ws = w + 4;
   const uint8_t* src = x + ((size_t)n * c * h + row) * w;
-  for (int i = threadIdx.x; i < c * w; i += blockDim.x) {
-    const int ch = i / w, col = i - ch * w;
-    s[ch * ws + col] = src[(size_t)ch * h * w + col];
+  if ((w & 3) == 0) {
+    const int w4 = w >> 2;
+    for (int i = threadIdx.x; i < c * w4; i += blockDim.x) {
+      const int ch = i / w4, c4 = i - ch * w4;
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(src + (size_t)ch * h * w + 4 * c4);
+      *reinterpret_cast<uint32_t*>(&s[ch * ws + 4 * c4]) = v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < c * w; i += blockDim.x) {
+      const int ch = i / w, col = i - ch * w;
+      s[ch * ws + col] = src[(size_t)ch * h * w + col];
+    }
   }
   __syncthreads();
   const int planes = c / 16;
@@ -512,23 +583,22 @@ __global__ void pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __rest
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int cb = 16 * j + 4 * q;
-      wd[q] = ((uint32_t)s[(cb + 0) * ws + col] | ((uint32_t)s[(cb + 1) * ws + col] << 8) |
-               ((uint32_t)s[(cb + 2) * ws + col] << 16) | ((uint32_t)s[(cb + 3) * ws + col] << 24)) ^ x4;
+      wd[q] = __byte_perm(__byte_perm(s[(cb + 0) * ws + col], s[(cb + 1) * ws + col], 0x0040),
+                          __byte_perm(s[(cb + 2) * ws + col], s[(cb + 3) * ws + col], 0x0040), 0x5410) ^ x4;
     }
-    *reinterpret_cast<uint4*>(y + (uint64_t)j * plane_pitch + (uint64_t)(row0 + col) * 16) =
-        make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    const int64_t g = row0 + col;
+    *reinterpret_cast<uint4*>(y + (uint64_t)g * c + 16 * swz_chunk(g, j, c)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
 }
 
 int launch_pad_nhwc(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int c = (int)op.ip[PAD_C], h = (int)op.ip[PAD_H], w = (int)op.ip[PAD_W];
   const size_t smem = (size_t)c * (w + 4);
-  if (smem > 48 * 1024 || c % 16) return 5;
+  if (smem > 48 * 1024 || (c != 32 && c != 64 && c != 128)) return 5;
   dim3 grid((unsigned)h, (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));
   cudaError_t e = launch_pdl(pad_planar_kernel, grid, dim3(256), smem, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
                              (uint8_t*)ptrs[op.t[1]], c, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
-                             (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint64_t)op.ip[PAD_ROWS] * 16u,
-                             (uint32_t)op.ip[PAD_XOR]);
+                             (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint32_t)op.ip[PAD_XOR]);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }

@@ -8,7 +8,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/emx_b200.h"
+#include "emx_b200.h"
 #include "host_util.h"
 #include "kernels.h"
 

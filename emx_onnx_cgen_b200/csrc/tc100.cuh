@@ -179,6 +179,34 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr, uint32_t s
   return d;
 }
 
+// Shared-memory matrix descriptor for a K-major operand stored with the
+// swizzle whose atom row equals the operand's row pitch: 32, 64 or 128 bytes
+// per row (SWIZZLE_32B / 64B / 128B), 8-row atoms SBO = 8 * row_bytes apart,
+// LBO = 16 bytes (the two 16-byte halves of one K = 32-byte step).  16-byte
+// chunk j of row r sits at chunk position j ^ (((r * row_bytes) >> 7) &
+// (row_bytes / 16 - 1)) counted from a 1024-byte aligned base.  The start may
+// sit anywhere on a 16-byte boundary (a row offset for a conv tap, +32 bytes
+// for the next K step): the tensor cores apply the swizzle to the absolute
+// shared-memory address bits, so the base-offset field stays 0 (checked on
+// B200: a start shifted by a non-multiple of 8 rows reads the right chunks with
+// base offset 0 and the wrong ones with base offset (start >> 7) & 7).
+__device__ __forceinline__ uint64_t smem_desc_k_swizzled(uint32_t saddr, uint32_t row_bytes) {
+  const uint64_t layout = row_bytes == 128 ? 2u : (row_bytes == 64 ? 4u : 6u);
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;                                    // LBO: 16 bytes
+  d |= (uint64_t)(((8u * row_bytes) >> 4) & 0x3FFFu) << 32;  // SBO: one 8-row atom
+  d |= (uint64_t)1u << 46;                                    // descriptor version for tcgen05
+  d |= layout << 61;
+  return d;
+}
+
+// Chunk position of 16-byte chunk j in row `row` of a swizzled K-major array
+// with `row_bytes` per row (the data layout smem_desc_k_swizzled reads).
+__host__ __device__ __forceinline__ int swz_chunk(int64_t row, int j, int row_bytes) {
+  return j ^ (int)(((row * row_bytes) >> 7) & (row_bytes / 16 - 1));
+}
+
 // Instruction descriptor (kind::f16 / kind::tf32 / kind::i8), dense, K-major A and B.
 //   c_fmt: 0 F16, 1 F32, 2 S32;  a_fmt/b_fmt: f16 kinds 0 F16 1 BF16 2 TF32, i8 kinds 0 U8 1 S8
 __host__ __device__ __forceinline__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt,
@@ -214,6 +242,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// 32 TMEM lanes x 32 bits, 8 consecutive columns -> 8 registers per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

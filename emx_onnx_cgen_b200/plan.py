@@ -163,6 +163,27 @@ class _Builder:
         return bytes(out)
 
 
+def swizzle_positions(rows: int, row_bytes: int) -> np.ndarray:
+    """[rows, row_bytes // 16]: position of 16-byte chunk j of row r in the
+    tensor-core K-major swizzle of a row_bytes-wide row (same rule as
+    swz_chunk in csrc/tc100.cuh)."""
+    nchunk = row_bytes // 16
+    phase = ((np.arange(rows, dtype=np.int64) * row_bytes) >> 7) & (nchunk - 1)
+    return np.arange(nchunk)[None, :] ^ phase[:, None]
+
+
+def qconv_weight_image(w: np.ndarray) -> np.ndarray:
+    """OIHW int8 weights -> the tensor-core operand image [tap][oc][cin]
+    (tap = kh*KW + kw), each oc row of cin bytes with its 16-byte chunks in
+    swizzled positions."""
+    oc, cin, kh, kw = w.shape
+    base = np.ascontiguousarray(w.transpose(2, 3, 0, 1)).reshape(kh * kw, oc, cin // 16, 16)
+    pos = swizzle_positions(oc, cin)
+    img = np.empty_like(base)
+    img[:, np.arange(oc)[:, None], pos, :] = base
+    return np.ascontiguousarray(img.reshape(kh * kw, oc, cin))
+
+
 @dataclass
 class _Padded:
     tid: int
@@ -447,7 +468,7 @@ class B200PlanEmitter:
         n, c, h, w = self._shape(name)
         hp, wp = h + pt + pb, w + pl + pr
         rows = n * hp * wp + 9 * wp + 264
-        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (c // 16, rows, 16), name=name + ":planar")
+        tid = self._b.arena_tensor(T_TEMP, self._dtype(name), (rows, c), name=name + ":swizzled-nhwc")
         pd = _Padded(tid, hp, wp, pt, pl, self._need_xor[name], rows)
         self._padded[name] = pd
         return pd
@@ -502,9 +523,7 @@ class B200PlanEmitter:
         bias = (self._const(op.bias, "bias").astype(np.int32) if op.bias is not None
                 else np.zeros(oc, np.int32))
         epi = np.concatenate([scale.view(np.uint8), bias.view(np.uint8)])
-        # weight image: [tap][chunk of 16 in-channels][oc][16 bytes]
-        img = w.transpose(2, 3, 1, 0).reshape(kh * kw, cin // 16, 16, oc).transpose(0, 1, 3, 2)
-        t_w = self._b.weight(np.ascontiguousarray(img), "i8", op.weights + ":tc")
+        t_w = self._b.weight(qconv_weight_image(w), "i8", op.weights + ":tc")
         t_e = self._b.weight(epi, "u8", op.weights + ":epi")
         xin = self._padded_of(op.input0)
         n, _, h, wd = self._shape(op.input0)

@@ -51,14 +51,17 @@ def test_unsupported_op_raises():
 
 
 def test_weight_image_layout():
-    """Tensor-core weight image: [tap][16-channel chunk][oc][16 bytes]."""
-    wl = W.qconv_stack_int8(batch=1, channels=32, height=4, width=4, n_convs=1)
-    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
-    conv = next(o for o in plan.ops if o.kernel == K.K_QCONV_TC)
-    t = plan.tensors[conv.tensors[1]]
-    img = np.frombuffer(plan.weight_bytes[t.offset:t.offset + t.nbytes], np.int8).reshape(9, 2, 32, 16)
-    w = wl.graph.initializers["w0"]
-    for tap in (0, 4, 8):
-        kh, kw = divmod(tap, 3)
-        for chunk in range(2):
-            assert np.array_equal(img[tap, chunk], w[:, chunk * 16:(chunk + 1) * 16, kh, kw])
+    """Tensor-core weight image: [tap][oc][cin] with each row's 16-byte chunks
+    at their swizzled positions (chunk j of row r at j ^ ((r*cin >> 7) & (cin/16-1)))."""
+    from emx_onnx_cgen_b200.plan import qconv_weight_image
+    for cin in (32, 64, 128):
+        w = np.random.default_rng(cin).integers(-127, 128, (64, cin, 3, 3)).astype(np.int8)
+        img = qconv_weight_image(w)
+        assert img.shape == (9, 64, cin)
+        for tap in (0, 4, 8):
+            kh, kw = divmod(tap, 3)
+            for oc in (0, 1, 2, 5, 63):
+                phase = ((oc * cin) >> 7) & (cin // 16 - 1)
+                for j in range(cin // 16):
+                    pos = j ^ phase
+                    assert np.array_equal(img[tap, oc, 16 * pos:16 * pos + 16], w[oc, 16 * j:16 * j + 16, kh, kw])
