@@ -270,12 +270,13 @@ def ours_arm(args) -> None:
         sess.sync()
         return sum(a.elapsed_time(b) for a, b in ev) / steps
 
+    from emx_onnx_cgen_b200.distributed import check_same_plan, max_over_ranks as _max_over_ranks
+
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(v, device="cuda")
+
+    if not check_same_plan(plan.plan_bytes, plan.weight_bytes, device="cuda"):
+        raise SystemExit("ranks emitted different plans")
 
     with ClockSampler(local) as clk:
         # warm-up: at least W steps and at least ~1 s of back-to-back work so the

@@ -547,57 +547,60 @@ int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, con
   return e == cudaSuccess ? 0 : 4;
 }
 
-// ------------------------------------------------------------------ NCHW -> chunk-planar zero-bordered
-// One block per (image, input row).  Phase 1 reads the row's C channel rows of
-// W bytes with 4-byte loads into shared memory [C][W+4]; phase 2 writes one
-// 16-byte chunk per (chunk, pixel) at its swizzled position in the pixel's
-// C-byte row.
-__global__ void pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int c, int h, int w,
-                                  int pt, int pl, int hp, int wp, uint32_t xr) {
-  extern __shared__ __align__(16) uint8_t s[];  // [c][ws]
-  const int row = blockIdx.x, n = blockIdx.y;
-  const int ws = w + 4;
+// ------------------------------------------------------------------ NCHW -> swizzled NHWC, zero-bordered
+// One block per (image, PAD_ROWS_PER_BLOCK input rows).  Phase 1: each warp
+// copies whole channel rows (4-byte words when W % 4 == 0) into shared memory
+// [rows][C][W+4]; phase 2: thread per (pixel, 4-channel word) packs the word
+// and stores it at its swizzled position in the pixel's C-byte row (a warp
+// writes whole pixels: contiguous 128-byte runs).  No runtime divisions.
+constexpr int PAD_ROWS_PER_BLOCK = 2;
+
+template <int C>
+__global__ void __launch_bounds__(256) pad_planar_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                                         int h, int w, int pt, int pl, int hp, int wp, uint32_t xr) {
+  extern __shared__ __align__(16) uint8_t s[];  // [PAD_ROWS_PER_BLOCK][C][ws]
+  constexpr int WPP = C / 4;                    // 4-byte words per pixel
+  const int row_base = blockIdx.x * PAD_ROWS_PER_BLOCK, n = blockIdx.y;
+  const int ws = (w + 4) & ~3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
-  const uint8_t* src = x + ((size_t)n * c * h + row) * w;
-  if ((w & 3) == 0) {
-    const int w4 = w >> 2;
-    for (int i = threadIdx.x; i < c * w4; i += blockDim.x) {
-      const int ch = i / w4, c4 = i - ch * w4;
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(src + (size_t)ch * h * w + 4 * c4);
-      *reinterpret_cast<uint32_t*>(&s[ch * ws + 4 * c4]) = v;
-    }
-  } else {
-    for (int i = threadIdx.x; i < c * w; i += blockDim.x) {
-      const int ch = i / w, col = i - ch * w;
-      s[ch * ws + col] = src[(size_t)ch * h * w + col];
+  const int rows = min(PAD_ROWS_PER_BLOCK, h - row_base);
+  // asynchronous global -> shared copies (no register round trip), all in flight at once
+  for (int t = warp; t < rows * C; t += 8) {  // one channel row per warp iteration
+    const int r = t / C, ch = t - r * C;      // C is a compile-time power of two
+    const uint8_t* src = x + (((size_t)n * C + ch) * h + row_base + r) * w;
+    uint8_t* dst = s + (r * C + ch) * ws;
+    if ((w & 3) == 0) {
+      for (int k = lane; k < (w >> 2); k += 32)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + 4 * k)), "l"(src + 4 * k)
+                     : "memory");
+    } else {
+      for (int k = lane; k < w; k += 32) dst[k] = src[k];
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  const int planes = c / 16;
-  const int64_t row0 = ((int64_t)n * hp + row + pt) * wp + pl;
   const uint32_t x4 = xr * 0x01010101u;
-  for (int i = threadIdx.x; i < planes * w; i += blockDim.x) {
-    const int j = i / w, col = i - j * w;
-    uint32_t wd[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int cb = 16 * j + 4 * q;
-      wd[q] = __byte_perm(__byte_perm(s[(cb + 0) * ws + col], s[(cb + 1) * ws + col], 0x0040),
-                          __byte_perm(s[(cb + 2) * ws + col], s[(cb + 3) * ws + col], 0x0040), 0x5410) ^ x4;
-    }
-    const int64_t g = row0 + col;
-    *reinterpret_cast<uint4*>(y + (uint64_t)g * c + 16 * swz_chunk(g, j, c)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  for (int i = threadIdx.x; i < rows * w * WPP; i += 256) {
+    const int g4 = i % WPP, pix = i / WPP;  // compile-time power-of-two divisor
+    const int r = pix / w, col = pix - r * w;
+    const uint8_t* sc = s + (r * C + 4 * g4) * ws + col;
+    const uint32_t word =
+        __byte_perm(__byte_perm(sc[0], sc[ws], 0x0040), __byte_perm(sc[2 * ws], sc[3 * ws], 0x0040), 0x5410) ^ x4;
+    const int64_t g = ((int64_t)n * hp + row_base + r + pt) * wp + pl + col;
+    *reinterpret_cast<uint32_t*>(y + (uint64_t)g * C + 16 * swz_chunk(g, g4 >> 2, C) + 4 * (g4 & 3)) = word;
   }
 }
 
 int launch_pad_nhwc(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int c = (int)op.ip[PAD_C], h = (int)op.ip[PAD_H], w = (int)op.ip[PAD_W];
-  const size_t smem = (size_t)c * (w + 4);
+  const size_t smem = (size_t)PAD_ROWS_PER_BLOCK * c * ((w + 4) & ~3);
   if (smem > 48 * 1024 || (c != 32 && c != 64 && c != 128)) return 5;
-  dim3 grid((unsigned)h, (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));
-  cudaError_t e = launch_pdl(pad_planar_kernel, grid, dim3(256), smem, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
-                             (uint8_t*)ptrs[op.t[1]], c, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
+  dim3 grid((unsigned)((h + PAD_ROWS_PER_BLOCK - 1) / PAD_ROWS_PER_BLOCK), (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));
+  auto kern = c == 32 ? pad_planar_kernel<32> : (c == 64 ? pad_planar_kernel<64> : pad_planar_kernel<128>);
+  cudaError_t e = launch_pdl(kern, grid, dim3(256), smem, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
+                             (uint8_t*)ptrs[op.t[1]], h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
                              (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint32_t)op.ip[PAD_XOR]);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
