@@ -1,7 +1,7 @@
 """Multi-GPU plumbing: one process per GPU, independent inferences per rank.
 
 The lowered-op path has no cross-inference reduction, so N GPUs run N full
-weight replicas on disjoint work (SURVEY.md-style "replicas"): either whole
+weight replicas on disjoint work ("replicas only"): either whole
 inferences per rank (weak scaling, what the benchmark does) or contiguous
 batch rows of one inference per rank through ``emx_b200_run``'s
 ``batch_begin/batch_count`` (strong scaling).  No collective touches the data
