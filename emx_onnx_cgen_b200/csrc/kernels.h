@@ -18,12 +18,11 @@ enum KernelId : uint32_t {
   K_QLINEAR_ADD = 4,    // com.microsoft QLinearAdd, same-shape operands
   K_GEMM_F32 = 5,       // Gemm fp32, reference accumulation order (+bias, +Relu)
   K_RELU_F32 = 6,
-  K_NBITS_GEMM = 7,     // MatMulNBits int4 -> fp16 on tcgen05 kind::f16 (+fused epilogues)
+  K_NBITS_GEMM = 7,     // MatMulNBits int4 x fp16 on tcgen05 kind::f16 (+ fused Swish*Mul of a gate/up pair)
   K_SWISH_F16 = 8,
   K_MUL_F16 = 9,
   K_ATTENTION_F16 = 10, // opset-23 Attention, flash tiling on tcgen05
   K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order
-  K_NBITS_DEQUANT = 12, // int4 blocks -> fp16 weight matrix (prologue of K_NBITS_GEMM)
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -58,6 +57,14 @@ enum { QAF_A_SCALE, QAF_B_SCALE, QAF_Y_SCALE };
 // ---- K_GEMM_F32: t[0]=A, t[1]=B, t[2]=bias|-1, t[3]=Y
 enum { GM_M, GM_N, GM_K, GM_TRANS_A, GM_TRANS_B, GM_BIAS_MODE, GM_RELU };
 enum { GMF_ALPHA, GMF_BETA };
+
+// ---- K_NBITS_GEMM: t[0]=A f16 [rows][a_pitch], t[1]=weight image (see nbits.cu),
+//      t[2]=bias f32 [n_tiles*128] | -1, t[3]=Y f16 [rows][y_pitch]
+enum {
+  NB_ROWS, NB_K, NB_N_OUT, NB_KSTEPS, NB_NTILES, NB_GROUPS, NB_FUSED, NB_A_PITCH, NB_Y_PITCH, NB_ROWS_PER_BATCH,
+  NB_ROUNDED_DEQUANT /*1: one MMA per K slice on fp16-rounded weights (default 0: exact hi + lo)*/
+};
+enum { NBF_ALPHA };
 
 // ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), last=y
 enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
@@ -119,5 +126,9 @@ int launch_qlinear_add(const PlanOp&, void* const*, const OpState*, const Launch
 int launch_gemm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 void launch_hold(const int* flag, int seq, int* err, cudaStream_t stream);
 int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_nbits(const PlanOp&, void* const*, OpState*, int, char*, size_t);
+int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

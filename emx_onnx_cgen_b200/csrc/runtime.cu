@@ -46,6 +46,9 @@ const KernelEntry kKernels[] = {
     {emx::K_QLINEAR_ADD, nullptr, emx::launch_qlinear_add, "qlinear_add"},
     {emx::K_GEMM_F32, nullptr, emx::launch_gemm_f32, "gemm_f32"},
     {emx::K_RELU_F32, nullptr, emx::launch_relu_f32, "relu_f32"},
+    {emx::K_NBITS_GEMM, emx::prepare_nbits, emx::launch_nbits, "nbits_gemm"},
+    {emx::K_SWISH_F16, nullptr, emx::launch_swish_f16, "swish_f16"},
+    {emx::K_MUL_F16, nullptr, emx::launch_mul_f16, "mul_f16"},
 };
 
 const KernelEntry* find_kernel(uint32_t id) {

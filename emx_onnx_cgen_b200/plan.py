@@ -184,6 +184,119 @@ def qconv_weight_image(w: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(img.reshape(kh * kw, oc, cin))
 
 
+NB_TILE_N, NB_KSTEP = 128, 64
+# nibble position p of a packed word holds the word's k offset _NB_PERM[p]:
+# (word >> 4i) & 0x000F000F then yields the pair (k = 2i, k = 2i + 1)
+_NB_PERM = np.array([0, 2, 4, 6, 1, 3, 5, 7])
+
+
+def unpack_nbits(b: np.ndarray, n: int, block: int) -> np.ndarray:
+    """MatMulNBits B [N][n_blocks][block/2] (4-bit, low nibble first, as
+    templates/matmul_nbits_op.c.j2 reads it) -> q [N][n_blocks * block]."""
+    nb = np.asarray(b, dtype=np.uint8).reshape(n, -1, block // 2)
+    return np.stack([nb & 15, nb >> 4], axis=-1).reshape(n, -1)
+
+
+def unpack_nbits_zero_points(zp, n: int, n_blocks: int) -> np.ndarray:
+    """MatMulNBits zero points -> [N][n_blocks] (lowering/matmul_nbits.py:171-185,
+    templates/matmul_nbits_op.c.j2): None -> 8; uint8 of rank >= 2 -> packed
+    4-bit per block (block b in byte b/2, low nibble first); rank 1 -> one per
+    column (its low nibble)."""
+    if zp is None:
+        return np.full((n, n_blocks), 8, np.uint8)
+    z = np.asarray(zp, dtype=np.uint8)
+    if z.ndim < 2:
+        return np.repeat((z.reshape(n, 1) & 15), n_blocks, axis=1)
+    z = z.reshape(n, -1)
+    return np.stack([z & 15, z >> 4], axis=-1).reshape(n, -1)[:, :n_blocks]
+
+
+def nbits_weight_image(parts, k: int, block: int, fused: bool):
+    """Weight image of the tcgen05 MatMulNBits kernel.
+
+    ``parts`` is [(q [N][Kq] uint8, zp [N][n_blocks] uint8, scales [N][n_blocks]
+    fp16, bias [N] f32 | None)] - one entry, or (gate, up) when ``fused``.
+    Tile rows: plain, 128 consecutive columns; fused, 64 gate columns then the
+    same 64 up columns.  Per (tile, K step of 64) one block of
+    4096 + 512 * G bytes: packed words [2][128][4] (see _NB_PERM) then
+    [128][G] words (scale fp16 | -(1024 + zp) fp16 << 16), G = 64 / SG scale
+    groups of SG = min(block, 32) columns.  Padding rows and columns dequantise
+    to exactly 0.  Returns (image bytes, bias f32 [n_tiles*128] | None,
+    n_tiles, k_steps, G)."""
+    n = parts[0][0].shape[0]
+    n_blocks = parts[0][1].shape[1]
+    sg = 32 if block >= 32 else 16
+    groups = NB_KSTEP // sg
+    k_steps = -(-k // NB_KSTEP)
+    kp = k_steps * NB_KSTEP
+    half = NB_TILE_N // 2 if fused else NB_TILE_N
+    n_tiles = -(-n // half)
+    rows = n_tiles * NB_TILE_N
+    # source (part, column) of every tile row; -1 = padding
+    src_col = np.full(rows, -1, np.int64)
+    src_part = np.zeros(rows, np.int64)
+    t = np.arange(rows)
+    tile, r = t // NB_TILE_N, t % NB_TILE_N
+    if fused:
+        col = tile * half + (r % half)
+        src_part = (r >= half).astype(np.int64)
+    else:
+        col = tile * half + r
+    src_col = np.where(col < n, col, -1)
+
+    q = np.full((rows, kp), 8, np.uint8)
+    gscale = np.zeros((rows, kp // sg), np.float16)
+    gzp = np.full((rows, kp // sg), 8, np.uint8)
+    gblk = np.minimum(np.arange(kp // sg) * sg // block, n_blocks - 1)
+    gvalid = np.arange(kp // sg) * sg < n_blocks * block
+    bias = np.zeros(rows, np.float32)
+    have_bias = False
+    for pi, (pq, pz, ps, pb) in enumerate(parts):
+        sel = (src_part == pi) & (src_col >= 0)
+        cols = src_col[sel]
+        kk = min(pq.shape[1], kp)
+        q[sel, :kk] = pq[cols, :kk]
+        gscale[sel] = np.where(gvalid[None, :], ps[cols][:, gblk], np.float16(0))
+        gzp[sel] = np.where(gvalid[None, :], pz[cols][:, gblk], 8)
+        if pb is not None:
+            have_bias = True
+            bias[sel] = np.asarray(pb, np.float32)[cols]
+    # padded K columns of real rows: q = zp, so the value is exactly 0 whatever the scale
+    if kp > n_blocks * block:
+        pad_zp = np.repeat(gzp, sg, axis=1)
+        q[:, n_blocks * block:] = pad_zp[:, n_blocks * block:]
+    words = np.zeros((rows, k_steps, 8), np.uint32)
+    qw = q.reshape(rows, k_steps, 8, 8).astype(np.uint32)
+    for p_, tk in enumerate(_NB_PERM):
+        words |= qw[..., tk] << np.uint32(4 * p_)
+    packed = words.reshape(n_tiles, NB_TILE_N, k_steps, 2, 4).transpose(0, 2, 3, 1, 4)
+    nbias = (-(1024.0 + gzp.astype(np.float32))).astype(np.float16)
+    sw = gscale.view(np.uint16).astype(np.uint32) | (nbias.view(np.uint16).astype(np.uint32) << np.uint32(16))
+    sw = sw.reshape(n_tiles, NB_TILE_N, k_steps, groups).transpose(0, 2, 1, 3)
+    img = np.concatenate([np.ascontiguousarray(packed).reshape(n_tiles, k_steps, -1).view(np.uint8),
+                          np.ascontiguousarray(sw).reshape(n_tiles, k_steps, -1).view(np.uint8)], axis=2)
+    return np.ascontiguousarray(img), (bias if have_bias else None), n_tiles, k_steps, groups
+
+
+def nbits_dequant_from_image(img: np.ndarray, n_tiles: int, k_steps: int, groups: int) -> np.ndarray:
+    """Decode a weight image the way the kernel's dequant warps do (fp16
+    arithmetic: (1024+q) + -(1024+zp), then x scale, each rounded to fp16) ->
+    [n_tiles*128][k_steps*64] fp16, tile row order.  Test helper."""
+    stage = img.reshape(n_tiles, k_steps, -1)
+    packed = stage[:, :, :4096].copy().view(np.uint32).reshape(n_tiles, k_steps, 2, NB_TILE_N, 4)
+    words = packed.transpose(0, 3, 1, 2, 4).reshape(n_tiles * NB_TILE_N, k_steps, 8)
+    sw = stage[:, :, 4096:].copy().view(np.uint32).reshape(n_tiles, k_steps, NB_TILE_N, groups)
+    sw = sw.transpose(0, 2, 1, 3).reshape(n_tiles * NB_TILE_N, k_steps, groups)
+    scale = (sw & 0xFFFF).astype(np.uint16).view(np.float16)
+    nb = (sw >> 16).astype(np.uint16).view(np.float16)
+    out = np.zeros((n_tiles * NB_TILE_N, k_steps, 8, 8), np.float16)
+    for p_, tk in enumerate(_NB_PERM):
+        qv = ((words >> np.uint32(4 * p_)) & 15).astype(np.float16) + np.float16(1024)
+        g = np.arange(8) * 8 * groups // NB_KSTEP  # chunk j -> its scale group
+        out[..., tk] = ((qv + nb[:, :, g]).astype(np.float16) * scale[:, :, g]).astype(np.float16)
+    return out.reshape(n_tiles * NB_TILE_N, k_steps * NB_KSTEP)
+
+
 @dataclass
 class _Padded:
     tid: int
@@ -198,8 +311,14 @@ class _Padded:
 class B200PlanEmitter:
     """Emit target producing a B200 launch plan from a LoweredModel."""
 
-    def __init__(self, *, use_tensor_cores: bool = True):
+    def __init__(self, *, use_tensor_cores: bool = True, nbits_rounded_dequant: bool = False):
+        """``nbits_rounded_dequant``: MatMulNBits multiplies fp16-rounded
+        dequantised weights (one MMA per K slice, about 2x the throughput)
+        instead of the exact hi + lo split; outputs then differ from the
+        reference by up to ~2^-12 of sum_k |a_k * deq_k| rather than by
+        summation order only."""
         self.use_tensor_cores = use_tensor_cores
+        self.nbits_rounded_dequant = nbits_rounded_dequant
 
     # ------------------------------------------------------------------ entry
     def emit_plan(self, model) -> Plan:
@@ -350,6 +469,40 @@ class B200PlanEmitter:
                 self._need_pad[name] = pads
                 self._need_xor[name] = cfg["xor"]
         self._absorbed = set(self._fused_add.values())
+        # gate/up MatMulNBits pair + Swish(gate) * up -> one kernel with a fused epilogue
+        self._nbits_fused: dict[int, dict] = {}
+        for mi, op in enumerate(ops):
+            if _name(op) != "BinaryOp" or _fn(op) != "MUL" or self._dtype(op.output) != "f16":
+                continue
+            for s_name, u_name in ((op.input0, op.input1), (op.input1, op.input0)):
+                i_s, i_u = producers.get(s_name), producers.get(u_name)
+                if i_s is None or i_u is None:
+                    continue
+                sw = ops[i_s]
+                if _name(sw) != "UnaryOp" or _fn(sw) != "SWISH":
+                    continue
+                i_g = producers.get(sw.input0)
+                if i_g is None or i_g == i_u:
+                    continue
+                g, u = ops[i_g], ops[i_u]
+                if _name(g) != "MatMulNBitsOp" or _name(u) != "MatMulNBitsOp":
+                    continue
+                if (g.input0 != u.input0 or int(g.k) != int(u.k) or int(g.n) != int(u.n)
+                        or int(g.block_size) != int(u.block_size)):
+                    continue
+                if self._nbits_reject(g) or self._nbits_reject(u):
+                    continue
+                inter = (g.output, u.output, s_name)
+                if any(nm in self._graph_outputs or len(consumers.get(nm, [])) != 1 for nm in inter):
+                    continue
+                first = min(i_g, i_u)
+                if first in self._nbits_fused or any(x in self._absorbed for x in (i_g, i_u, i_s, mi)):
+                    continue
+                # `const _Float16 alpha = <literal>;` in the reference's helper: fp16-rounded
+                alpha = float(np.float16(float(sw.params[0]) if getattr(sw, "params", ()) else 1.0))
+                self._nbits_fused[first] = {"gate": g, "up": u, "mul": op, "alpha": alpha}
+                self._absorbed.update({max(i_g, i_u), i_s, mi})
+                break
         for i, j in self._fused_add.items():
             add = ops[j]
             conv_out = ops[i].output
@@ -656,5 +809,90 @@ class B200PlanEmitter:
         ip = {K.EW_COUNT: count, K.EW_ROWS: rows}
         if fn == "RELU" and dt == "f32":
             self._b.op(K.K_RELU_F32, [x, y], ip, label=op.output, batched=rows > 0)
+        elif fn == "SWISH" and dt == "f16":
+            alpha = float(np.float16(float(op.params[0]) if getattr(op, "params", ()) else 1.0))
+            self._b.op(K.K_SWISH_F16, [x, y], ip, {K.EWF_ALPHA: alpha}, label=op.output, batched=rows > 0)
         else:
             raise UnsupportedOpError(f"Unary {fn} on {dt} has no B200 kernel")
+
+    def _emit_BinaryOp(self, i, op):
+        fn = _fn(op)
+        dt = self._dtype(op.output)
+        sa, sb = tuple(self._shape(op.input0)), tuple(self._shape(op.input1))
+        if fn != "MUL" or dt != "f16" or self._dtype(op.input0) != "f16" or self._dtype(op.input1) != "f16":
+            raise UnsupportedOpError(f"Binary {fn} on {dt} has no B200 kernel")
+        if sa != sb:
+            raise UnsupportedOpError("Mul: broadcasting operands have no B200 kernel")
+        a, b_ = self._src(op.input0), self._src(op.input1)
+        y = self._dest(op.output, dt, sa)
+        rows = (sa[0] if sa and sa[0] == self._batch and self._is_batched(op.input0)
+                and self._is_batched(op.input1) else 0)
+        self._b.op(K.K_MUL_F16, [a, b_, y], {K.EW_COUNT: int(np.prod(sa)), K.EW_ROWS: rows}, label=op.output,
+                   batched=rows > 0)
+
+    # ------------------------------------------------------------------ MatMulNBits
+    def _nbits_reject(self, op) -> str | None:
+        """Why this MatMulNBits has no tensor-core kernel (None: it has one)."""
+        if int(op.bits) != 4:
+            return f"{op.bits}-bit weights"
+        if self._dtype(op.input0) != "f16" or _suffix(op.output_dtype) != "f16":
+            return "only fp16 activations and outputs"
+        if int(op.accuracy_level) == 4:
+            return "accuracy_level 4 (int8 activation path)"
+        bs = int(op.block_size)
+        if bs < 16 or bs & (bs - 1):
+            return f"block_size {bs}"
+        if int(op.k) % 8 or int(op.n) % 8:
+            return "K and N must be multiples of 8 (16-byte row pitches)"
+        for what, name in (("B", op.input1), ("scales", op.scales), ("zero_points", op.zero_points),
+                           ("bias", op.bias)):
+            if name is not None and name not in self._consts:
+                return f"{what} must be an initializer"
+        if self._dtype(op.scales) != "f16":
+            return "only fp16 scales"
+        if op.zero_points is not None and self._dtype(op.zero_points) != "u8":
+            return "only packed uint8 zero points"
+        return None
+
+    def _nbits_part(self, op):
+        n, k, bs = int(op.n), int(op.k), int(op.block_size)
+        n_blocks = -(-k // bs)
+        q = unpack_nbits(self._consts[op.input1], n, bs)
+        zp = unpack_nbits_zero_points(self._consts[op.zero_points] if op.zero_points else None, n, n_blocks)
+        sc = np.asarray(self._consts[op.scales], np.float16).reshape(n, -1)
+        if sc.shape[1] == 1 and n_blocks > 1:
+            sc = np.repeat(sc, n_blocks, axis=1)
+        bias = np.asarray(self._consts[op.bias], np.float16).astype(np.float32).reshape(-1) if op.bias else None
+        return q, zp, sc, bias
+
+    def _nbits_emit(self, ops_, out_name, fused_alpha=None):
+        g = ops_[0]
+        k, n = int(g.k), int(g.n)
+        a_shape = tuple(self._shape(g.input0))
+        rows = int(np.prod(a_shape[:-1])) if len(a_shape) > 1 else 1
+        img, bias, n_tiles, k_steps, groups = nbits_weight_image(
+            [self._nbits_part(o) for o in ops_], k, int(g.block_size), fused_alpha is not None)
+        t_w = self._b.weight(img, "u8", g.input1 + ":tc")
+        t_b = self._b.weight(bias, "f32", g.output + ":bias") if bias is not None else -1
+        a = self._src(g.input0)
+        out_shape = a_shape[:-1] + (n,)
+        y = self._dest(out_name, "f16", out_shape)
+        batched = (len(a_shape) > 1 and a_shape[0] == self._batch and self._batch > 0
+                   and self._is_batched(g.input0))
+        ip = {K.NB_ROWS: rows, K.NB_K: k, K.NB_N_OUT: n, K.NB_KSTEPS: k_steps, K.NB_NTILES: n_tiles,
+              K.NB_GROUPS: groups, K.NB_FUSED: int(fused_alpha is not None), K.NB_A_PITCH: k, K.NB_Y_PITCH: n,
+              K.NB_ROWS_PER_BATCH: rows // self._batch if batched else 0,
+              K.NB_ROUNDED_DEQUANT: int(self.nbits_rounded_dequant)}
+        fp = {K.NBF_ALPHA: float(fused_alpha if fused_alpha is not None else 1.0)}
+        label = (f"{ops_[0].output}, {ops_[1].output} -> Swish * Mul -> {out_name} (tcgen05 f16, fused)"
+                 if fused_alpha is not None else f"{out_name} (tcgen05 f16)")
+        self._b.op(K.K_NBITS_GEMM, [a, t_w, t_b, y], ip, fp, label=label, batched=batched)
+
+    def _emit_MatMulNBitsOp(self, i, op):
+        if i in self._nbits_fused:
+            f = self._nbits_fused[i]
+            return self._nbits_emit([f["gate"], f["up"]], f["mul"].output, fused_alpha=f["alpha"])
+        why = self._nbits_reject(op)
+        if why:
+            raise UnsupportedOpError(f"MatMulNBits: {why}")
+        self._nbits_emit([op], op.output)

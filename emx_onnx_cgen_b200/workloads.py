@@ -153,7 +153,7 @@ def llama_mlp_int4(m: int = 2048, hidden: int = 4096, inter: int = 11008, block:
     rng = np.random.default_rng(weight_seed)
 
     def nbits(prefix: str, k: int, n: int) -> dict[str, np.ndarray]:
-        nb = k // block
+        nb = -(-k // block)  # n_blocks_per_col = ceil(K / block_size)
         return {
             f"{prefix}_B": rng.integers(0, 256, (n, nb, block // 2)).astype(np.uint8),
             f"{prefix}_s": rng.uniform(0.005, 0.02, (n, nb)).astype(np.float16),
@@ -239,10 +239,73 @@ def lstm_fp32(seq: int = 512, batch: int = 256, input_size: int = 512, hidden: i
                     dict(seq=seq, batch=batch, input_size=input_size, hidden=hidden))
 
 
+# --------------------------------------------------------------------------- single ops
+def matmul_nbits_f16(m: int = 64, k: int = 256, n: int = 192, block: int = 32, zero_points: str = "none",
+                     bias: bool = False, weight_seed: int = 1) -> Workload:
+    """One com.microsoft MatMulNBits (bits 4) on fp16 activations ~N(0,1).
+
+    zero_points: "none" (default zero point 8), "block" (uint8 [N][ceil(n_blocks/2)],
+    4-bit packed per block) or "column" (uint8 [N], one per column).  Optional
+    fp16 bias [N] ~U(-1, 1); scales fp16 [N][n_blocks] ~U(0.005, 0.02).
+    """
+    rng = np.random.default_rng(weight_seed)
+    nb = -(-k // block)
+    inits = {"B": rng.integers(0, 256, (n, nb, block // 2)).astype(np.uint8),
+             "scales": rng.uniform(0.005, 0.02, (n, nb)).astype(np.float16)}
+    ins = ["A", "B", "scales"]
+    if zero_points == "block":
+        inits["zp"] = rng.integers(0, 256, (n, (nb + 1) // 2)).astype(np.uint8)
+    elif zero_points == "column":
+        inits["zp"] = rng.integers(0, 16, (n,)).astype(np.uint8)
+    if zero_points != "none":
+        ins.append("zp")
+    if bias:
+        inits["bias"] = rng.uniform(-1.0, 1.0, (n,)).astype(np.float16)
+        ins += [""] * (5 - len(ins)) + ["bias"]
+    g = GraphSpec(
+        name="matmul_nbits_f16",
+        inputs=[TensorSpec("A", "f16", (m, k))],
+        outputs=[TensorSpec("Y", "f16", (m, n))],
+        nodes=[NodeSpec("MatMulNBits", "mm", tuple(ins), ("Y",),
+                        {"bits": 4, "block_size": block, "K": k, "N": n, "accuracy_level": 0}, "com.microsoft")],
+        initializers=inits,
+        opset_imports=(("", 21), ("com.microsoft", 1)),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"A": np.random.default_rng(seed).standard_normal((m, k)).astype(np.float16)}
+
+    return Workload("matmul_nbits_f16", g, make_inputs, {"A": 0, "Y": 0},
+                    dict(m=m, k=k, n=n, block=block, zero_points=zero_points, bias=bias))
+
+
+def swish_mul_f16(shape: tuple[int, ...] = (256, 512), alpha: float = 1.0) -> Workload:
+    """Swish(X, alpha) * Z on fp16 tensors (the unfused element-wise kernels)."""
+    g = GraphSpec(
+        name="swish_mul_f16",
+        inputs=[TensorSpec("X", "f16", tuple(shape)), TensorSpec("Z", "f16", tuple(shape))],
+        outputs=[TensorSpec("S", "f16", tuple(shape)), TensorSpec("P", "f16", tuple(shape))],
+        nodes=[NodeSpec("Swish", "silu", ("X",), ("S",), {"alpha": alpha}),
+               NodeSpec("Mul", "mul", ("S", "Z"), ("P",))],
+        initializers={},
+        opset_imports=(("", 24),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        r = np.random.default_rng(seed)
+        return {"X": (4 * r.standard_normal(shape)).astype(np.float16),
+                "Z": r.standard_normal(shape).astype(np.float16)}
+
+    return Workload("swish_mul_f16", g, make_inputs, {"X": 0, "Z": 0, "S": 0, "P": 0},
+                    dict(shape=tuple(shape), alpha=alpha))
+
+
 BUILDERS = {
     "mlp_fp32": mlp_fp32,
     "qconv_stack_int8": qconv_stack_int8,
     "llama_mlp_int4": llama_mlp_int4,
     "attention_fp16": attention_fp16,
     "lstm_fp32": lstm_fp32,
+    "matmul_nbits_f16": matmul_nbits_f16,
+    "swish_mul_f16": swish_mul_f16,
 }

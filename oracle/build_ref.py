@@ -33,7 +33,7 @@ from oracle import refc  # noqa: E402
 TARGETS = {
     "ref_qconv_b1": ("qconv_stack_int8", dict(batch=1), 1, 32),
     "ref_mlp_m64": ("mlp_fp32", dict(m=64), 64, 64),
-    "ref_nbits_m8": ("llama_mlp_int4", dict(m=8), 8, 2048),
+    "ref_nbits_m1": ("llama_mlp_int4", dict(m=1), 1, 2048),
     "ref_attn_b1h1": ("attention_fp16", dict(batch=1, heads=1), 1, 8 * 32),
     "ref_lstm_b1": ("lstm_fp32", dict(batch=1), 1, 256),
 }

@@ -162,15 +162,19 @@ void orc_relu_f32(const float *x, float *y, size_t count)
 /* ---------------------------------------------------------------------------
  * com.microsoft MatMulNBits, bits=4, accuracy_level 0, fp16 A, float accumulator.
  * templates/matmul_nbits_op.c.j2:1-58; B packed [N][n_blocks][block/2], low
- * nibble first; zero point 8 when no zero-point input (ir/ops/nn.py:1172).
- * zero_points (optional) are unpacked uint8 per (n, block).
+ * nibble first.  Zero points (ir/ops/nn.py:1172, lowering/matmul_nbits.py:
+ * 171-185): absent -> 8; uint8 of rank >= 2 -> packed 4-bit per block, block
+ * b in byte b/2 at shift (b*4)%8; rank 1 -> one per column (low nibble).
+ * Scales [N][n_blocks] (per block) or [N].  Bias [N] (fp16) is added to the
+ * float accumulator after the k loop; the result is cast to _Float16.
  * ------------------------------------------------------------------------- */
-void orc_matmul_nbits_f16(const f16 *a, const uint8_t *b, const f16 *scales,
-                          const uint8_t *zero_points, int m, int n, int k, int block,
-                          f16 *y)
+void orc_matmul_nbits_f16(const f16 *a, const uint8_t *b, const f16 *scales, int scales_per_block,
+                          const uint8_t *zero_points, int zp_per_block, const f16 *bias,
+                          int m, int n, int k, int block, f16 *y)
 {
     const int n_blocks = (k + block - 1) / block;
     const int blob = block / 2;
+    const int zp_cols = (n_blocks * 4 + 7) / 8;
     for (int i0 = 0; i0 < m; ++i0) {
         for (int i1 = 0; i1 < n; ++i1) {
             float acc = 0.0f;
@@ -180,10 +184,16 @@ void orc_matmul_nbits_f16(const f16 *a, const uint8_t *b, const f16 *scales,
                 const int byte_idx = k_in_block * 4 / 8;
                 const int bit_shift = (k_in_block * 4) % 8;
                 const int quant_val = ((int)(unsigned char)b[((size_t)i1 * n_blocks + block_idx) * blob + byte_idx] >> bit_shift) & 15;
-                const int zp = zero_points ? (int)zero_points[(size_t)i1 * n_blocks + block_idx] : 8;
-                const float dequant = ((float)quant_val - (float)zp) * (float)scales[(size_t)i1 * n_blocks + block_idx];
+                int zp = 8;
+                if (zero_points && zp_per_block)
+                    zp = ((int)zero_points[(size_t)i1 * zp_cols + block_idx * 4 / 8] >> ((block_idx * 4) % 8)) & 15;
+                else if (zero_points)
+                    zp = (int)zero_points[i1] & 15;
+                const float s = (float)scales[scales_per_block ? (size_t)i1 * n_blocks + block_idx : (size_t)i1];
+                const float dequant = ((float)quant_val - (float)zp) * s;
                 acc += (float)a[(size_t)i0 * k + kk] * dequant;
             }
+            if (bias) acc += (float)bias[i1];
             y[(size_t)i0 * n + i1] = (f16)acc;
         }
     }

@@ -116,22 +116,28 @@ def _binary(fn, a, b, dtype):
 def relu_f32(x): return _unary("orc_relu_f32", x, np.float32)
 def sigmoid_f32(x): return _unary("orc_sigmoid_f32", x, np.float32)
 def tanh_f32(x): return _unary("orc_tanh_f32", x, np.float32)
-def swish_f16(x, alpha=1.0): return _unary("orc_swish_f16", x, np.float16, _f(alpha))
+def swish_f16(x, alpha=1.0):
+    # the generated C declares `const _Float16 alpha = <double literal>;`
+    # (shared/scalar_functions.py:880-896): alpha is rounded once to fp16
+    return _unary("orc_swish_f16", x, np.float16, _f(float(np.float16(alpha))))
 def sigmoid_f16(x): return _unary("orc_sigmoid_f16", x, np.float16)
 def mul_f16(a, b): return _binary("orc_mul_f16", a, b, np.float16)
 def mul_f32(a, b): return _binary("orc_mul_f32", a, b, np.float32)
 def add_f32(a, b): return _binary("orc_add_f32", a, b, np.float32)
 
 
-def matmul_nbits_f16(a, b_packed, scales, k, n, block=32, zero_points=None):
+def matmul_nbits_f16(a, b_packed, scales, k, n, block=32, zero_points=None, bias=None):
     a = np.ascontiguousarray(a, np.float16)
     m = int(np.prod(a.shape[:-1]))
     y = np.zeros((*a.shape[:-1], n), np.float16)
     b_packed = np.ascontiguousarray(b_packed, np.uint8)
+    scales_pb = int(np.ndim(scales) >= 2)
     scales = np.ascontiguousarray(scales, np.float16)
+    zp_pb = int(zero_points is not None and np.ndim(zero_points) >= 2)
     zp = None if zero_points is None else np.ascontiguousarray(zero_points, np.uint8)
-    lib().orc_matmul_nbits_f16(_p(a), _p(b_packed), _p(scales), _p(zp), _i(m), _i(n), _i(k),
-                               _i(block), _p(y))
+    bias = None if bias is None else np.ascontiguousarray(bias, np.float16)
+    lib().orc_matmul_nbits_f16(_p(a), _p(b_packed), _p(scales), _i(scales_pb), _p(zp), _i(zp_pb), _p(bias),
+                               _i(m), _i(n), _i(k), _i(block), _p(y))
     return y
 
 
@@ -192,7 +198,8 @@ def run_graph(spec: GraphSpec, inputs: dict[str, np.ndarray]) -> dict[str, np.nd
         elif op == "MatMulNBits":
             res = [matmul_nbits_f16(ins[0], ins[1], ins[2], int(a["K"]), int(a["N"]),
                                     int(a.get("block_size", 32)),
-                                    ins[3] if len(ins) > 3 else None)]
+                                    ins[3] if len(ins) > 3 else None,
+                                    ins[5] if len(ins) > 5 else None)]
         elif op == "Swish":
             res = [swish_f16(ins[0], float(a.get("alpha", 1.0)))]
         elif op == "Sigmoid":

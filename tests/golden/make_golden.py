@@ -12,7 +12,7 @@ test time.
 Run from the repository root (needs the reference source tree, default
 ``/root/reference/src``, override with ``EMX_REFERENCE_SRC``)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [case ...]   # all cases, or only the named ones
 """
 from __future__ import annotations
 
@@ -50,6 +50,12 @@ CASES = [
     ("attn_b1_h1_t33_d64", "attention_fp16", dict(batch=1, heads=1, seq=33, head_dim=64), 2),
     ("lstm_t3_b2_i8_h16", "lstm_fp32", dict(seq=3, batch=2, input_size=8, hidden=16), 0),
     ("lstm_t5_b3_i16_h32", "lstm_fp32", dict(seq=5, batch=3, input_size=16, hidden=32), 1),
+    ("nbits1_m5_k96_n40_zpblock_bias", "matmul_nbits_f16",
+     dict(m=5, k=96, n=40, block=32, zero_points="block", bias=True), 0),
+    ("nbits1_m3_k64_n24_zpcol_b16", "matmul_nbits_f16", dict(m=3, k=64, n=24, block=16, zero_points="column"), 1),
+    ("nbits1_m2_k256_n16_b128", "matmul_nbits_f16", dict(m=2, k=256, n=16, block=128), 2),
+    ("swishmul_8x24", "swish_mul_f16", dict(shape=(8, 24)), 0),
+    ("swishmul_5x16_alpha1702", "swish_mul_f16", dict(shape=(5, 16), alpha=1.702), 1),
 ]
 
 
@@ -60,8 +66,13 @@ def main() -> None:
     libc = " ".join(platform.libc_ver())
     index = {"generator": "reference generated C, gcc -std=c99 -O2", "gcc": gcc, "libc": libc,
              "cases": {}}
+    only = set(sys.argv[1:])
+    if only and (HERE / "cases.json").exists():
+        index["cases"] = json.loads((HERE / "cases.json").read_text())["cases"]
     with tempfile.TemporaryDirectory() as tmp:
         for name, builder, kwargs, seed in CASES:
+            if only and name not in only:
+                continue
             wl = W.BUILDERS[builder](**kwargs)
             tag = "g_" + name
             refc.build(wl.graph, tag, Path(tmp))

@@ -34,3 +34,22 @@ def assert_bitexact(got: np.ndarray, ref: np.ndarray, what: str = ""):
         diff = np.argwhere(got != ref)
         raise AssertionError(f"{what}: {len(diff)} of {got.size} elements differ; first at {diff[:5].tolist()}: "
                              f"got {got[tuple(diff[0])]} expected {ref[tuple(diff[0])]}")
+
+
+def ulp_diff_f16(got: np.ndarray, ref: np.ndarray, atol_eps: float = 1.0) -> np.ndarray:
+    """Per-element ULP distance of fp16 arrays as the reference's verify
+    metric defines it (shared/ulp.py:26-50, verification.py:30-50): same sign
+    |bits(a) - bits(b)|, opposite signs ulp(0,|a|) + ulp(0,|b|) + 1, NaN/NaN 0,
+    NaN/number 0xFFFF; pairs with |a - b| <= atol_eps * eps(fp16) count 0."""
+    a = np.ascontiguousarray(got, np.float16).reshape(-1)
+    b = np.ascontiguousarray(ref, np.float16).reshape(-1)
+    ia = a.view(np.uint16).astype(np.int64)
+    ib = b.view(np.uint16).astype(np.int64)
+    mag_a, mag_b = ia & 0x7FFF, ib & 0x7FFF
+    same = (ia >> 15) == (ib >> 15)
+    d = np.where(same, np.abs(mag_a - mag_b), mag_a + mag_b + 1)
+    na, nb = np.isnan(a), np.isnan(b)
+    d = np.where(na & nb, 0, np.where(na | nb, 0xFFFF, d))
+    with np.errstate(invalid="ignore"):
+        close = np.abs(a.astype(np.float64) - b.astype(np.float64)) <= atol_eps * float(np.finfo(np.float16).eps)
+    return np.where(close & ~(na | nb), 0, d).reshape(np.shape(got))

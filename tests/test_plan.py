@@ -13,6 +13,11 @@ from oracle import refc
 SMALL = {
     "qconv": lambda: W.qconv_stack_int8(batch=2, height=12, width=12),
     "qconv_c16": lambda: W.qconv_stack_int8(batch=1, channels=16, height=5, width=5, n_convs=3),
+    "mlp": lambda: W.mlp_fp32(m=4, k=32, hidden=64),
+    "llama_int4": lambda: W.llama_mlp_int4(m=4, hidden=64, inter=96),
+    "nbits_zp_bias": lambda: W.matmul_nbits_f16(m=5, k=96, n=40, zero_points="block", bias=True),
+    "nbits_zpcol_b16": lambda: W.matmul_nbits_f16(m=3, k=64, n=24, block=16, zero_points="column"),
+    "swish_mul": lambda: W.swish_mul_f16((8, 24)),
 }
 
 
@@ -41,6 +46,20 @@ def test_qconv_stack_plan_shape():
     hdr = _HDR.unpack_from(plan.plan_bytes)
     assert hdr[0] == PLAN_MAGIC and hdr[6] == 32
     assert len(plan.plan_bytes) == 56 + 96 * len(plan.tensors) + 2 * 8 + 440 * len(plan.ops)
+
+
+def test_llama_mlp_plan_fuses_gate_up_swish_mul():
+    plan = B200PlanEmitter().emit_plan(lowering.lower(W.llama_mlp_int4(m=8, hidden=128, inter=192).graph))
+    kinds = [K.NAMES[o.kernel] for o in plan.ops]
+    assert kinds == ["nbits_gemm", "nbits_gemm"]
+    assert plan.ops[0].ip[K.NB_FUSED] == 1 and plan.ops[1].ip[K.NB_FUSED] == 0
+    assert plan.ops[0].ip[K.NB_NTILES] == 3 and plan.ops[1].ip[K.NB_NTILES] == 1
+
+
+def test_nbits_rejections():
+    wl = W.matmul_nbits_f16(m=4, k=60, n=24)
+    with pytest.raises(lowering.UnsupportedOpError, match="multiples of 8"):
+        B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
 
 
 def test_unsupported_op_raises():
