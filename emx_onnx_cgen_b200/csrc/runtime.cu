@@ -59,6 +59,9 @@ const KernelEntry* find_kernel(uint32_t id) {
 
 }  // namespace
 
+// Lets other translation units of the library report through emx_b200_last_error.
+int emx_report_error(int code, const char* msg) { return set_error(code, "%s", msg); }
+
 struct emx_plan {
   int device = 0;
   int num_sms = 0;

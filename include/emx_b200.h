@@ -118,6 +118,30 @@ int emx_b200_op_times(const emx_plan_t *plan, double *ms, int32_t n_ops, int64_t
  * Off: every run launches the kernels one by one. */
 int emx_b200_set_graphs(emx_plan_t *plan, int enable);
 
+/* Allocation-free standalone QLinearConv, 3x3 kernel, stride 1, pads 1,
+ * group 1, no dilation: uint8 NCHW x [n][c][h][w] with x_zero_point 0 or 128,
+ * int8 OIHW weights [oc][c][3][3] with per-output-channel fp32 scales
+ * w_scale[oc] and zero point 0, optional int32 bias[oc] (NULL: none), uint8
+ * NCHW y [n][oc][h][w].  c, oc in {32, 64, 128} (not 32/128 or 128/32).  All
+ * pointers are device pointers; the call enqueues on `stream` (a
+ * cudaStream_t, NULL = legacy default stream) and returns without waiting.
+ *
+ * No counterpart in the reference: its generated C has one function per
+ * model, not per op.  This entry point exists for callers that must not
+ * allocate device memory after start-up (fixed-footprint embedded or
+ * real-time integrations, GPUs shared under a fixed memory budget): it
+ * performs no cudaMalloc/cudaFree and calls no allocating library; it works
+ * in an 8 MiB static device scratch array and rejects geometries that need
+ * more (EMX_ERR_INVALID_ARGUMENT, e.g. a 32 x 64 x 56 x 56 batch fits).
+ * The first call on a device sets up the scratch address (with that device
+ * current) and must come before any stream capture begins.  Calls that can
+ * overlap in time share the scratch and race: serialise them.  Only launch
+ * errors are returned; device-side wait timeouts are not reported here. */
+int emx_b200_qlinear_conv3x3_noalloc(const uint8_t *x, const int8_t *w, const float *w_scale,
+                                     const int32_t *bias, float x_scale, int x_zero_point,
+                                     float y_scale, int y_zero_point, int n, int c, int h, int w_,
+                                     int oc, uint8_t *y, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
