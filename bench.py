@@ -71,6 +71,15 @@ def workload_spec(name: str):
                "engine": "f16", "unit_ops": "TFLOP/s", "dtype": "f16 x int4 -> f32 acc -> f16",
                "ref_tag": "ref_nbits_m1", "ref_rows": 1, "full_rows": m}
         return wl, dom
+    if name == "lstm_fp32":
+        wl = W.lstm_fp32()
+        p = wl.params
+        t, b, i, h = p["seq"], p["batch"], p["input_size"], p["hidden"]
+        flops = 2 * t * b * 4 * h * (i + h)
+        byts = 4 * (t * b * i + t * b * h + 4 * h * (i + h) + 2 * b * h)
+        dom = {"kernel": "lstm_f32", "launches": 1, "ops_total": flops, "bytes_total": byts, "engine": "fp32",
+               "unit_ops": "TFLOP/s", "dtype": "f32", "ref_tag": "ref_lstm_b1", "ref_rows": 1, "full_rows": b}
+        return wl, dom
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -81,6 +90,28 @@ def measured_peaks() -> dict:
         d = json.loads(p.read_text())
         return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def measure_fp32_peak(torch) -> float:
+    """fp32 CUDA-core throughput of cuBLAS SGEMM (TF32 off), best of 10, TFLOP/s."""
+    n = 8192
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(2):
+        a @ b
+    best = 1e30
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        a @ b
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
 
 
 def measure_int8_peak(torch) -> float:
@@ -329,6 +360,9 @@ def ours_arm(args) -> None:
     if dom["engine"] == "int8":
         eng_peak = measure_int8_peak(torch) if rank == 0 else None
         eng_src = "int8 dense, cuBLASLt torch._int_mm 8192^3 best of 10, measured in this run"
+    elif dom["engine"] == "fp32":
+        eng_peak = measure_fp32_peak(torch) if rank == 0 else None
+        eng_src = "fp32 CUDA cores, cuBLAS SGEMM (TF32 off) 8192^3 best of 10, measured in this run"
     else:
         eng_peak = peaks["bf16_tflops"]
         eng_src = f"dense bf16 (= fp16 rate) burst, MEASURED_PEAKS.json ({peaks['source']})"

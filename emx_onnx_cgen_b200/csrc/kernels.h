@@ -22,7 +22,7 @@ enum KernelId : uint32_t {
   K_SWISH_F16 = 8,
   K_MUL_F16 = 9,
   K_ATTENTION_F16 = 10, // opset-23 Attention, flash tiling on tcgen05
-  K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order
+  K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order (1 + 1 + T launches)
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -65,6 +65,11 @@ enum {
   NB_ROUNDED_DEQUANT /*1: one MMA per K slice on fp16-rounded weights (default 0: exact hi + lo)*/
 };
 enum { NBF_ALPHA };
+
+// ---- K_LSTM_F32: t[0]=X [T][B][I], t[1]=W rows interleaved [4H][I] (row 4h+g, g = i,o,f,c),
+//      t[2]=R interleaved [4H][H], t[3]=Wb+Rb interleaved [4H], t[4]=scratch [T*B][4H],
+//      t[5]=scratch h [2][B][H], t[6]=scratch c [B][H], t[7]=Y|-1, t[8]=Y_h|-1, t[9]=Y_c|-1
+enum { LS_T, LS_B, LS_I, LS_H };
 
 // ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), last=y
 enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
@@ -130,5 +135,6 @@ int prepare_nbits(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_lstm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

@@ -49,6 +49,7 @@ const KernelEntry kKernels[] = {
     {emx::K_NBITS_GEMM, emx::prepare_nbits, emx::launch_nbits, "nbits_gemm"},
     {emx::K_SWISH_F16, nullptr, emx::launch_swish_f16, "swish_f16"},
     {emx::K_MUL_F16, nullptr, emx::launch_mul_f16, "mul_f16"},
+    {emx::K_LSTM_F32, nullptr, emx::launch_lstm_f32, "lstm_f32"},
 };
 
 const KernelEntry* find_kernel(uint32_t id) {

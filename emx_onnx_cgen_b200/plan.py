@@ -830,6 +830,52 @@ class B200PlanEmitter:
         self._b.op(K.K_MUL_F16, [a, b_, y], {K.EW_COUNT: int(np.prod(sa)), K.EW_ROWS: rows}, label=op.output,
                    batched=rows > 0)
 
+    # ------------------------------------------------------------------ LSTM
+    def _emit_LstmOp(self, i, op):
+        why = None
+        if self._dtype(op.input_x) != "f32":
+            why = "only fp32"
+        elif str(op.direction) != "forward" or int(op.num_directions) != 1:
+            why = f"direction {op.direction}"
+        elif int(op.layout) != 0:
+            why = "layout 1"
+        elif op.clip is not None or int(op.input_forget):
+            why = "clip / input_forget"
+        elif tuple(op.activation_kinds) not in ((), (2, 1, 1)):
+            why = "non-default activations"
+        elif any(getattr(op, f, None) for f in ("input_sequence_lens", "input_initial_h", "input_initial_c",
+                                                 "input_p")):
+            why = "sequence_lens / initial_h / initial_c / peepholes"
+        elif int(op.input_size) % 4 or int(op.hidden_size) % 4:
+            why = "input and hidden sizes must be multiples of 4"
+        if why:
+            raise UnsupportedOpError(f"LSTM: {why} has no B200 kernel")
+        t, b, isz, h = int(op.seq_length), int(op.batch_size), int(op.input_size), int(op.hidden_size)
+        w = self._const(op.input_w, "W").astype(np.float32).reshape(4, h, isz)
+        r = self._const(op.input_r, "R").astype(np.float32).reshape(4, h, h)
+        # interleave the gate blocks (i, o, f, c) so unit h's gates are rows 4h .. 4h+3
+        wp = np.ascontiguousarray(w.transpose(1, 0, 2)).reshape(4 * h, isz)
+        rp = np.ascontiguousarray(r.transpose(1, 0, 2)).reshape(4 * h, h)
+        if op.input_b is not None:
+            bb = self._const(op.input_b, "B").astype(np.float32).reshape(8, h)
+            bsum = (bb[:4] + bb[4:]).astype(np.float32)  # Wb + Rb, one float add as in the reference
+        else:
+            bsum = np.zeros((4, h), np.float32)
+        bsum = np.ascontiguousarray(bsum.T).reshape(4 * h)
+        t_w = self._b.weight(wp, "f32", op.input_w + ":interleaved")
+        t_r = self._b.weight(rp, "f32", op.input_r + ":interleaved")
+        t_bs = self._b.weight(bsum, "f32", (op.input_b or "lstm") + ":bias-sum")
+        x = self._src(op.input_x)
+        t_gx = self._b.arena_tensor(T_TEMP, "f32", (t * b, 4 * h), name=f"{op.input_x}:lstm-x-partials")
+        t_h = self._b.arena_tensor(T_TEMP, "f32", (2, b, h), name="lstm:h")
+        t_c = self._b.arena_tensor(T_TEMP, "f32", (b, h), name="lstm:c")
+        outs = []
+        for name, shp in ((op.output_y, (t, 1, b, h)), (op.output_y_h, (1, b, h)), (op.output_y_c, (1, b, h))):
+            outs.append(self._dest(name, "f32", shp) if name else -1)
+        self._b.op(K.K_LSTM_F32, [x, t_w, t_r, t_bs, t_gx, t_h, t_c, *outs],
+                   {K.LS_T: t, K.LS_B: b, K.LS_I: isz, K.LS_H: h},
+                   label=f"LSTM T={t} B={b} I={isz} H={h} (reference order)")
+
     # ------------------------------------------------------------------ MatMulNBits
     def _nbits_reject(self, op) -> str | None:
         """Why this MatMulNBits has no tensor-core kernel (None: it has one)."""

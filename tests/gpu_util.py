@@ -53,3 +53,19 @@ def ulp_diff_f16(got: np.ndarray, ref: np.ndarray, atol_eps: float = 1.0) -> np.
     with np.errstate(invalid="ignore"):
         close = np.abs(a.astype(np.float64) - b.astype(np.float64)) <= atol_eps * float(np.finfo(np.float16).eps)
     return np.where(close & ~(na | nb), 0, d).reshape(np.shape(got))
+
+
+def ulp_diff_f32(got: np.ndarray, ref: np.ndarray, atol_eps: float = 1.0) -> np.ndarray:
+    """fp32 counterpart of ulp_diff_f16 (shared/ulp.py:26-50 metric)."""
+    a = np.ascontiguousarray(got, np.float32).reshape(-1)
+    b = np.ascontiguousarray(ref, np.float32).reshape(-1)
+    ia = a.view(np.uint32).astype(np.int64)
+    ib = b.view(np.uint32).astype(np.int64)
+    mag_a, mag_b = ia & 0x7FFFFFFF, ib & 0x7FFFFFFF
+    same = (ia >> 31) == (ib >> 31)
+    d = np.where(same, np.abs(mag_a - mag_b), mag_a + mag_b + 1)
+    na, nb = np.isnan(a), np.isnan(b)
+    d = np.where(na & nb, 0, np.where(na | nb, 0xFFFFFFFF, d))
+    with np.errstate(invalid="ignore"):
+        close = np.abs(a.astype(np.float64) - b.astype(np.float64)) <= atol_eps * float(np.finfo(np.float32).eps)
+    return np.where(close & ~(na | nb), 0, d).reshape(np.shape(got))

@@ -18,6 +18,7 @@ SMALL = {
     "nbits_zp_bias": lambda: W.matmul_nbits_f16(m=5, k=96, n=40, zero_points="block", bias=True),
     "nbits_zpcol_b16": lambda: W.matmul_nbits_f16(m=3, k=64, n=24, block=16, zero_points="column"),
     "swish_mul": lambda: W.swish_mul_f16((8, 24)),
+    "lstm": lambda: W.lstm_fp32(seq=3, batch=2, input_size=8, hidden=16),
 }
 
 
