@@ -71,6 +71,16 @@ def workload_spec(name: str):
                "engine": "f16", "unit_ops": "TFLOP/s", "dtype": "f16 x int4 -> f32 acc -> f16",
                "ref_tag": "ref_nbits_m1", "ref_rows": 1, "full_rows": m}
         return wl, dom
+    if name == "attention_fp16":
+        wl = W.attention_fp16()
+        p = wl.params
+        b, h, t, d = p["batch"], p["heads"], p["seq"], p["head_dim"]
+        flops = 2 * (2 * b * h * t * t * d) // 2  # causal: QK^T and PV over the unmasked half
+        byts = 4 * b * h * t * d * 2
+        dom = {"kernel": "attention_f16", "launches": 1, "ops_total": flops, "bytes_total": byts, "engine": "f16",
+               "unit_ops": "TFLOP/s", "dtype": "f16 (reference statement rounding)", "ref_tag": "ref_attn_b1h1",
+               "ref_rows": 1, "full_rows": b * h}
+        return wl, dom
     if name == "lstm_fp32":
         wl = W.lstm_fp32()
         p = wl.params

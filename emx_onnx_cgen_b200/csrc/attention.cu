@@ -1,0 +1,347 @@
+// ONNX Attention (opset 23), fp16, in the reference's own arithmetic.
+//
+// Reference (src/emx_onnx_cgen/templates/attention_op.c.j2:47-188, c_type
+// _Float16, gcc on x86-64: every _Float16 expression is evaluated in float
+// and rounded to _Float16 when stored), per (b, h, qi):
+//   score = 0; for d: score = r16(score + q*k)        (float add, then fp16)
+//   score = r16(score * scale);  score_bias = r16(score + bias)
+//   bias = -inf where is_causal and ki > qi + past, else 0
+//   max = fmax chain from -inf
+//   w[ki] = max != -inf ? r16(exp((double)r16(score_bias - max))) : 0
+//   sum = r16(sum + w) over ki ascending;  inv = sum == 0 ? 0 : r16(1.0f / sum)
+//   out[vd] = acc, acc = r16(acc + r16(w * inv) * v) over ki ascending
+// where r16 rounds a float to fp16 (round to nearest even) and products of
+// two fp16 values are exact in float.  This kernel repeats exactly these
+// operations (float adds/multiplies with explicit rounding, cvt to fp16 and
+// back), so its output is bit-identical to the reference's.  exp runs as a
+// guarded float evaluation with a double fallback near fp16 rounding
+// boundaries (see exp_f16_ref).
+//
+// Masked keys.  Under is_causal a masked score is -inf, its weight exp(-inf)
+// = +0, and it leaves max, sum and (barring a -0 accumulator) every output
+// unchanged -- provided no score is +inf or NaN and no V value is inf or NaN.
+// A pre-pass checks Q, K, V for that (all finite, and D * max|q| * max|k|
+// small enough that no partial score can overflow fp16); when it holds the
+// kernel skips masked keys entirely (half the work), otherwise it evaluates
+// every key with the mask arithmetic of the reference.
+//
+// Work split: one CTA per (q block of 16 rows, head, batch); phase 1
+// computes the block's scores one K tile (64 keys, transposed in shared
+// memory) at a time, 8 sequential chains per thread; the row maxima,
+// weights, per-row sequential sums and scaled weights follow in shared
+// memory; phase 2 streams V tiles and runs the per-(row, vd) accumulations.
+// Heaviest q blocks (last rows, most keys) are scheduled first.
+#include <cuda_fp16.h>
+
+#include "host_util.h"
+#include "kernels.h"
+#include "tc100.cuh"
+
+namespace emx {
+
+constexpr int AT_QB = 16;    // query rows per CTA
+constexpr int AT_KT = 64;    // keys per K / V tile
+constexpr int AT_THREADS = 128;
+
+struct AttnParams {
+  const uint16_t* q;
+  const uint16_t* k;
+  const uint16_t* v;
+  uint16_t* o;
+  int64_t q_sb, q_sh, q_st, k_sb, k_sh, k_st, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
+  int B, HQ, group, TQ, TK, past, D, DV, causal, scn;
+  float scale;          // fp16 scale value
+  const uint32_t* stats;  // [0] max|q| bits, [1] max|k| bits, [2] non-finite seen
+  int* err;
+};
+
+__device__ __forceinline__ float h2f(uint16_t h) {
+  float r;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(r) : "h"(h));
+  return r;
+}
+__device__ __forceinline__ uint16_t f2h(float f) {
+  uint16_t r;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f));
+  return r;
+}
+__device__ __forceinline__ float r16(float f) { return h2f(f2h(f)); }
+__device__ __forceinline__ uint16_t d2h(double v) {
+  uint16_t r;
+  asm("cvt.rn.f16.f64 %0, %1;" : "=h"(r) : "d"(v));
+  return r;
+}
+
+// fp16(exp((double)a)) for an fp16 value a: float expf (documented <= 2 ulp)
+// widened by a 2^-20 relative margin; if both ends round to the same fp16 it
+// is the correctly rounded result, else the double evaluation decides.
+__device__ __forceinline__ uint16_t exp_f16_ref(float a) {
+  const float e = expf(a);
+  const uint16_t lo = f2h(__fmul_rn(e, 1.0f - 0x1p-20f));
+  const uint16_t hi = f2h(__fmul_rn(e, 1.0f + 0x1p-20f));
+  if (lo == hi && !isnan(e)) return lo;
+  return d2h(exp((double)a));
+}
+
+__global__ void attn_stats_reset_kernel(uint32_t* stats) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x < 4) stats[threadIdx.x] = 0;
+}
+
+// max |x| (as bits of a non-negative fp16) and a non-finite flag over n fp16 values
+__global__ void attn_stats_kernel(const uint16_t* __restrict__ q, int64_t nq, const uint16_t* __restrict__ k,
+                                  int64_t nk, const uint16_t* __restrict__ v, int64_t nv, uint32_t* stats) {
+  pdl_wait();
+  pdl_launch_dependents();
+  uint32_t mq = 0, mk = 0, bad = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nq; i += stride) {
+    const uint32_t a = q[i] & 0x7FFFu;
+    mq = max(mq, a);
+    bad |= a >= 0x7C00u;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nk; i += stride) {
+    const uint32_t a = k[i] & 0x7FFFu;
+    mk = max(mk, a);
+    bad |= a >= 0x7C00u;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += stride)
+    bad |= (v[i] & 0x7FFFu) >= 0x7C00u;
+  for (int o = 16; o > 0; o >>= 1) {
+    mq = max(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+    mk = max(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (mq) atomicMax(&stats[0], mq);
+    if (mk) atomicMax(&stats[1], mk);
+    if (bad) atomicOr(&stats[2], 1u);
+  }
+}
+
+__global__ void __launch_bounds__(AT_THREADS) attention_exact_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) uint8_t at_smem[];
+  uint16_t* qs = reinterpret_cast<uint16_t*>(at_smem);        // [QB][D]
+  uint16_t* kt = qs + AT_QB * p.D;                              // [D][KT]
+  uint16_t* vt = kt + p.D * AT_KT;                              // [KT][DV]
+  uint16_t* sc = vt + AT_KT * p.DV;                             // [QB][scn]
+  float* rowmax = reinterpret_cast<float*>(sc + (size_t)AT_QB * p.scn);
+  float* rowinv = rowmax + AT_QB;
+
+  const int qblk = gridDim.x - 1 - blockIdx.x;  // heaviest (last) rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / p.group;
+  const int q0 = qblk * AT_QB;
+  const int tid = threadIdx.x;
+  const uint16_t* qg = p.q + b * p.q_sb + h * p.q_sh;
+  const uint16_t* kg = p.k + b * p.k_sb + kvh * p.k_sh;
+  const uint16_t* vg = p.v + b * p.v_sb + kvh * p.v_sh;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  // masked keys may be skipped only when every score is finite (see header)
+  bool fast = false;
+  if (p.causal && p.stats[2] == 0) {
+    const float mq = h2f((uint16_t)p.stats[0]), mk = h2f((uint16_t)p.stats[1]);
+    fast = (float)p.D * mq * mk * 1.3f * fmaxf(1.0f, fabsf(p.scale)) < 60000.0f;
+  }
+  auto row_end = [&](int r) -> int {  // keys row r must visit
+    const int qi = q0 + r;
+    if (fast) return min(p.TK, qi + p.past + 1);
+    return p.TK;
+  };
+  const int last_row = min(AT_QB, p.TQ - q0) - 1;
+  const int kend_blk = row_end(last_row);
+
+  for (int i = tid; i < AT_QB * p.D; i += AT_THREADS) {
+    const int r = i / p.D, d = i - r * p.D;
+    qs[i] = q0 + r < p.TQ ? qg[(int64_t)(q0 + r) * p.q_st + d] : 0;
+  }
+
+  // ---- phase 1: scores (8 chains per thread: key kk, rows rs, rs+2, ..., rs+14)
+  const int kk = tid & (AT_KT - 1), rs = tid >> 6;
+  for (int k0 = 0; k0 < kend_blk; k0 += AT_KT) {
+    __syncthreads();
+    // transpose into [d][key]: key fastest, so the shared-memory stores do not collide
+    for (int i = tid; i < AT_KT * p.D; i += AT_THREADS) {
+      const int key = i % AT_KT, d = i / AT_KT;
+      kt[d * AT_KT + key] = k0 + key < p.TK ? kg[(int64_t)(k0 + key) * p.k_st + d] : 0;
+    }
+    __syncthreads();
+    const int key = k0 + kk;
+    float s[AT_QB / 2];
+#pragma unroll
+    for (int j = 0; j < AT_QB / 2; ++j) s[j] = 0.0f;
+    for (int d = 0; d < p.D; ++d) {
+      const float kf = h2f(kt[d * AT_KT + kk]);
+#pragma unroll
+      for (int j = 0; j < AT_QB / 2; ++j) s[j] = r16(__fadd_rn(s[j], __fmul_rn(h2f(qs[(rs + 2 * j) * p.D + d]), kf)));
+    }
+#pragma unroll
+    for (int j = 0; j < AT_QB / 2; ++j) {
+      const int r = rs + 2 * j;
+      if (key >= row_end(r) || q0 + r >= p.TQ) continue;
+      const float sv = r16(__fmul_rn(s[j], p.scale));
+      const bool masked = p.causal && key > q0 + r + p.past;
+      sc[r * p.scn + key] = f2h(__fadd_rn(sv, masked ? -INFINITY : 0.0f));
+    }
+  }
+  __syncthreads();
+
+  // ---- row maxima (fmax chain from -inf; NaN-ignoring and order-free)
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int r = warp; r < AT_QB; r += AT_THREADS / 32) {
+    float m = -INFINITY;
+    if (q0 + r < p.TQ)
+      for (int key = lane; key < row_end(r); key += 32) m = fmaxf(m, h2f(sc[r * p.scn + key]));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) rowmax[r] = m;
+  }
+  __syncthreads();
+  // ---- weights
+  for (int r = warp; r < AT_QB; r += AT_THREADS / 32) {
+    if (q0 + r >= p.TQ) continue;
+    const float m = rowmax[r];
+    for (int key = lane; key < row_end(r); key += 32) {
+      uint16_t w = 0;
+      if (m != -INFINITY) w = exp_f16_ref(r16(__fsub_rn(h2f(sc[r * p.scn + key]), m)));
+      sc[r * p.scn + key] = w;
+    }
+  }
+  __syncthreads();
+  // ---- sequential sums and reciprocals, one thread per row
+  if (tid < AT_QB && q0 + tid < p.TQ) {
+    float sum = 0.0f;
+    const int e = row_end(tid);
+    for (int key = 0; key < e; ++key) sum = r16(__fadd_rn(sum, h2f(sc[tid * p.scn + key])));
+    rowinv[tid] = sum == 0.0f ? 0.0f : r16(__fdiv_rn(1.0f, sum));
+  }
+  __syncthreads();
+  // ---- scaled weights r16(w * inv)
+  for (int r = warp; r < AT_QB; r += AT_THREADS / 32) {
+    if (q0 + r >= p.TQ) continue;
+    const float inv = rowinv[r];
+    for (int key = lane; key < row_end(r); key += 32)
+      sc[r * p.scn + key] = f2h(__fmul_rn(h2f(sc[r * p.scn + key]), inv));
+  }
+
+  // ---- phase 2: outputs (chains for vd pair vp, rows rs, rs+2, ...)
+  const int vp = tid & 63;
+  const bool vd_ok = 2 * vp < p.DV;
+  float acc[AT_QB / 2][2];
+#pragma unroll
+  for (int j = 0; j < AT_QB / 2; ++j) acc[j][0] = acc[j][1] = 0.0f;
+  for (int k0 = 0; k0 < kend_blk; k0 += AT_KT) {
+    __syncthreads();
+    for (int i = tid; i < AT_KT * p.DV; i += AT_THREADS) {
+      const int key = i / p.DV, d = i - key * p.DV;
+      vt[i] = k0 + key < p.TK ? vg[(int64_t)(k0 + key) * p.v_st + d] : 0;
+    }
+    __syncthreads();
+    if (!vd_ok) continue;
+    const int kn = min(AT_KT, kend_blk - k0);
+    for (int kk2 = 0; kk2 < kn; ++kk2) {
+      const int key = k0 + kk2;
+      const uint32_t v2 = *reinterpret_cast<const uint32_t*>(&vt[kk2 * p.DV + 2 * vp]);
+      const float v0 = h2f((uint16_t)v2), v1 = h2f((uint16_t)(v2 >> 16));
+#pragma unroll
+      for (int j = 0; j < AT_QB / 2; ++j) {
+        const int r = rs + 2 * j;
+        if (key >= row_end(r)) continue;
+        const float w = h2f(sc[r * p.scn + key]);
+        acc[j][0] = r16(__fadd_rn(acc[j][0], __fmul_rn(w, v0)));
+        acc[j][1] = r16(__fadd_rn(acc[j][1], __fmul_rn(w, v1)));
+      }
+    }
+  }
+  if (!vd_ok) return;
+#pragma unroll
+  for (int j = 0; j < AT_QB / 2; ++j) {
+    const int r = rs + 2 * j;
+    const int qi = q0 + r;
+    if (qi >= p.TQ) continue;
+    if (fast) {
+      // skipped keys each add r16(+0 * v) = +-0: it matters only to a -0 accumulator
+      for (int c = 0; c < 2; ++c) {
+        if (__float_as_uint(acc[j][c]) != 0x80000000u) continue;
+        for (int key = row_end(r); key < p.TK; ++key)
+          acc[j][c] = r16(__fadd_rn(acc[j][c], __fmul_rn(0.0f, h2f(vg[(int64_t)key * p.v_st + 2 * vp + c]))));
+      }
+    }
+    uint16_t* og = p.o + b * p.o_sb + h * p.o_sh + (int64_t)qi * p.o_st + 2 * vp;
+    og[0] = f2h(acc[j][0]);
+    if (2 * vp + 1 < p.DV) og[1] = f2h(acc[j][1]);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+struct AttnState {
+  size_t smem;
+  int scn;
+};
+static_assert(sizeof(AttnState) <= sizeof(OpState), "state fits");
+
+static size_t attn_smem(int d, int dv, int scn) {
+  return (size_t)2 * (AT_QB * d + d * AT_KT + AT_KT * dv + (size_t)AT_QB * scn) + 2 * AT_QB * 4 + 16;
+}
+
+int prepare_attention(const PlanOp& op, void* const*, OpState* st_, int, char* msg, size_t n) {
+  AttnState* st = reinterpret_cast<AttnState*>(st_);
+  const int d = (int)op.ip[AT_D], dv = (int)op.ip[AT_DV], tk = (int)op.ip[AT_TK];
+  if (d <= 0 || dv <= 0 || dv > 128 || (dv & 1)) return fail(msg, n, 5, "Attention: head sizes D=%d DV=%d", d, dv);
+  st->scn = (int)align_up((size_t)tk, AT_KT);
+  st->smem = attn_smem(d, dv, st->scn);
+  if (st->smem > 227 * 1024) return fail(msg, n, 5, "Attention: %zu B shared memory for %d keys", st->smem, tk);
+  cudaError_t e =
+      cudaFuncSetAttribute(attention_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)st->smem);
+  if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+int launch_attention(const PlanOp& op, void* const* ptrs, const OpState* st_, const LaunchCtx& ctx, int* launches) {
+  const AttnState* st = reinterpret_cast<const AttnState*>(st_);
+  AttnParams p{};
+  p.q = (const uint16_t*)ptrs[op.t[0]];
+  p.k = (const uint16_t*)ptrs[op.t[1]];
+  p.v = (const uint16_t*)ptrs[op.t[2]];
+  p.o = (uint16_t*)ptrs[op.t[3]];
+  uint32_t* stats = (uint32_t*)ptrs[op.t[4]];
+  p.stats = stats;
+  p.err = ctx.d_error;
+  p.B = (int)eff_batch(ctx, op, op.ip[AT_B]);
+  p.HQ = (int)op.ip[AT_HQ];
+  p.group = (int)op.ip[AT_GROUP];
+  p.TQ = (int)op.ip[AT_TQ];
+  p.TK = (int)op.ip[AT_TK];
+  p.past = (int)op.ip[AT_PAST];
+  p.D = (int)op.ip[AT_D];
+  p.DV = (int)op.ip[AT_DV];
+  p.causal = (int)op.ip[AT_CAUSAL];
+  p.scn = st->scn;
+  p.scale = (float)op.fp[ATF_SCALE];
+  const int64_t* s = &op.ip[AT_Q_SB];
+  p.q_sb = s[0]; p.q_sh = s[1]; p.q_st = s[2];
+  p.k_sb = s[3]; p.k_sh = s[4]; p.k_st = s[5];
+  p.v_sb = s[6]; p.v_sh = s[7]; p.v_st = s[8];
+  p.o_sb = s[9]; p.o_sh = s[10]; p.o_st = s[11];
+  if (p.B <= 0 || p.TQ <= 0) return 0;
+  const int64_t hkv = p.HQ / p.group;
+  const int64_t nq = (int64_t)p.B * p.q_sb, nk = (int64_t)p.B * p.k_sb, nv = (int64_t)p.B * p.v_sb;
+  (void)hkv;
+  cudaError_t e = launch_pdl(attn_stats_reset_kernel, dim3(1), dim3(32), 0, ctx.stream, stats);
+  ++*launches;
+  if (e == cudaSuccess) {
+    e = launch_pdl(attn_stats_kernel, dim3(ctx.num_sms * 4), dim3(256), 0, ctx.stream, p.q, nq, p.k, nk, p.v, nv,
+                   stats);
+    ++*launches;
+  }
+  if (e == cudaSuccess) {
+    dim3 grid((unsigned)((p.TQ + AT_QB - 1) / AT_QB), (unsigned)p.HQ, (unsigned)p.B);
+    e = launch_pdl(attention_exact_kernel, grid, dim3(AT_THREADS), st->smem, ctx.stream, p);
+    ++*launches;
+  }
+  return e == cudaSuccess ? 0 : 4;
+}
+
+}  // namespace emx

@@ -21,7 +21,7 @@ enum KernelId : uint32_t {
   K_NBITS_GEMM = 7,     // MatMulNBits int4 x fp16 on tcgen05 kind::f16 (+ fused Swish*Mul of a gate/up pair)
   K_SWISH_F16 = 8,
   K_MUL_F16 = 9,
-  K_ATTENTION_F16 = 10, // opset-23 Attention, flash tiling on tcgen05
+  K_ATTENTION_F16 = 10, // opset-23 Attention in the reference's fp16 arithmetic
   K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order (1 + 1 + T launches)
 };
 
@@ -65,6 +65,14 @@ enum {
   NB_ROUNDED_DEQUANT /*1: one MMA per K slice on fp16-rounded weights (default 0: exact hi + lo)*/
 };
 enum { NBF_ALPHA };
+
+// ---- K_ATTENTION_F16: t[0]=Q, t[1]=K, t[2]=V, t[3]=Y (fp16), t[4]=scratch (4 words);
+//      element (b, h, t, d) of a tensor sits at b*SB + h*SH + t*ST + d (3-D or 4-D layouts)
+enum {
+  AT_B, AT_HQ, AT_GROUP, AT_TQ, AT_TK, AT_PAST, AT_D, AT_DV, AT_CAUSAL,
+  AT_Q_SB, AT_Q_SH, AT_Q_ST, AT_K_SB, AT_K_SH, AT_K_ST, AT_V_SB, AT_V_SH, AT_V_ST, AT_O_SB, AT_O_SH, AT_O_ST
+};
+enum { ATF_SCALE };
 
 // ---- K_LSTM_F32: t[0]=X [T][B][I], t[1]=W rows interleaved [4H][I] (row 4h+g, g = i,o,f,c),
 //      t[2]=R interleaved [4H][H], t[3]=Wb+Rb interleaved [4H], t[4]=scratch [T*B][4H],
@@ -136,5 +144,7 @@ int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, 
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_lstm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_attention(const PlanOp&, void* const*, OpState*, int, char*, size_t);
+int launch_attention(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

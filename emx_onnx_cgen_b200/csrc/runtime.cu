@@ -50,6 +50,7 @@ const KernelEntry kKernels[] = {
     {emx::K_SWISH_F16, nullptr, emx::launch_swish_f16, "swish_f16"},
     {emx::K_MUL_F16, nullptr, emx::launch_mul_f16, "mul_f16"},
     {emx::K_LSTM_F32, nullptr, emx::launch_lstm_f32, "lstm_f32"},
+    {emx::K_ATTENTION_F16, emx::prepare_attention, emx::launch_attention, "attention_f16"},
 };
 
 const KernelEntry* find_kernel(uint32_t id) {

@@ -830,6 +830,49 @@ class B200PlanEmitter:
         self._b.op(K.K_MUL_F16, [a, b_, y], {K.EW_COUNT: int(np.prod(sa)), K.EW_ROWS: rows}, label=op.output,
                    batched=rows > 0)
 
+    # ------------------------------------------------------------------ Attention
+    def _emit_AttentionOp(self, i, op):
+        why = None
+        if self._dtype(op.input_q) != "f16" or _suffix(op.dtype) != "f16":
+            why = "only fp16"
+        elif any(getattr(op, f, None) for f in ("input_attn_mask", "input_past_key", "input_past_value",
+                                                 "input_nonpad_kv_seqlen", "output_present_key",
+                                                 "output_present_value", "output_qk_matmul")):
+            why = "masks, past key/value and extra outputs"
+        elif float(op.softcap) != 0.0:
+            why = "softcap"
+        elif int(op.v_head_size) > 128 or int(op.v_head_size) % 2:
+            why = "v head size above 128 or odd"
+        if why:
+            raise UnsupportedOpError(f"Attention: {why} has no B200 kernel")
+        b, hq, hkv = int(op.batch), int(op.q_heads), int(op.kv_heads)
+        tq, tk, d, dv = int(op.q_seq), int(op.total_seq), int(op.qk_head_size), int(op.v_head_size)
+
+        def strides(rank, heads, t, hd):
+            # 4-D [B][H][T][hd] or 3-D [B][T][H*hd]: (batch, head, token) strides in elements
+            return (heads * t * hd, t * hd, hd) if rank == 4 else (t * heads * hd, hd, heads * hd)
+
+        q_rank = int(op.q_rank)
+        k_rank = int(getattr(op, "k_rank", q_rank))
+        v_rank = int(getattr(op, "v_rank", q_rank))
+        o_rank = int(getattr(op, "output_rank", q_rank))
+        ss = (*strides(q_rank, hq, tq, d), *strides(k_rank, hkv, int(op.kv_seq), d),
+              *strides(v_rank, hkv, int(op.kv_seq), dv), *strides(o_rank, hq, tq, dv))
+        q, k, v = self._src(op.input_q), self._src(op.input_k), self._src(op.input_v)
+        out_shape = tuple(self._shape(op.output))
+        y = self._dest(op.output, "f16", out_shape)
+        t_st = self._b.arena_tensor(T_TEMP, "u8", (16,), name="attention:stats")
+        # `const _Float16 scale = (_Float16)<float literal>;`: float first, then fp16
+        scale16 = float(np.float16(np.float32(float(op.scale))))
+        batched = (self._batch > 0 and b == self._batch and self._is_batched(op.input_q)
+                   and self._is_batched(op.input_k) and self._is_batched(op.input_v))
+        ip = {K.AT_B: b, K.AT_HQ: hq, K.AT_GROUP: hq // hkv, K.AT_TQ: tq, K.AT_TK: tk, K.AT_PAST: int(op.past_seq),
+              K.AT_D: d, K.AT_DV: dv, K.AT_CAUSAL: int(bool(op.is_causal))}
+        for slot, val in zip(range(K.AT_Q_SB, K.AT_O_ST + 1), ss):
+            ip[slot] = val
+        self._b.op(K.K_ATTENTION_F16, [q, k, v, y, t_st], ip, {K.ATF_SCALE: scale16},
+                   label=f"{op.output} (reference fp16 arithmetic)", batched=batched)
+
     # ------------------------------------------------------------------ LSTM
     def _emit_LstmOp(self, i, op):
         why = None

@@ -19,6 +19,7 @@ SMALL = {
     "nbits_zpcol_b16": lambda: W.matmul_nbits_f16(m=3, k=64, n=24, block=16, zero_points="column"),
     "swish_mul": lambda: W.swish_mul_f16((8, 24)),
     "lstm": lambda: W.lstm_fp32(seq=3, batch=2, input_size=8, hidden=16),
+    "attention": lambda: W.attention_fp16(batch=1, heads=2, seq=16, head_dim=8),
 }
 
 
