@@ -23,6 +23,12 @@ enum KernelId : uint32_t {
   K_MUL_F16 = 9,
   K_ATTENTION_F16 = 10, // opset-23 Attention in the reference's fp16 arithmetic
   K_LSTM_F32 = 11,      // LSTM forward, reference accumulation order (1 + 1 + T launches)
+  K_QLINEAR_MATMUL = 13,
+  K_MATMUL_INTEGER = 14,
+  K_CONV_F32 = 15,
+  K_SOFTMAX_F32 = 16,
+  K_QUANTIZE_LINEAR = 17,
+  K_DEQUANTIZE_LINEAR = 18,
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -78,6 +84,22 @@ enum { ATF_SCALE };
 //      t[2]=R interleaved [4H][H], t[3]=Wb+Rb interleaved [4H], t[4]=scratch [T*B][4H],
 //      t[5]=scratch h [2][B][H], t[6]=scratch c [B][H], t[7]=Y|-1, t[8]=Y_h|-1, t[9]=Y_c|-1
 enum { LS_T, LS_B, LS_I, LS_H };
+
+// ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y
+enum {
+  QM_M, QM_K, QM_N, QM_A_SIGNED, QM_B_SIGNED, QM_A_ZERO, QM_B_ZERO, QM_QUANTIZED, QM_USE_INT, QM_FRAC_BITS,
+  QM_MULT, QM_Y_ZERO, QM_Y_SIGNED, QM_ROWS_PER_BATCH
+};
+enum { QMF_SCALE };
+
+// ---- K_CONV_F32: t[0]=X NCHW, t[1]=W OIHW, t[2]=bias|-1, t[3]=Y
+enum { CF_N, CF_C, CF_H, CF_W, CF_OC, CF_KH, CF_KW, CF_OH, CF_OW, CF_SH, CF_SW, CF_PT, CF_PL, CF_DH, CF_DW, CF_GROUP };
+
+// ---- K_SOFTMAX_F32: t[0]=X, t[1]=Y; shape viewed as [outer][axis][inner]
+enum { SM_OUTER, SM_AXIS, SM_INNER, SM_OUTER_PER_BATCH };
+
+// ---- K_QUANTIZE_LINEAR / K_DEQUANTIZE_LINEAR: t[0]=X, t[1]=scale f32 [axis_len], t[2]=zero point|-1, t[3]=Y
+enum { QL_COUNT, QL_AXIS_LEN, QL_INNER, QL_SIGNED, QL_ROWS };
 
 // ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), last=y
 enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
@@ -144,6 +166,10 @@ int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, 
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_lstm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_qmatmul(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_conv_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_softmax_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_quant(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_attention(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_attention(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 

@@ -246,6 +246,97 @@ class LstmOp:
     dtype: ScalarType
 
 
+@dataclass(frozen=True)
+class QLinearMatMulOp:
+    input0: str
+    input0_scale: str
+    input0_zero_point: str
+    input1: str
+    input1_scale: str
+    input1_zero_point: str
+    output_scale: str
+    output_zero_point: str
+    output: str
+    input0_shape: tuple[int, ...]
+    input1_shape: tuple[int, ...]
+    output_shape: tuple[int, ...]
+    m: int
+    n: int
+    k: int
+    input0_dtype: ScalarType
+    input1_dtype: ScalarType
+    dtype: ScalarType
+    input0_scale_dtype: ScalarType
+    input1_scale_dtype: ScalarType
+    output_scale_dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class MatMulIntegerOp:
+    input0: str
+    input1: str
+    input0_zero_point: str | None
+    input1_zero_point: str | None
+    output: str
+    input0_shape: tuple[int, ...]
+    input1_shape: tuple[int, ...]
+    output_shape: tuple[int, ...]
+    m: int
+    n: int
+    k: int
+    input0_dtype: ScalarType
+    input1_dtype: ScalarType
+    dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class ConvOp:
+    input0: str
+    weights: str
+    bias: str | None
+    output: str
+    batch: int
+    in_channels: int
+    out_channels: int
+    spatial_rank: int
+    in_spatial: tuple[int, ...]
+    out_spatial: tuple[int, ...]
+    kernel_shape: tuple[int, ...]
+    strides: tuple[int, ...]
+    pads: tuple[int, ...]
+    dilations: tuple[int, ...]
+    group: int
+    dtype: ScalarType
+
+
+@dataclass(frozen=True)
+class SoftmaxOp:
+    input0: str
+    output: str
+    axis: int | None
+    use_legacy_axis_semantics: bool = False
+
+
+@dataclass(frozen=True)
+class QuantizeLinearOp:
+    input0: str
+    scale: str
+    zero_point: str | None
+    output: str
+    axis: int | None
+    block_size: int | None
+
+
+@dataclass(frozen=True)
+class DequantizeLinearOp:
+    input0: str
+    scale: str
+    zero_point: str | None
+    output: str
+    axis: int | None
+    block_size: int | None
+
+
 # ------------------------------------------------------------------ lowering
 def _st(suffix: str) -> ScalarType:
     return ScalarType(suffix)
@@ -357,6 +448,64 @@ def _lower_node(node, shapes, dtypes):
             accuracy_level=int(a.get("accuracy_level", 0)), n_blocks_per_col=nb, blob_size=block * bits // 8,
             input0_shape=xs, output_shape=shapes[y], m=int(np.prod(xs[:-1])), input0_dtype=dtypes[ins[0]],
             output_dtype=dtypes[ins[0]], scales_dtype=dtypes[ins[2]])
+    if op in ("QLinearMatMul", "MatMulInteger"):
+        a_name, b_name = ins[0], ins[3] if op == "QLinearMatMul" else ins[1]
+        xs, ws = shapes[a_name], shapes[b_name]
+        if len(ws) != 2:
+            raise UnsupportedOpError(f"{op}: only 2-D B has a B200 kernel")
+        m, k, n = int(np.prod(xs[:-1])) if len(xs) > 1 else 1, xs[-1], ws[1]
+        y = node.outputs[0]
+        shapes[y] = (*xs[:-1], n)
+        if op == "QLinearMatMul":
+            dtypes[y] = dtypes[ins[7]]
+            return QLinearMatMulOp(
+                input0=ins[0], input0_scale=ins[1], input0_zero_point=ins[2], input1=ins[3], input1_scale=ins[4],
+                input1_zero_point=ins[5], output_scale=ins[6], output_zero_point=ins[7], output=y,
+                input0_shape=xs, input1_shape=ws, output_shape=shapes[y], m=m, n=n, k=k,
+                input0_dtype=dtypes[ins[0]], input1_dtype=dtypes[ins[3]], dtype=dtypes[y],
+                input0_scale_dtype=dtypes[ins[1]], input1_scale_dtype=dtypes[ins[4]],
+                output_scale_dtype=dtypes[ins[6]])
+        dtypes[y] = ScalarType.I32
+        return MatMulIntegerOp(
+            input0=ins[0], input1=ins[1], input0_zero_point=ins[2] if len(ins) > 2 and ins[2] else None,
+            input1_zero_point=ins[3] if len(ins) > 3 and ins[3] else None, output=y, input0_shape=xs,
+            input1_shape=ws, output_shape=shapes[y], m=m, n=n, k=k, input0_dtype=dtypes[ins[0]],
+            input1_dtype=dtypes[ins[1]], dtype=ScalarType.I32)
+    if op == "Conv":
+        x, w = ins[0], ins[1]
+        n, c, *sp = shapes[x]
+        oc, _, *ks = shapes[w]
+        rank = len(sp)
+        ks = tuple(a.get("kernel_shape", ks))
+        strides = tuple(a.get("strides", [1] * rank))
+        dil = tuple(a.get("dilations", [1] * rank))
+        pads = tuple(a.get("pads", [0] * (2 * rank)))
+        out_sp = tuple((sp[i] + pads[i] + pads[i + rank] - ((ks[i] - 1) * dil[i] + 1)) // strides[i] + 1
+                       for i in range(rank))
+        y = node.outputs[0]
+        shapes[y] = (n, oc, *out_sp)
+        dtypes[y] = dtypes[x]
+        return ConvOp(input0=x, weights=w, bias=ins[2] if len(ins) > 2 and ins[2] else None, output=y, batch=n,
+                      in_channels=c, out_channels=oc, spatial_rank=rank, in_spatial=tuple(sp),
+                      out_spatial=out_sp, kernel_shape=ks, strides=strides, pads=pads, dilations=dil,
+                      group=int(a.get("group", 1)), dtype=dtypes[x])
+    if op == "Softmax":
+        y = node.outputs[0]
+        shapes[y] = shapes[ins[0]]
+        dtypes[y] = dtypes[ins[0]]
+        return SoftmaxOp(input0=ins[0], output=y, axis=int(a.get("axis", -1)))
+    if op in ("QuantizeLinear", "DequantizeLinear"):
+        y = node.outputs[0]
+        shapes[y] = shapes[ins[0]]
+        if op == "QuantizeLinear":
+            dtypes[y] = dtypes[ins[2]] if len(ins) > 2 and ins[2] else ScalarType.U8
+            cls = QuantizeLinearOp
+        else:
+            dtypes[y] = dtypes[ins[1]]
+            cls = DequantizeLinearOp
+        return cls(input0=ins[0], scale=ins[1], zero_point=ins[2] if len(ins) > 2 and ins[2] else None, output=y,
+                   axis=int(a["axis"]) if "axis" in a else None,
+                   block_size=int(a["block_size"]) if "block_size" in a else None)
     if op == "Attention":
         b, hq, tq, d = shapes[ins[0]]
         _, hkv, tkv, _ = shapes[ins[1]]

@@ -23,6 +23,7 @@ parameter slots in ``csrc/kernels.h`` (mirrored in ``kernel_ids.py``).
 """
 from __future__ import annotations
 
+import math
 import struct
 from dataclasses import dataclass, field
 
@@ -550,7 +551,9 @@ class B200PlanEmitter:
             "QLinearConvOp": ("input0",), "QLinearAddOp": ("input0", "input1"),
             "GemmOp": ("input_a", "input_b", "input_c"), "UnaryOp": ("input0",), "BinaryOp": ("input0", "input1"),
             "MatMulNBitsOp": ("input0",), "AttentionOp": ("input_q", "input_k", "input_v"),
-            "LstmOp": ("input_x",),
+            "LstmOp": ("input_x",), "QLinearMatMulOp": ("input0", "input1"), "MatMulIntegerOp": ("input0", "input1"),
+            "ConvOp": ("input0", "weights", "bias"), "SoftmaxOp": ("input0",), "QuantizeLinearOp": ("input0",),
+            "DequantizeLinearOp": ("input0",),
         }.get(_name(op), ())
         return [getattr(op, f) for f in fields if getattr(op, f, None)]
 
@@ -829,6 +832,135 @@ class B200PlanEmitter:
                 and self._is_batched(op.input1) else 0)
         self._b.op(K.K_MUL_F16, [a, b_, y], {K.EW_COUNT: int(np.prod(sa)), K.EW_ROWS: rows}, label=op.output,
                    batched=rows > 0)
+
+    # ------------------------------------------------------------------ QLinearMatMul / MatMulInteger
+    def _rows_batched(self, name: str, shape) -> tuple[bool, int]:
+        """(batched, rows per batch entry) for an op whose rows are shape[:-1]."""
+        rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+        batched = (self._batch > 0 and len(shape) > 1 and shape[0] == self._batch and self._is_batched(name))
+        return batched, (rows // self._batch if batched else 0)
+
+    def _emit_matmul8(self, op, quantized: bool):
+        what = "QLinearMatMul" if quantized else "MatMulInteger"
+        a_dt, b_dt = self._dtype(op.input0), self._dtype(op.input1)
+        if a_dt not in ("u8", "i8") or b_dt not in ("u8", "i8") or len(op.input1_shape) != 2:
+            raise UnsupportedOpError(f"{what}: 8-bit A and 2-D 8-bit B only")
+        a, b_ = self._src(op.input0), self._src(op.input1)
+        batched, rpb = self._rows_batched(op.input0, tuple(op.input0_shape))
+        zero = lambda nm, w: 0 if nm is None else int(self._scalar(nm, w))
+        ip = {K.QM_M: int(op.m), K.QM_K: int(op.k), K.QM_N: int(op.n), K.QM_A_SIGNED: int(a_dt == "i8"),
+              K.QM_B_SIGNED: int(b_dt == "i8"), K.QM_A_ZERO: zero(op.input0_zero_point, "a zero point"),
+              K.QM_B_ZERO: zero(op.input1_zero_point, "b zero point"), K.QM_QUANTIZED: int(quantized),
+              K.QM_ROWS_PER_BATCH: rpb}
+        fp = {}
+        if quantized:
+            dts = {_suffix(op.input0_scale_dtype), _suffix(op.input1_scale_dtype), _suffix(op.output_scale_dtype)}
+            if dts != {"f32"}:
+                raise UnsupportedOpError("QLinearMatMul: only fp32 scales")
+            sa, sb, sy = (np.float32(self._scalar(nm, "scale")) for nm in
+                          (op.input0_scale, op.input1_scale, op.output_scale))
+            # the template's float scale ((float)sa * (float)sb / (float)sy) and its integer requant
+            # parameters, computed with the same double operations
+            scale = np.float32(np.float32(sa * sb) / sy)
+            real = float(sa) * float(sb) / float(sy)
+            frac = 31
+            scaled = math.ldexp(real, frac)
+            while frac > 0 and abs(scaled) > 2147483647.0:
+                frac -= 1
+                scaled = math.ldexp(real, frac)
+            mult = int(math.copysign(math.floor(abs(scaled) + 0.5), scaled)) if math.isfinite(scaled) else 0
+            if math.isfinite(scaled) and abs(scaled) - math.floor(abs(scaled)) == 0.5:
+                mult = int(math.copysign(math.floor(abs(scaled)) + 1, scaled))  # llround: ties away from zero
+            rq = math.ldexp(float(mult), -frac)
+            use_int = math.isfinite(real) and abs(real - rq) <= max(1e-12, abs(real) * 1e-12)
+            ydt = _suffix(op.dtype)
+            ip.update({K.QM_USE_INT: int(use_int), K.QM_FRAC_BITS: frac, K.QM_MULT: mult,
+                       K.QM_Y_ZERO: int(self._scalar(op.output_zero_point, "y zero point")),
+                       K.QM_Y_SIGNED: int(ydt == "i8")})
+            fp = {K.QMF_SCALE: float(scale)}
+            y = self._dest(op.output, ydt, tuple(op.output_shape))
+            kern = K.K_QLINEAR_MATMUL
+        else:
+            y = self._dest(op.output, "i32", tuple(op.output_shape))
+            kern = K.K_MATMUL_INTEGER
+        self._b.op(kern, [a, b_, y], ip, fp, label=f"{op.output} ({what})", batched=batched)
+
+    def _emit_QLinearMatMulOp(self, i, op):
+        self._emit_matmul8(op, True)
+
+    def _emit_MatMulIntegerOp(self, i, op):
+        self._emit_matmul8(op, False)
+
+    # ------------------------------------------------------------------ Conv fp32
+    def _emit_ConvOp(self, i, op):
+        if _suffix(op.dtype) != "f32" or int(op.spatial_rank) != 2:
+            raise UnsupportedOpError("Conv: fp32 2-D only")
+        x, w = self._src(op.input0), self._src(op.weights)
+        t_b = self._src(op.bias) if op.bias is not None else -1
+        n, c = int(op.batch), int(op.in_channels)
+        h, wd = op.in_spatial
+        oh, ow = op.out_spatial
+        y = self._dest(op.output, "f32", (n, int(op.out_channels), oh, ow))
+        kh, kw = op.kernel_shape
+        self._b.op(K.K_CONV_F32, [x, w, t_b, y], {
+            K.CF_N: n, K.CF_C: c, K.CF_H: h, K.CF_W: wd, K.CF_OC: int(op.out_channels), K.CF_KH: kh, K.CF_KW: kw,
+            K.CF_OH: oh, K.CF_OW: ow, K.CF_SH: op.strides[0], K.CF_SW: op.strides[1], K.CF_PT: op.pads[0],
+            K.CF_PL: op.pads[1], K.CF_DH: op.dilations[0], K.CF_DW: op.dilations[1], K.CF_GROUP: int(op.group)},
+            label=f"{op.output} (Conv fp32, reference order)",
+            batched=self._batch > 0 and n == self._batch and self._is_batched(op.input0))
+
+    # ------------------------------------------------------------------ Softmax fp32
+    def _emit_SoftmaxOp(self, i, op):
+        if self._dtype(op.input0) != "f32" or getattr(op, "use_legacy_axis_semantics", False):
+            raise UnsupportedOpError("Softmax: fp32 with opset-13 axis semantics only")
+        shape = tuple(self._shape(op.input0))
+        ax = (-1 if op.axis is None else int(op.axis)) % len(shape)
+        outer = int(np.prod(shape[:ax]))
+        inner = int(np.prod(shape[ax + 1:]))
+        x = self._src(op.input0)
+        y = self._dest(op.output, "f32", shape)
+        batched = self._batch > 0 and ax > 0 and shape[0] == self._batch and self._is_batched(op.input0)
+        self._b.op(K.K_SOFTMAX_F32, [x, y], {K.SM_OUTER: outer, K.SM_AXIS: shape[ax], K.SM_INNER: inner,
+                                             K.SM_OUTER_PER_BATCH: outer // self._batch if batched else 0},
+                   label=f"{op.output} (Softmax fp32)", batched=batched)
+
+    # ------------------------------------------------------------------ Quantize / Dequantize
+    def _emit_quant(self, op, quantize: bool):
+        what = "QuantizeLinear" if quantize else "DequantizeLinear"
+        if getattr(op, "block_size", None):
+            raise UnsupportedOpError(f"{what}: blocked quantisation has no B200 kernel")
+        shape = tuple(self._shape(op.input0))
+        qdt = self._dtype(op.output) if quantize else self._dtype(op.input0)
+        if qdt not in ("u8", "i8") or self._dtype(op.scale) != "f32":
+            raise UnsupportedOpError(f"{what}: 8-bit data and fp32 scales only")
+        if (self._dtype(op.input0) if quantize else self._dtype(op.output)) != "f32":
+            raise UnsupportedOpError(f"{what}: fp32 side only")
+        sc = self._const(op.scale, "scale").astype(np.float32).reshape(-1)
+        if sc.size > 1:
+            ax = (1 if op.axis is None else int(op.axis)) % len(shape)
+            axis_len, inner = shape[ax], int(np.prod(shape[ax + 1:]))
+            if sc.size != axis_len:
+                raise UnsupportedOpError(f"{what}: scale length does not match the axis")
+        else:
+            axis_len, inner = 1, 1
+        t_s = self._b.weight(sc, "f32", op.scale)
+        t_z = -1
+        if op.zero_point is not None:
+            z = self._const(op.zero_point, "zero point").reshape(-1)
+            t_z = self._b.weight(z.astype(np.int8 if qdt == "i8" else np.uint8), qdt, op.zero_point)
+        x = self._src(op.input0)
+        y = self._dest(op.output, qdt if quantize else "f32", shape)
+        rows = shape[0] if (shape and self._batch > 0 and shape[0] == self._batch and self._is_batched(op.input0)
+                            and not (axis_len > 1 and (1 if op.axis is None else int(op.axis)) % len(shape) == 0)) else 0
+        self._b.op(K.K_QUANTIZE_LINEAR if quantize else K.K_DEQUANTIZE_LINEAR, [x, t_s, t_z, y],
+                   {K.QL_COUNT: int(np.prod(shape)), K.QL_AXIS_LEN: axis_len, K.QL_INNER: inner,
+                    K.QL_SIGNED: int(qdt == "i8"), K.QL_ROWS: rows}, label=f"{op.output} ({what})", batched=rows > 0)
+
+    def _emit_QuantizeLinearOp(self, i, op):
+        self._emit_quant(op, True)
+
+    def _emit_DequantizeLinearOp(self, i, op):
+        self._emit_quant(op, False)
 
     # ------------------------------------------------------------------ Attention
     def _emit_AttentionOp(self, i, op):

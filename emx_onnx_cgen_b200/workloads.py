@@ -300,6 +300,118 @@ def swish_mul_f16(shape: tuple[int, ...] = (256, 512), alpha: float = 1.0) -> Wo
                     dict(shape=tuple(shape), alpha=alpha))
 
 
+def qlinear_matmul_u8(m: int = 64, k: int = 256, n: int = 128, a_zero: int = 128, b_dtype: str = "i8",
+                      b_zero: int = 0, scales: tuple[float, float, float] = (0.02, 0.005, 0.5),
+                      weight_seed: int = 1) -> Workload:
+    """QLinearMatMul: uint8 A [m,k], int8/uint8 B [k,n] initializer, uint8 output (zero point
+    10); scales (a, b, y) per tensor -- powers of two make the multiplier exact, which selects
+    the reference's integer requantisation."""
+    rng = np.random.default_rng(weight_seed)
+    npt = np.int8 if b_dtype == "i8" else np.uint8
+    lo, hi = (-127, 128) if b_dtype == "i8" else (0, 256)
+    inits = {"B": rng.integers(lo, hi, (k, n)).astype(npt),
+             "a_s": _scalar(scales[0], np.float32), "a_z": _scalar(a_zero, np.uint8),
+             "b_s": _scalar(scales[1], np.float32), "b_z": _scalar(b_zero, npt),
+             "y_s": _scalar(scales[2], np.float32), "y_z": _scalar(10, np.uint8)}
+    g = GraphSpec(
+        name="qlinear_matmul_u8",
+        inputs=[TensorSpec("A", "u8", (m, k))],
+        outputs=[TensorSpec("Y", "u8", (m, n))],
+        nodes=[NodeSpec("QLinearMatMul", "qmm", ("A", "a_s", "a_z", "B", "b_s", "b_z", "y_s", "y_z"), ("Y",))],
+        initializers=inits, opset_imports=(("", 10),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"A": np.random.default_rng(seed).integers(0, 256, (m, k)).astype(np.uint8)}
+
+    return Workload("qlinear_matmul_u8", g, make_inputs, {"A": 0, "Y": 0},
+                    dict(m=m, k=k, n=n, a_zero=a_zero, b_dtype=b_dtype, b_zero=b_zero, scales=tuple(scales)))
+
+
+def matmul_integer_u8(m: int = 64, k: int = 256, n: int = 128, a_zero: int = 128, b_zero: int = 3,
+                      weight_seed: int = 1) -> Workload:
+    """MatMulInteger: uint8 A [m,k], int8 B [k,n] initializer, scalar zero points, int32 output."""
+    rng = np.random.default_rng(weight_seed)
+    inits = {"B": rng.integers(-127, 128, (k, n)).astype(np.int8),
+             "a_z": _scalar(a_zero, np.uint8), "b_z": _scalar(b_zero, np.int8)}
+    g = GraphSpec(
+        name="matmul_integer_u8",
+        inputs=[TensorSpec("A", "u8", (m, k))],
+        outputs=[TensorSpec("Y", "i32", (m, n))],
+        nodes=[NodeSpec("MatMulInteger", "mmi", ("A", "B", "a_z", "b_z"), ("Y",))],
+        initializers=inits, opset_imports=(("", 10),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"A": np.random.default_rng(seed).integers(0, 256, (m, k)).astype(np.uint8)}
+
+    return Workload("matmul_integer_u8", g, make_inputs, {"A": 0, "Y": 0}, dict(m=m, k=k, n=n))
+
+
+def conv_f32(batch: int = 2, cin: int = 8, cout: int = 16, h: int = 12, w: int = 12, kernel: int = 3,
+             stride: int = 1, pad: int = 1, dilation: int = 1, group: int = 1, weight_seed: int = 1) -> Workload:
+    """fp32 Conv 2-D with bias."""
+    rng = np.random.default_rng(weight_seed)
+    inits = {"W": rng.standard_normal((cout, cin // group, kernel, kernel)).astype(np.float32) * np.float32(0.1),
+             "bias": rng.uniform(-0.1, 0.1, cout).astype(np.float32)}
+    oh = (h + 2 * pad - dilation * (kernel - 1) - 1) // stride + 1
+    ow = (w + 2 * pad - dilation * (kernel - 1) - 1) // stride + 1
+    g = GraphSpec(
+        name="conv_f32",
+        inputs=[TensorSpec("X", "f32", (batch, cin, h, w))],
+        outputs=[TensorSpec("Y", "f32", (batch, cout, oh, ow))],
+        nodes=[NodeSpec("Conv", "conv", ("X", "W", "bias"), ("Y",),
+                        {"kernel_shape": [kernel, kernel], "pads": [pad] * 4, "strides": [stride] * 2,
+                         "dilations": [dilation] * 2, "group": group})],
+        initializers=inits, opset_imports=(("", 17),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"X": np.random.default_rng(seed).standard_normal((batch, cin, h, w)).astype(np.float32)}
+
+    return Workload("conv_f32", g, make_inputs, {"X": 0, "Y": 0},
+                    dict(batch=batch, cin=cin, cout=cout, h=h, w=w, kernel=kernel, stride=stride, pad=pad,
+                         dilation=dilation, group=group))
+
+
+def softmax_f32(shape: tuple[int, ...] = (32, 1000), axis: int = -1) -> Workload:
+    """Softmax over one axis, fp32 inputs ~N(0, 4)."""
+    g = GraphSpec(
+        name="softmax_f32",
+        inputs=[TensorSpec("X", "f32", tuple(shape))],
+        outputs=[TensorSpec("Y", "f32", tuple(shape))],
+        nodes=[NodeSpec("Softmax", "sm", ("X",), ("Y",), {"axis": axis})],
+        initializers={}, opset_imports=(("", 13),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"X": (2 * np.random.default_rng(seed).standard_normal(shape)).astype(np.float32)}
+
+    return Workload("softmax_f32", g, make_inputs, {"X": 0, "Y": 0}, dict(shape=tuple(shape), axis=axis))
+
+
+def quant_dequant(shape: tuple[int, ...] = (16, 64), out_dtype: str = "u8", zero: int = 7,
+                  scale: float = 0.03) -> Workload:
+    """QuantizeLinear (fp32 -> u8/i8, per-tensor scale and zero point) followed by
+    DequantizeLinear back to fp32; both results are graph outputs."""
+    npt = np.uint8 if out_dtype == "u8" else np.int8
+    inits = {"s": _scalar(scale, np.float32), "z": _scalar(zero, npt)}
+    g = GraphSpec(
+        name="quant_dequant",
+        inputs=[TensorSpec("X", "f32", tuple(shape))],
+        outputs=[TensorSpec("Q", out_dtype, tuple(shape)), TensorSpec("D", "f32", tuple(shape))],
+        nodes=[NodeSpec("QuantizeLinear", "q", ("X", "s", "z"), ("Q",)),
+               NodeSpec("DequantizeLinear", "dq", ("Q", "s", "z"), ("D",))],
+        initializers=inits, opset_imports=(("", 13),),
+    )
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"X": (3 * np.random.default_rng(seed).standard_normal(shape)).astype(np.float32)}
+
+    return Workload("quant_dequant", g, make_inputs, {"X": 0, "Q": 0, "D": 0},
+                    dict(shape=tuple(shape), out_dtype=out_dtype, zero=zero, scale=scale))
+
+
 BUILDERS = {
     "mlp_fp32": mlp_fp32,
     "qconv_stack_int8": qconv_stack_int8,
@@ -308,4 +420,9 @@ BUILDERS = {
     "lstm_fp32": lstm_fp32,
     "matmul_nbits_f16": matmul_nbits_f16,
     "swish_mul_f16": swish_mul_f16,
+    "qlinear_matmul_u8": qlinear_matmul_u8,
+    "matmul_integer_u8": matmul_integer_u8,
+    "conv_f32": conv_f32,
+    "softmax_f32": softmax_f32,
+    "quant_dequant": quant_dequant,
 }

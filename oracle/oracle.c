@@ -370,3 +370,155 @@ void orc_lstm_f32(const float *x, const float *w, const float *r, const float *b
     memcpy(y_c, c_prev, sizeof(float) * (size_t)batch * H);
     free(h_prev); free(c_prev); free(h_next); free(c_next);
 }
+
+/* ---------------------------------------------------------------------------
+ * QLinearMatMul, 2-D B, per-tensor parameters, f32 scales (ir/ops/nn.py:
+ * 710-769, templates/qlinear_matmul_op.c.j2:1-81): int32 accumulation of
+ * (a - za) * (b - zb); if the double multiplier s_a*s_b/s_y is representable
+ * in 31 fractional bits (within 1e-12) the integer path rounds
+ * acc*multiplier >> frac_bits half-to-even, else (double)acc * (double)scale
+ * + zy is rounded by llrint, scale being the float expression s_a*s_b/s_y.
+ * ------------------------------------------------------------------------- */
+void orc_qlinear_matmul(const uint8_t *a, int a_signed, const uint8_t *b, int b_signed, float sa, int za,
+                        float sb, int zb, float sy, int zy, int y_signed, int m, int k, int n, uint8_t *y)
+{
+    const float scale = ((float)sa) * ((float)sb) / ((float)sy);
+    const double real_multiplier = ((double)sa) * ((double)sb) / ((double)sy);
+    int frac_bits = 31;
+    double scaled_multiplier = ldexp(real_multiplier, frac_bits);
+    while (frac_bits > 0 && fabs(scaled_multiplier) > (double)INT32_MAX) {
+        --frac_bits;
+        scaled_multiplier = ldexp(real_multiplier, frac_bits);
+    }
+    const int64_t mult = (int64_t)llround(scaled_multiplier);
+    const double rq_scale = ldexp((double)mult, -frac_bits);
+    const double err = fabs(real_multiplier - rq_scale);
+    const double tol = fmax(1e-12, fabs(real_multiplier) * 1e-12);
+    const int use_int = isfinite(real_multiplier) && err <= tol;
+    const uint64_t mask = frac_bits > 0 ? (((uint64_t)1u << frac_bits) - 1u) : 0u;
+    const uint64_t half = frac_bits > 0 ? ((uint64_t)1u << (frac_bits - 1)) : 0u;
+    const int64_t lo = y_signed ? -128 : 0, hi = y_signed ? 127 : 255;
+    for (int i = 0; i < m; ++i) {
+        for (int j = 0; j < n; ++j) {
+            int32_t acc = 0;
+            for (int kk = 0; kk < k; ++kk) {
+                const int32_t av = a_signed ? (int32_t)(int8_t)a[(size_t)i * k + kk] : (int32_t)a[(size_t)i * k + kk];
+                const int32_t bv = b_signed ? (int32_t)(int8_t)b[(size_t)kk * n + j] : (int32_t)b[(size_t)kk * n + j];
+                acc += (av - za) * (bv - zb);
+            }
+            int64_t q;
+            if (use_int) {
+                int64_t r = (int64_t)acc * mult;
+                if (frac_bits > 0) {
+                    uint64_t mag = r < 0 ? (uint64_t)(-r) : (uint64_t)r;
+                    uint64_t quo = mag >> frac_bits, rem = mag & mask;
+                    if (rem > half || (rem == half && (quo & 1u))) ++quo;
+                    r = r < 0 ? -(int64_t)quo : (int64_t)quo;
+                }
+                q = r + (int64_t)zy;
+            } else {
+                const double scaled = ((double)acc) * (double)scale + (double)zy;
+                q = (int64_t)llrint(scaled);
+            }
+            if (q < lo) q = lo; else if (q > hi) q = hi;
+            y[(size_t)i * n + j] = (uint8_t)(int8_t)q;
+        }
+    }
+}
+
+/* MatMulInteger (templates/matmul_integer_op.c.j2): int32 sum of (a - za) * (b - zb). */
+void orc_matmul_integer(const uint8_t *a, int a_signed, const uint8_t *b, int b_signed, int za, int zb,
+                        int m, int k, int n, int32_t *y)
+{
+    for (int i = 0; i < m; ++i)
+        for (int j = 0; j < n; ++j) {
+            int32_t acc = 0;
+            for (int kk = 0; kk < k; ++kk) {
+                const int32_t av = a_signed ? (int32_t)(int8_t)a[(size_t)i * k + kk] : (int32_t)a[(size_t)i * k + kk];
+                const int32_t bv = b_signed ? (int32_t)(int8_t)b[(size_t)kk * n + j] : (int32_t)b[(size_t)kk * n + j];
+                acc += (av - za) * (bv - zb);
+            }
+            y[(size_t)i * n + j] = acc;
+        }
+}
+
+/* Conv fp32, 2-D (templates/conv_op.c.j2): acc = bias (or 0); in-bounds taps
+ * in (ic, kh, kw) order: acc += x * w. */
+void orc_conv2d_f32(const float *x, const float *w, const float *bias, int n, int c, int h, int wd, int oc,
+                    int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int group, int oh, int ow,
+                    float *y)
+{
+    const int gic = c / group, goc = oc / group;
+    for (int b = 0; b < n; ++b)
+        for (int g = 0; g < group; ++g)
+            for (int o = 0; o < goc; ++o) {
+                const int og = g * goc + o;
+                for (int yy = 0; yy < oh; ++yy)
+                    for (int xx = 0; xx < ow; ++xx) {
+                        float acc = bias ? bias[og] : 0.0f;
+                        for (int ic = 0; ic < gic; ++ic) {
+                            const int icg = g * gic + ic;
+                            for (int a = 0; a < kh; ++a)
+                                for (int bb = 0; bb < kw; ++bb) {
+                                    const int iy = yy * sh + a * dh - pt, ix = xx * sw + bb * dw - pl;
+                                    if (iy >= 0 && iy < h && ix >= 0 && ix < wd)
+                                        acc += x[(((size_t)b * c + icg) * h + iy) * wd + ix] *
+                                               w[(((size_t)og * gic + ic) * kh + a) * kw + bb];
+                                }
+                        }
+                        y[(((size_t)b * oc + og) * oh + yy) * ow + xx] = acc;
+                    }
+            }
+}
+
+/* Softmax fp32 over one axis (templates/softmax_op.c.j2): fmaxf chain, expf,
+ * sequential float sum, division. */
+void orc_softmax_f32(const float *x, float *y, long outer, long axis, long inner)
+{
+    for (long o = 0; o < outer; ++o)
+        for (long i = 0; i < inner; ++i) {
+            const long base = o * axis * inner + i;
+            float mx = x[base];
+            for (long a = 1; a < axis; ++a) mx = fmaxf(mx, x[base + a * inner]);
+            float sum = 0;
+            for (long a = 0; a < axis; ++a) {
+                const float v = expf(x[base + a * inner] - mx);
+                y[base + a * inner] = v;
+                sum += v;
+            }
+            for (long a = 0; a < axis; ++a) y[base + a * inner] /= sum;
+        }
+}
+
+/* QuantizeLinear fp32 -> 8-bit (templates/quantize_linear_op.c.j2): scale and
+ * zero point per tensor (axis_len 1) or per index along an axis. */
+void orc_quantize_linear(const float *x, const float *scale, const uint8_t *zp, int zp_signed, int y_signed,
+                         long outer, long axis_len, long inner, uint8_t *y)
+{
+    const float lo = y_signed ? (float)INT8_MIN : 0.0f, hi = y_signed ? (float)INT8_MAX : (float)UINT8_MAX;
+    for (long o = 0; o < outer; ++o)
+        for (long a = 0; a < axis_len; ++a)
+            for (long i = 0; i < inner; ++i) {
+                const long idx = (o * axis_len + a) * inner + i;
+                const float z = zp ? (zp_signed ? (float)(int8_t)zp[a] : (float)zp[a]) : 0.0f;
+                const float scaled = x[idx] / scale[a];
+                float r = nearbyintf(scaled) + z;
+                r = fmaxf(r, lo);
+                r = fminf(r, hi);
+                y[idx] = y_signed ? (uint8_t)(int8_t)r : (uint8_t)r;
+            }
+}
+
+/* DequantizeLinear 8-bit -> fp32 (templates/dequantize_linear_op.c.j2). */
+void orc_dequantize_linear(const uint8_t *x, int x_signed, const float *scale, const uint8_t *zp,
+                           long outer, long axis_len, long inner, float *y)
+{
+    for (long o = 0; o < outer; ++o)
+        for (long a = 0; a < axis_len; ++a)
+            for (long i = 0; i < inner; ++i) {
+                const long idx = (o * axis_len + a) * inner + i;
+                const float xv = x_signed ? (float)(int8_t)x[idx] : (float)x[idx];
+                const float z = zp ? (x_signed ? (float)(int8_t)zp[a] : (float)zp[a]) : 0.0f;
+                y[idx] = (xv - z) * scale[a];
+            }
+}

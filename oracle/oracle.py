@@ -169,6 +169,89 @@ def lstm_f32(x, w, r, bias):
 
 
 # ------------------------------------------------------------------ graph runner
+def _u8(a):
+    a = np.ascontiguousarray(a)
+    return a.view(np.uint8), int(a.dtype == np.int8)
+
+
+def qlinear_matmul(a, sa, za, b, sb, zb, sy, zy):
+    a8, a_s = _u8(a)
+    b8, b_s = _u8(b)
+    m = int(np.prod(a.shape[:-1])) if a.ndim > 1 else 1
+    k, n = a.shape[-1], b.shape[1]
+    y_signed = int(np.asarray(zy).dtype == np.int8)
+    y = np.zeros((*a.shape[:-1], n), np.int8 if y_signed else np.uint8)
+    f = lambda v: float(np.asarray(v, np.float32).reshape(-1)[0])
+    i = lambda v: int(np.asarray(v).reshape(-1)[0])
+    lib().orc_qlinear_matmul(_p(a8), _i(a_s), _p(b8), _i(b_s), _f(f(sa)), _i(i(za)), _f(f(sb)), _i(i(zb)),
+                             _f(f(sy)), _i(i(zy)), _i(y_signed), _i(m), _i(k), _i(n), _p(y.view(np.uint8)))
+    return y
+
+
+def matmul_integer(a, b, za=None, zb=None):
+    a8, a_s = _u8(a)
+    b8, b_s = _u8(b)
+    m = int(np.prod(a.shape[:-1])) if a.ndim > 1 else 1
+    k, n = a.shape[-1], b.shape[1]
+    y = np.zeros((*a.shape[:-1], n), np.int32)
+    i = lambda v: 0 if v is None else int(np.asarray(v).reshape(-1)[0])
+    lib().orc_matmul_integer(_p(a8), _i(a_s), _p(b8), _i(b_s), _i(i(za)), _i(i(zb)), _i(m), _i(k), _i(n), _p(y))
+    return y
+
+
+def conv2d_f32(x, w, bias, strides, pads, dilations, group):
+    x = np.ascontiguousarray(x, np.float32); w = np.ascontiguousarray(w, np.float32)
+    n, c, h, wd = x.shape
+    oc, _, kh, kw = w.shape
+    oh = (h + pads[0] + pads[2] - ((kh - 1) * dilations[0] + 1)) // strides[0] + 1
+    ow = (wd + pads[1] + pads[3] - ((kw - 1) * dilations[1] + 1)) // strides[1] + 1
+    y = np.zeros((n, oc, oh, ow), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().orc_conv2d_f32(_p(x), _p(w), _p(b), _i(n), _i(c), _i(h), _i(wd), _i(oc), _i(kh), _i(kw),
+                         _i(strides[0]), _i(strides[1]), _i(pads[0]), _i(pads[1]), _i(dilations[0]),
+                         _i(dilations[1]), _i(group), _i(oh), _i(ow), _p(y))
+    return y
+
+
+def softmax_f32(x, axis=-1):
+    x = np.ascontiguousarray(x, np.float32)
+    ax = axis % x.ndim
+    outer = int(np.prod(x.shape[:ax])); inner = int(np.prod(x.shape[ax + 1:]))
+    y = np.zeros_like(x)
+    lib().orc_softmax_f32(_p(x), _p(y), ctypes.c_long(outer), ctypes.c_long(x.shape[ax]), ctypes.c_long(inner))
+    return y
+
+
+def _axis_split(shape, scale, axis):
+    if np.asarray(scale).size == 1:
+        return int(np.prod(shape)), 1, 1
+    ax = (1 if axis is None else axis) % len(shape)
+    return int(np.prod(shape[:ax])), shape[ax], int(np.prod(shape[ax + 1:]))
+
+
+def quantize_linear(x, scale, zp=None, axis=None):
+    x = np.ascontiguousarray(x, np.float32)
+    sc = np.ascontiguousarray(np.asarray(scale, np.float32).reshape(-1))
+    outer, alen, inner = _axis_split(x.shape, sc, axis)
+    zdt = np.uint8 if zp is None else np.asarray(zp).dtype
+    z8 = None if zp is None else np.ascontiguousarray(np.asarray(zp).reshape(-1)).view(np.uint8)
+    y = np.zeros(x.shape, zdt)
+    lib().orc_quantize_linear(_p(x), _p(sc), _p(z8), _i(zdt == np.int8), _i(zdt == np.int8), ctypes.c_long(outer),
+                              ctypes.c_long(alen), ctypes.c_long(inner), _p(y.view(np.uint8)))
+    return y
+
+
+def dequantize_linear(x, scale, zp=None, axis=None):
+    x8, xs = _u8(x)
+    sc = np.ascontiguousarray(np.asarray(scale, np.float32).reshape(-1))
+    outer, alen, inner = _axis_split(x.shape, sc, axis)
+    z8 = None if zp is None else np.ascontiguousarray(np.asarray(zp).reshape(-1)).view(np.uint8)
+    y = np.zeros(x.shape, np.float32)
+    lib().orc_dequantize_linear(_p(x8), _i(xs), _p(sc), _p(z8), ctypes.c_long(outer), ctypes.c_long(alen),
+                                ctypes.c_long(inner), _p(y))
+    return y
+
+
 def run_graph(spec: GraphSpec, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
     env: dict[str, np.ndarray] = dict(spec.initializers)
     env.update(inputs)
@@ -206,6 +289,22 @@ def run_graph(spec: GraphSpec, inputs: dict[str, np.ndarray]) -> dict[str, np.nd
             res = [sigmoid_f16(ins[0]) if ins[0].dtype == np.float16 else sigmoid_f32(ins[0])]
         elif op == "Mul":
             res = [mul_f16(ins[0], ins[1]) if ins[0].dtype == np.float16 else mul_f32(ins[0], ins[1])]
+        elif op == "QLinearMatMul":
+            res = [qlinear_matmul(*ins[:8])]
+        elif op == "MatMulInteger":
+            res = [matmul_integer(ins[0], ins[1], ins[2] if len(ins) > 2 else None,
+                                  ins[3] if len(ins) > 3 else None)]
+        elif op == "Conv":
+            rank = ins[0].ndim - 2
+            res = [conv2d_f32(ins[0], ins[1], ins[2] if len(ins) > 2 else None,
+                              tuple(a.get("strides", [1] * rank)), tuple(a.get("pads", [0] * 2 * rank)),
+                              tuple(a.get("dilations", [1] * rank)), int(a.get("group", 1)))]
+        elif op == "Softmax":
+            res = [softmax_f32(ins[0], int(a.get("axis", -1)))]
+        elif op == "QuantizeLinear":
+            res = [quantize_linear(ins[0], ins[1], ins[2] if len(ins) > 2 else None, a.get("axis"))]
+        elif op == "DequantizeLinear":
+            res = [dequantize_linear(ins[0], ins[1], ins[2] if len(ins) > 2 else None, a.get("axis"))]
         elif op == "Attention":
             res = [attention_f16(ins[0], ins[1], ins[2], a.get("scale"), bool(a.get("is_causal", 0)))]
         elif op == "LSTM":

@@ -56,6 +56,16 @@ CASES = [
     ("nbits1_m2_k256_n16_b128", "matmul_nbits_f16", dict(m=2, k=256, n=16, block=128), 2),
     ("swishmul_8x24", "swish_mul_f16", dict(shape=(8, 24)), 0),
     ("swishmul_5x16_alpha1702", "swish_mul_f16", dict(shape=(5, 16), alpha=1.702), 1),
+    ("qmm_m5_k40_n24", "qlinear_matmul_u8", dict(m=5, k=40, n=24), 0),
+    ("qmm_m3_k17_n9_u8b", "qlinear_matmul_u8", dict(m=3, k=17, n=9, a_zero=100, b_dtype="u8", b_zero=120), 1),
+    ("qmm_m4_k20_n7_intrequant", "qlinear_matmul_u8", dict(m=4, k=20, n=7, scales=(0.5, 0.25, 4.0)), 2),
+    ("mmi_m4_k33_n10", "matmul_integer_u8", dict(m=4, k=33, n=10), 0),
+    ("conv_b2_c4_9x7_s2", "conv_f32", dict(batch=2, cin=4, cout=6, h=9, w=7, stride=2, pad=1), 0),
+    ("conv_b1_c4_8x8_g2_d2", "conv_f32", dict(batch=1, cin=4, cout=4, h=8, w=8, pad=2, dilation=2, group=2), 1),
+    ("softmax_4x37", "softmax_f32", dict(shape=(4, 37)), 0),
+    ("softmax_3x5x6_axis1", "softmax_f32", dict(shape=(3, 5, 6), axis=1), 1),
+    ("qdq_u8_6x11", "quant_dequant", dict(shape=(6, 11)), 0),
+    ("qdq_i8_4x9", "quant_dequant", dict(shape=(4, 9), out_dtype="i8", zero=-3, scale=0.05), 1),
 ]
 
 

@@ -1,0 +1,80 @@
+"""QLinearMatMul, MatMulInteger, fp32 Conv, fp32 Softmax and
+Quantize/DequantizeLinear on the B200 kernels, against the reference's
+generated C (golden fixtures) and the CPU restatement.
+
+Bars: bit-exact for every op except Softmax, whose reference calls glibc's
+expf (CUDA's differs by at most 2 ulp, glibc's by up to 0.502 ulp from the
+exact value); Softmax outputs must agree within SOFTMAX_MAX_ULP fp32 ULP
+(reference metric, shared/ulp.py:26-50, atol 1 eps)."""
+import numpy as np
+import pytest
+
+from emx_onnx_cgen_b200 import workloads as W
+from emx_onnx_cgen_b200.runtime import Session
+from emx_onnx_cgen_b200.spec import GraphSpec, NodeSpec, TensorSpec
+from golden_util import cases, load
+from gpu_util import assert_bitexact, plan_for, require_gpu, ulp_diff_f32
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+SOFTMAX_MAX_ULP = 8
+EXACT = ("qmm", "mmi", "conv", "qdq")
+
+
+@pytest.mark.parametrize("name", sorted(n for n in cases() if n.startswith(EXACT + ("softmax",))))
+def test_golden(name):
+    require_gpu()
+    wl, inputs, ref = load(name)
+    out = Session(plan_for(wl)).run(inputs)
+    for k, v in ref.items():
+        if name.startswith("softmax"):
+            assert int(ulp_diff_f32(out[k], v).max(initial=0)) <= SOFTMAX_MAX_ULP, name
+        else:
+            assert_bitexact(out[k], v, f"{name}:{k}")
+
+
+@pytest.mark.parametrize("wl", [
+    W.qlinear_matmul_u8(m=300, k=513, n=130),
+    W.qlinear_matmul_u8(m=7, k=64, n=33, a_zero=3, b_dtype="u8", b_zero=200, scales=(0.25, 0.125, 0.5)),
+    W.matmul_integer_u8(m=129, k=1000, n=65, a_zero=0, b_zero=-5),
+    W.conv_f32(batch=3, cin=16, cout=24, h=20, w=17, kernel=3, stride=2, pad=1),
+    W.conv_f32(batch=1, cin=6, cout=6, h=11, w=11, kernel=5, pad=4, dilation=2, group=3),
+    W.quant_dequant((33, 70), out_dtype="i8", zero=5, scale=0.01),
+], ids=lambda w: w.name + str(sorted(w.params.items()))[:60])
+def test_exact_vs_port(wl):
+    require_gpu()
+    x = wl.make_inputs(4)
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan_for(wl)).run(x)
+    for k, v in ref.items():
+        assert_bitexact(out[k], v, k)
+
+
+@pytest.mark.parametrize("shape,axis", [((64, 1000), -1), ((8, 300, 5), 1), ((2, 3, 4, 50), 3), ((1, 1), 0)])
+def test_softmax_vs_port(shape, axis):
+    require_gpu()
+    wl = W.softmax_f32(shape, axis)
+    x = wl.make_inputs(2)
+    flat = x["X"].reshape(-1)
+    flat[:3] = np.array([30.0, -50.0, 0.0], np.float32)[:flat.size]
+    ref = oracle.run_graph(wl.graph, x)["Y"]
+    out = Session(plan_for(wl)).run(x)["Y"]
+    assert int(ulp_diff_f32(out, ref).max(initial=0)) <= SOFTMAX_MAX_ULP
+
+
+def test_quantize_per_axis_and_specials():
+    require_gpu()
+    shape = (3, 4, 10)
+    g = GraphSpec("qax", [TensorSpec("X", "f32", shape)], [TensorSpec("Q", "u8", shape), TensorSpec("D", "f32", shape)],
+                  [NodeSpec("QuantizeLinear", "q", ("X", "s", "z"), ("Q",), {"axis": 1}),
+                   NodeSpec("DequantizeLinear", "dq", ("Q", "s", "z"), ("D",), {"axis": 1})],
+                  {"s": np.array([0.1, 0.02, 0.5, 3.0], np.float32), "z": np.array([0, 100, 128, 255], np.uint8)},
+                  opset_imports=(("", 13),))
+    wl = W.Workload("qax", g, lambda seed=0: {}, {"X": 0, "Q": 0, "D": 0}, {})
+    x = (np.random.default_rng(0).standard_normal(shape) * 20).astype(np.float32)
+    x[0, 0, :6] = [np.inf, -np.inf, np.nan, 0.05, 0.15, -0.25]   # ties at .5 round to even
+    ref = oracle.run_graph(g, {"X": x})
+    out = Session(plan_for(wl)).run({"X": x})
+    for k in ("Q", "D"):
+        assert_bitexact(out[k], ref[k], k)
