@@ -39,7 +39,8 @@ enum KernelId : uint32_t {
 enum { PAD_N, PAD_C, PAD_H, PAD_W, PAD_TOP, PAD_LEFT, PAD_HP, PAD_WP, PAD_XOR, PAD_ROWS };
 
 // ---- K_QCONV_TC: t[0]=x (planar), t[1]=w image, t[2]=epilogue table
-//      (float scale[OC], int32 bias[OC]), t[3]=residual (planar) or -1, t[4]=y
+//      (float scale[OC], int32 bias[OC]), t[3]=residual (planar) or -1, t[4]=y,
+//      t[5]=fused-add table [conv byte][residual byte] -> output byte, or -1
 enum {
   QC_N, QC_CIN, QC_OC, QC_KH, QC_KW, QC_HP, QC_WP, QC_OH, QC_OW, QC_A_SIGNED, QC_Y_ZERO,
   QC_Y_LAYOUT /*0 planar, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,

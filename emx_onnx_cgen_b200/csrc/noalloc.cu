@@ -166,7 +166,8 @@ extern "C" int emx_b200_qlinear_conv3x3_noalloc(const uint8_t* x, const int8_t* 
   pad.ip[PAD_ROWS] = rows;
   PlanOp conv{};
   conv.kernel = K_QCONV_TC;
-  conv.n_tensors = 5;
+  conv.n_tensors = 6;
+  conv.t[5] = -1;  // no fused add
   conv.t[0] = 1;
   conv.t[1] = 2;
   conv.t[2] = 3;

@@ -68,7 +68,16 @@ struct QConvTcParams {
   int has_add, fast_div;
   float c_scale, r_scale, add_scale, add_inv_scale, add_zero, c_zero, r_zero, add_lo, add_hi;
   int r_xor, r_signed, r_hp, r_wp, r_pt, r_pl;
+  // residual rows of a tile are contiguous when the residual has the input's
+  // padded geometry: row q + r_off for pitched row q; they are then staged in
+  // shared memory by one bulk copy per tile (r_bulk)
+  int r_bulk;
+  int64_t r_off;
+  // fused add by table: out byte = lut[(conv byte << 8) | residual byte], staged in shared memory
+  const uint8_t* lut;
 };
+
+constexpr int QC_RSTAGES = 3;  // residual ring depth (tiles)
 
 // Warp roles: warp 0 producer, warps 1..2 MMA issuers (one partial
 // accumulator each: one issuing thread completes a tcgen05.mma every ~150
@@ -145,7 +154,8 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_b = smem;
-  uint8_t* s_a = smem + align_up_dev(p.b_bytes, 1024);
+  uint8_t* s_lut = smem + align_up_dev(p.b_bytes, 1024);  // 64 KB when p.lut
+  uint8_t* s_a = s_lut + (p.lut ? 65536 : 0);
   float* s_scale = reinterpret_cast<float*>(s_a + (size_t)p.stages * p.stage_bytes);
   int32_t* s_bias = reinterpret_cast<int32_t*>(s_scale + OC);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_bias + OC);
@@ -155,7 +165,11 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
   uint64_t* acce = accf + 2;
   uint64_t* bbar = acce + 2;
   uint64_t* drain = bbar + 1;  // one per MMA warp
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + QC_MMA_WARPS);
+  uint64_t* rfull = drain + QC_MMA_WARPS;
+  uint64_t* rempty = rfull + QC_RSTAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + QC_RSTAGES);
+  // residual ring after the barrier block (16-byte aligned)
+  uint8_t* s_r = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_holder + 4) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -176,6 +190,10 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
     }
     mbar_init(bbar, 1);
     for (int w = 0; w < QC_MMA_WARPS; ++w) mbar_init(&drain[w], 1);
+    for (int r = 0; r < QC_RSTAGES; ++r) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], QC_EPI_WARPS);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -197,11 +215,13 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: weights once, then one window per tile
-      mbar_arrive_expect_tx(bbar, p.b_bytes);
+      mbar_arrive_expect_tx(bbar, p.b_bytes + (p.lut ? 65536u : 0u));
       for (uint32_t off = 0; off < p.b_bytes; off += 16384u) {
         const uint32_t n = min(16384u, p.b_bytes - off);
         bulk_load(s_b + off, p.w_img + off, n, bbar);
       }
+      if (p.lut)
+        for (uint32_t off = 0; off < 65536u; off += 16384u) bulk_load(s_lut + off, p.lut + off, 16384u, bbar);
       pdl_wait();  // activations come from the preceding kernel
       int stage = 0;
       uint32_t phase = 0;
@@ -282,6 +302,33 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
         (void)mbar_wait(&drain[my], 0, nullptr, 0);
       }
     }
+  } else if (warp == 3) {
+    if (lane == 0 && p.has_add && p.r_bulk) {
+      // ---------------- residual producer: the tile's residual rows, one bulk copy each
+      pdl_wait();  // the residual may come from the preceding kernel
+      int rs = 0;
+      uint32_t rph = 0, issued = 0, parity_of = 0;
+      bool ok = true;
+      const uint32_t rbytes = (uint32_t)QC_TILE_M * OC;
+      for (int tile = t_begin; tile < t_end; ++tile) {
+        if (!mbar_wait(&rempty[rs], rph ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&rfull[rs], rbytes);
+        bulk_load(s_r + (size_t)rs * rbytes, p.resid + (uint64_t)((int64_t)tile * QC_TILE_M + p.r_off) * OC, rbytes,
+                  &rfull[rs]);
+        issued |= 1u << rs;
+        parity_of = (parity_of & ~(1u << rs)) | (rph << rs);
+        if (++rs == QC_RSTAGES) {
+          rs = 0;
+          rph ^= 1u;
+        }
+      }
+      if (!ok)
+        for (int s2 = 0; s2 < QC_RSTAGES; ++s2)
+          if (issued & (1u << s2)) (void)mbar_wait(&rfull[s2], (parity_of >> s2) & 1u, nullptr, 0);
+    }
   } else if (warp >= QC_EPI_WARP0) {
     // ---------------- epilogue: TMEM -> registers -> requant (+ QLinearAdd) -> global
     const int quarter = warp & 3;
@@ -290,6 +337,9 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
     const int64_t hpwp = (int64_t)p.hp * p.wp;
     const uint32_t yx4 = (uint32_t)p.y_xor * 0x01010101u;
     pdl_wait();  // residual reads and output writes follow the preceding kernel
+    if (p.lut && !__all_sync(0xffffffffu, mbar_wait(bbar, 0, p.err, DEV_TIMEOUT_EPILOGUE))) {
+      // the add table never arrived (an error is recorded); nothing to do
+    } else {
     int it = 0;
     for (int tile = t_begin; tile < t_end; ++tile, ++it) {
       __syncwarp();
@@ -313,6 +363,12 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[acc]);
+      const bool rb_on = p.has_add && p.r_bulk;
+      const int rs = it % QC_RSTAGES;
+      if (rb_on) {
+        ok = mbar_wait(&rfull[rs], (uint32_t)(it / QC_RSTAGES) & 1u, p.err, DEV_TIMEOUT_EPILOGUE);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
       uint32_t v[G];
 #pragma unroll
       for (int c = 0; c < G; ++c) {
@@ -330,8 +386,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       const int rem = (int)(q - (uint32_t)n * (uint32_t)hpwp);
       const int oh = (int)(((uint64_t)(uint32_t)rem * p.wp_mul) >> 40);
       const int ow = rem - oh * p.wp;
-      if (n >= p.batch || oh >= p.oh || ow >= p.ow) continue;
-
+      if (n < p.batch && oh < p.oh && ow < p.ow) {
       float r[G];
 #pragma unroll
       for (int c4 = 0; c4 < G / 4; ++c4) {
@@ -344,7 +399,44 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       }
       if (p.has_add) {
         uint32_t rb[G / 4];
-        qc_load_resid<OC, G>(p, rb, col0, n, oh, ow);
+        if (p.r_bulk) {
+          const uint8_t* rrow = s_r + ((size_t)rs * QC_TILE_M + row) * OC;
+          const int64_t rpix = (int64_t)q + p.r_off;
+          if constexpr (G == 8) {
+            const uint2 t = *reinterpret_cast<const uint2*>(rrow + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
+            rb[0] = t.x;
+            rb[1] = t.y;
+          } else {
+#pragma unroll
+            for (int c = 0; c < G / 16; ++c) {
+              const uint4 t = *reinterpret_cast<const uint4*>(rrow + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
+              rb[4 * c + 0] = t.x;
+              rb[4 * c + 1] = t.y;
+              rb[4 * c + 2] = t.z;
+              rb[4 * c + 3] = t.w;
+            }
+          }
+        } else {
+          qc_load_resid<OC, G>(p, rb, col0, n, oh, ow);
+        }
+        if (p.lut) {
+          // out byte = table[(conv byte << 8) | residual byte]
+          uint32_t out[G / 4];
+#pragma unroll
+          for (int c4 = 0; c4 < G / 4; ++c4) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int c = 4 * c4 + j;
+              const uint32_t ab = float_to_byte(r[c]);
+              const uint32_t bb = ((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu;
+              word |= (uint32_t)s_lut[(ab << 8) | bb] << (8 * j);
+            }
+            out[c4] = word ^ yx4;
+          }
+          qc_store<OC, G>(p, out, col0, n, oh, ow);
+          goto tile_done;
+        }
         if (p.fast_div) {
 #pragma unroll
           for (int c = 0; c < G; ++c) {
@@ -366,6 +458,13 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       for (int c4 = 0; c4 < G / 4; ++c4)
         out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
       qc_store<OC, G>(p, out, col0, n, oh, ow);
+      }
+    tile_done:
+      if (rb_on) {  // this warp is done with the tile's residual rows
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[rs]);
+      }
+    }
     }
   }
 
@@ -396,6 +495,8 @@ __global__ void qadd_fastdiv_check_kernel(QConvTcParams p, int* mismatch) {
 // ------------------------------------------------------------------ host side
 struct QConvTcState {
   int variant;
+  int resid_ring;  // stage the fused add's residual rows in shared memory
+  int use_lut;     // stage the fused add's table in shared memory
   int stages;
   int win_rows;
   int fast_div;
@@ -416,12 +517,14 @@ static const QcVariant kQcVariants[] = {
     {128, 128, qconv_tc_kernel<128, 128>},
 };
 
-static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_bytes, int oc) {
+static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_bytes, int oc, bool resid_ring,
+                               bool lut) {
   size_t s = 1024;  // alignment slack
-  s += align_up(b_bytes, 1024);
+  s += align_up(b_bytes, 1024) + (lut ? 65536 : 0);
   s += (size_t)stages * stage_bytes;
   s += (size_t)oc * 8;
-  s += (size_t)(2 * stages + 5 + QC_MMA_WARPS) * 8 + 16;
+  s += (size_t)(2 * stages + 5 + QC_MMA_WARPS + 2 * QC_RSTAGES) * 8 + 16;
+  if (resid_ring) s += 128 + (size_t)QC_RSTAGES * QC_TILE_M * oc;
   return s;
 }
 
@@ -481,6 +584,16 @@ static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, c
   p.r_wp = (int)op.ip[QC_R_WP];
   p.r_pt = (int)op.ip[QC_R_PT];
   p.r_pl = (int)op.ip[QC_R_PL];
+  // residual rows of a tile are contiguous when the residual's padded geometry equals the input's
+  p.lut = st->use_lut && op.t[5] >= 0 ? (const uint8_t*)ptrs[op.t[5]] : nullptr;
+  p.r_bulk = 0;
+  p.r_off = 0;
+  if (p.has_add && st->resid_ring && p.r_hp == p.hp && p.r_wp == p.wp) {
+    p.r_off = (int64_t)p.r_pt * p.wp + p.r_pl;
+    const int64_t last_row = (int64_t)((op.ip[QC_N] * (int64_t)p.hp * p.wp + QC_TILE_M - 1) / QC_TILE_M) *
+                                 QC_TILE_M + p.r_off;
+    p.r_bulk = last_row <= op.ip[QC_R_ROWS] ? 1 : 0;
+  }
 }
 
 int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int device, char* msg, size_t n) {
@@ -509,9 +622,16 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
                 (long long)rows_needed);
   const size_t budget = 210 * 1024;
   int stages = 8;
-  while (stages > 2 && qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc) > budget) --stages;
+  // fused-add helpers in shared memory only where at least 4 window stages remain
+  bool lut = op.ip[QC_HAS_ADD] != 0 && op.t[5] >= 0;
+  if (lut && qconv_smem_bytes(st->b_bytes, 4, st->stage_bytes, oc, false, true) > budget) lut = false;
+  bool ring = op.ip[QC_HAS_ADD] != 0;
+  if (ring && qconv_smem_bytes(st->b_bytes, 4, st->stage_bytes, oc, true, lut) > budget) ring = false;
+  st->use_lut = lut ? 1 : 0;
+  st->resid_ring = ring ? 1 : 0;
+  while (stages > 2 && qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc, ring, lut) > budget) --stages;
   st->stages = stages;
-  st->smem_bytes = qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc);
+  st->smem_bytes = qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc, ring, lut);
   if (st->smem_bytes > 227 * 1024)
     return fail(msg, n, 5, "QLinearConv tensor-core path needs %zu B smem", st->smem_bytes);
   cudaError_t e = cudaFuncSetAttribute(kQcVariants[st->variant].fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -593,8 +713,69 @@ __global__ void __launch_bounds__(256) pad_planar_kernel(const uint8_t* __restri
   }
 }
 
+// Widths that are multiples of 4 (the common case): no shared memory.  One
+// thread per (image, row, 4-pixel quad, 16-channel chunk) loads the 16
+// channel words (4 pixels each) straight from NCHW -- a warp covers 8 quads x
+// 4 chunks, so every channel row is read as 32 contiguous bytes -- turns them
+// into 4 pixels x 16 channels with 4x4 byte transposes (8 PRMT each) and
+// stores each pixel's 16-byte chunk at its swizzled position.
+template <int C>
+__global__ void __launch_bounds__(256) pad_planar_q4_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                                            int n_img, int h, int w, int pt, int pl, int hp, int wp,
+                                                            uint32_t xr) {
+  constexpr int CG = C / 16;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int wq = w >> 2;
+  const int64_t items = (int64_t)n_img * h * wq * CG;
+  const uint32_t x4 = xr * 0x01010101u;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < items; it += (int64_t)gridDim.x * blockDim.x) {
+    const int cg = (int)(it % CG);
+    const int64_t r = it / CG;
+    const int pq = (int)(r % wq);
+    const int64_t nh = r / wq;  // n * h + row
+    const int row = (int)(nh % h), n = (int)(nh / h);
+    const uint8_t* src = x + (((int64_t)n * C + 16 * cg) * h + row) * w + 4 * pq;
+    const int64_t plane = (int64_t)h * w;
+    uint32_t v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = *reinterpret_cast<const uint32_t*>(src + k * plane);
+    uint32_t o[4][4];  // [pixel][word of 4 channels]
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // channels 4q .. 4q+3
+      const uint32_t t0 = __byte_perm(v[4 * q], v[4 * q + 1], 0x5140), t1 = __byte_perm(v[4 * q], v[4 * q + 1], 0x7362);
+      const uint32_t t2 = __byte_perm(v[4 * q + 2], v[4 * q + 3], 0x5140),
+                     t3 = __byte_perm(v[4 * q + 2], v[4 * q + 3], 0x7362);
+      o[0][q] = __byte_perm(t0, t2, 0x5410) ^ x4;
+      o[1][q] = __byte_perm(t0, t2, 0x7632) ^ x4;
+      o[2][q] = __byte_perm(t1, t3, 0x5410) ^ x4;
+      o[3][q] = __byte_perm(t1, t3, 0x7632) ^ x4;
+    }
+    const int64_t g0 = ((int64_t)n * hp + row + pt) * wp + pl + 4 * pq;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int64_t g = g0 + p;
+      *reinterpret_cast<uint4*>(y + (uint64_t)g * C + 16 * swz_chunk(g, cg, C)) =
+          make_uint4(o[p][0], o[p][1], o[p][2], o[p][3]);
+    }
+  }
+}
+
 int launch_pad_nhwc(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int c = (int)op.ip[PAD_C], h = (int)op.ip[PAD_H], w = (int)op.ip[PAD_W];
+  if ((w & 3) == 0 && ((uintptr_t)ptrs[op.t[0]] & 3) == 0 && (c == 32 || c == 64 || c == 128)) {
+    const int n_img = (int)eff_batch(ctx, op, op.ip[PAD_N]);
+    const int64_t items = (int64_t)n_img * h * (w / 4) * (c / 16);
+    if (items == 0) return 0;
+    const int64_t blocks64 = (items + 255) / 256;
+    const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+    auto kq = c == 32 ? pad_planar_q4_kernel<32> : (c == 64 ? pad_planar_q4_kernel<64> : pad_planar_q4_kernel<128>);
+    cudaError_t e = launch_pdl(kq, dim3(blocks), dim3(256), 0, ctx.stream, (const uint8_t*)ptrs[op.t[0]],
+                               (uint8_t*)ptrs[op.t[1]], n_img, h, w, (int)op.ip[PAD_TOP], (int)op.ip[PAD_LEFT],
+                               (int)op.ip[PAD_HP], (int)op.ip[PAD_WP], (uint32_t)op.ip[PAD_XOR]);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
   const size_t smem = (size_t)PAD_ROWS_PER_BLOCK * c * ((w + 4) & ~3);
   if (smem > 48 * 1024 || (c != 32 && c != 64 && c != 128)) return 5;
   dim3 grid((unsigned)((h + PAD_ROWS_PER_BLOCK - 1) / PAD_ROWS_PER_BLOCK), (unsigned)eff_batch(ctx, op, op.ip[PAD_N]));

@@ -164,6 +164,23 @@ class _Builder:
         return bytes(out)
 
 
+def qadd_table(c_signed: bool, c_zero: int, c_scale, r_signed: bool, r_zero: int, r_scale, y_scale, y_zero: int,
+               y_signed: bool) -> np.ndarray:
+    """QLinearAdd of every (conv byte, residual byte) pair, as the reference
+    evaluates it in float (templates/qlinear_add_op.c.j2:2-17):
+    clamp(nearbyintf(((float)(a-za)*sa + (float)(b-zb)*sb) / ys + zy)).
+    Returns the 65536 output bytes indexed by (conv byte << 8) | residual byte."""
+    byte = np.arange(256, dtype=np.int64)
+    a = (byte.astype(np.uint8).view(np.int8) if c_signed else byte).astype(np.int64)
+    b = (byte.astype(np.uint8).view(np.int8) if r_signed else byte).astype(np.int64)
+    f32 = np.float32
+    ar = (a - c_zero).astype(f32) * f32(c_scale)
+    br = (b - r_zero).astype(f32) * f32(r_scale)
+    s = ((ar[:, None] + br[None, :]).astype(f32) / f32(y_scale)).astype(f32) + f32(y_zero)
+    r = np.clip(np.rint(s.astype(f32)), -128 if y_signed else 0, 127 if y_signed else 255).astype(np.int64)
+    return (r & 0xFF).astype(np.uint8).reshape(-1)
+
+
 def swizzle_positions(rows: int, row_bytes: int) -> np.ndarray:
     """[rows, row_bytes // 16]: position of 16-byte chunk j of row r in the
     tensor-core K-major swizzle of a row_bytes-wide row (same rule as
@@ -688,7 +705,7 @@ class B200PlanEmitter:
               K.QC_OH: oh, K.QC_OW: ow, K.QC_A_SIGNED: cfg["a_signed"], K.QC_Y_ZERO: zy,
               K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QC_X_ROWS: xin.rows}
         fp = {}
-        t_r = -1
+        t_r = t_lut = -1
         out_name = op.output
         out_dtype = _suffix(op.dtype)
         label = f"{op.output}"
@@ -702,6 +719,12 @@ class B200PlanEmitter:
             r_z = add.input1_zero_point if conv_side0 else add.input0_zero_point
             rp = self._padded_of(resid)
             t_r = rp.tid
+            lut = qadd_table(_suffix(op.dtype) == "i8", int(self._scalar(c_z, "add zero")),
+                             np.float32(self._scalar(c_s, "add scale")), self._dtype(resid) == "i8",
+                             int(self._scalar(r_z, "add zero")), np.float32(self._scalar(r_s, "add scale")),
+                             np.float32(self._scalar(add.output_scale, "add scale")),
+                             int(self._scalar(add.output_zero_point, "add zero")), _suffix(add.dtype) == "i8")
+            t_lut = self._b.weight(lut, "u8", add.output + ":qadd-table")
             ip.update({K.QC_HAS_ADD: 1, K.QC_C_ZERO: int(self._scalar(c_z, "add zero")),
                        K.QC_R_ZERO: int(self._scalar(r_z, "add zero")), K.QC_R_XOR: rp.xor,
                        K.QC_R_SIGNED: int(self._dtype(resid) == "i8"), K.QC_R_HP: rp.hp, K.QC_R_WP: rp.wp,
@@ -723,7 +746,7 @@ class B200PlanEmitter:
         else:
             t_y = self._dest(out_name, out_dtype, (n, oc, oh, ow))
             ip.update({K.QC_Y_LAYOUT: 1})
-        self._b.op(K.K_QCONV_TC, [xin.tid, t_w, t_e, t_r, t_y], ip, fp, label=label + " (tcgen05 i8)",
+        self._b.op(K.K_QCONV_TC, [xin.tid, t_w, t_e, t_r, t_y, t_lut], ip, fp, label=label + " (tcgen05 i8)",
                    batched=n == self._batch)
         if padded_out is False and out_name in self._need_pad:
             self._padded_of(out_name)  # consumers also need the NHWC copy
