@@ -71,6 +71,16 @@ def workload_spec(name: str):
                "engine": "f16", "unit_ops": "TFLOP/s", "dtype": "f16 x int4 -> f32 acc -> f16",
                "ref_tag": "ref_nbits_m1", "ref_rows": 1, "full_rows": m}
         return wl, dom
+    if name == "mlp_fp32":
+        wl = W.mlp_fp32()
+        p = wl.params
+        m, k, h = p["m"], p["k"], p["hidden"]
+        flops = 2 * m * k * h * 2
+        byts = 4 * (2 * k * h + m * k + m * k + k + h)
+        dom = {"kernel": "gemm_f32", "launches": 2, "ops_total": flops, "bytes_total": byts, "engine": "fp32",
+               "unit_ops": "TFLOP/s", "dtype": "f32 (reference accumulation order)", "ref_tag": "ref_mlp_m64",
+               "ref_rows": 64, "full_rows": m}
+        return wl, dom
     if name == "attention_fp16":
         wl = W.attention_fp16()
         p = wl.params

@@ -10,6 +10,7 @@
 // the host picks the CTA tile that puts at least ~2 CTAs on each of the 148
 // SMs.  Bound: FP32 issue rate at 2 instructions per multiply-add (FMUL +
 // FADD), i.e. half the FFMA peak; HBM traffic (weights once) is far below it.
+#include "exact_chain.cuh"
 #include "host_util.h"
 #include "kernels.h"
 #include "tc100.cuh"
@@ -125,7 +126,75 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const G
   }
 }
 
+// Y = op(A) * B^T with A [M][K] and B [N][K] row-major (no transA, transB = 1:
+// K contiguous in both): the cp.async-pipelined exact chains of exact_chain.cuh.
+template <int BM, int BN, int RM, int RN>
+__global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(const GemmF32Params p) {
+  using XC = ExactChain<BM, BN, RM, RN, 32, 4>;
+  extern __shared__ __align__(16) float xc_smem[];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  uint64_t acc[RM][RN / 2];
+#pragma unroll
+  for (int r = 0; r < RM; ++r)
+#pragma unroll
+    for (int c = 0; c < RN / 2; ++c) acc[r][c] = 0;  // +0.0f pairs
+  XC::run(p.a, p.k, p.b, p.k, p.m, p.n, p.k, m0, n0, acc, xc_smem);
+  const int tx = threadIdx.x % XC::TX, ty = threadIdx.x / XC::TX;
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    const int i = m0 + ty * RM + r;
+    if (i >= p.m) continue;
+#pragma unroll
+    for (int c = 0; c < RN / 2; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = n0 + XC::col(tx, c, h);
+        if (j >= p.n) continue;
+        const float a = h ? xc_hi(acc[r][c]) : xc_lo(acc[r][c]);
+        float y;
+        if (p.bias_mode) {
+          float bias;
+          switch (p.bias_mode) {
+            case 1: bias = p.bias[0]; break;
+            case 2: bias = p.bias[j]; break;
+            case 3: bias = p.bias[i]; break;
+            default: bias = p.bias[(size_t)i * p.n + j]; break;
+          }
+          y = __fadd_rn(__fmul_rn(a, p.alpha), __fmul_rn(bias, p.beta));
+        } else {
+          y = __fmul_rn(a, p.alpha);
+        }
+        if (p.relu) y = y > 0.0f ? y : 0.0f;  // ref_scalar_f32_relu
+        p.y[(size_t)i * p.n + j] = y;
+      }
+  }
+}
+
 typedef void (*GemmKernel)(const GemmF32Params);
+struct ChainVariant {
+  int bm, bn, threads;
+  size_t smem;
+  GemmKernel fn;
+};
+#define EMX_CHAIN_VARIANT(BM, BN, RM, RN)                                                        \
+  {BM, BN, (BM / RM) * (BN / RN), ExactChain<BM, BN, RM, RN, 32, 4>::SMEM_BYTES,                 \
+   gemm_f32_chain_kernel<BM, BN, RM, RN>}
+static const ChainVariant kChainVariants[] = {
+    EMX_CHAIN_VARIANT(64, 64, 4, 4), EMX_CHAIN_VARIANT(32, 64, 4, 4), EMX_CHAIN_VARIANT(32, 32, 2, 2),
+    EMX_CHAIN_VARIANT(16, 32, 2, 2), EMX_CHAIN_VARIANT(16, 16, 2, 2), EMX_CHAIN_VARIANT(8, 16, 1, 2),
+};
+#undef EMX_CHAIN_VARIANT
+
+int prepare_gemm_f32(const PlanOp&, void* const*, OpState*, int, char* msg, size_t n) {
+  for (const auto& v : kChainVariants) {
+    cudaError_t e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem);
+    if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  return 0;
+}
+
 struct GemmVariant {
   int bm, bn, threads;
   GemmKernel fn;
@@ -155,6 +224,21 @@ int launch_gemm_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   p.beta = (float)op.fp[GMF_BETA];
   if (p.trans_a && p.m != op.ip[GM_M]) return 5;  // a transposed A cannot be sliced by rows
   if (p.m <= 0 || p.n <= 0) return 0;
+  if (!p.trans_a && p.trans_b && p.k % 4 == 0 && !(((uintptr_t)p.a | (uintptr_t)p.b) & 15u)) {
+    // the largest tile that still gives >= 3 CTAs per SM; else the smallest tile
+    const ChainVariant* v = &kChainVariants[sizeof(kChainVariants) / sizeof(kChainVariants[0]) - 1];
+    for (const auto& c : kChainVariants) {
+      const long ctas = (long)((p.m + c.bm - 1) / c.bm) * ((p.n + c.bn - 1) / c.bn);
+      if (ctas >= 3L * ctx.num_sms) {
+        v = &c;
+        break;
+      }
+    }
+    dim3 grid((unsigned)((p.n + v->bn - 1) / v->bn), (unsigned)((p.m + v->bm - 1) / v->bm));
+    cudaError_t e = launch_pdl(v->fn, grid, dim3(v->threads), v->smem, ctx.stream, p);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
   // the largest tile that still gives >= 2 CTAs per SM; else the smallest tile
   const GemmVariant* v = &kGemmVariants[sizeof(kGemmVariants) / sizeof(kGemmVariants[0]) - 1];
   for (const auto& c : kGemmVariants) {

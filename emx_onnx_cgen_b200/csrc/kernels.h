@@ -81,10 +81,13 @@ enum {
 };
 enum { ATF_SCALE };
 
-// ---- K_LSTM_F32: t[0]=X [T][B][I], t[1]=W rows interleaved [4H][I] (row 4h+g, g = i,o,f,c),
-//      t[2]=R interleaved [4H][H], t[3]=Wb+Rb interleaved [4H], t[4]=scratch [T*B][4H],
+// ---- K_LSTM_F32: t[0]=X [T][B][I], t[1]=W rows interleaved [4Hp][I] (g = i,o,f,c; see below),
+//      t[2]=R interleaved [4Hp][H], t[3]=Wb+Rb interleaved [4Hp], t[4]=scratch [T*B][4Hp],
 //      t[5]=scratch h [2][B][H], t[6]=scratch c [B][H], t[7]=Y|-1, t[8]=Y_h|-1, t[9]=Y_c|-1
+//      gate columns are in tiles of 4 * LS_TILE_UNITS: position g * LS_TILE_UNITS + u of tile T is
+//      gate g of unit T * LS_TILE_UNITS + u (units padded to a multiple of LS_TILE_UNITS with zero rows)
 enum { LS_T, LS_B, LS_I, LS_H };
+enum { LS_TILE_UNITS = 16 };
 
 // ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y
 enum {
@@ -159,6 +162,7 @@ int launch_qconv_tc(const PlanOp&, void* const*, const OpState*, const LaunchCtx
 int launch_pad_nhwc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qconv_generic(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qlinear_add(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_gemm_f32(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_gemm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 void launch_hold(const int* flag, int seq, int* err, cudaStream_t stream);
 int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
@@ -166,6 +170,7 @@ int prepare_nbits(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_lstm_f32(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_lstm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_qmatmul(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_conv_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);

@@ -1051,20 +1051,31 @@ class B200PlanEmitter:
         t, b, isz, h = int(op.seq_length), int(op.batch_size), int(op.input_size), int(op.hidden_size)
         w = self._const(op.input_w, "W").astype(np.float32).reshape(4, h, isz)
         r = self._const(op.input_r, "R").astype(np.float32).reshape(4, h, h)
-        # interleave the gate blocks (i, o, f, c) so unit h's gates are rows 4h .. 4h+3
-        wp = np.ascontiguousarray(w.transpose(1, 0, 2)).reshape(4 * h, isz)
-        rp = np.ascontiguousarray(r.transpose(1, 0, 2)).reshape(4 * h, h)
         if op.input_b is not None:
             bb = self._const(op.input_b, "B").astype(np.float32).reshape(8, h)
             bsum = (bb[:4] + bb[4:]).astype(np.float32)  # Wb + Rb, one float add as in the reference
         else:
             bsum = np.zeros((4, h), np.float32)
-        bsum = np.ascontiguousarray(bsum.T).reshape(4 * h)
+        # gate columns in tiles of 4 * U: position g*U + u of tile T is gate g (i, o, f, c) of
+        # unit T*U + u; units padded to a multiple of U with zero rows
+        u = K.LS_TILE_UNITS
+        hp = -(-h // u) * u
+        order = np.arange(4 * hp)
+        tile, pos = order // (4 * u), order % (4 * u)
+        gate, unit = pos // u, tile * u + pos % u
+        real = unit < h
+        wp = np.zeros((4 * hp, isz), np.float32)
+        rp = np.zeros((4 * hp, h), np.float32)
+        bs = np.zeros(4 * hp, np.float32)
+        wp[real] = w[gate[real], unit[real]]
+        rp[real] = r[gate[real], unit[real]]
+        bs[real] = bsum[gate[real], unit[real]]
+        bsum = bs
         t_w = self._b.weight(wp, "f32", op.input_w + ":interleaved")
         t_r = self._b.weight(rp, "f32", op.input_r + ":interleaved")
         t_bs = self._b.weight(bsum, "f32", (op.input_b or "lstm") + ":bias-sum")
         x = self._src(op.input_x)
-        t_gx = self._b.arena_tensor(T_TEMP, "f32", (t * b, 4 * h), name=f"{op.input_x}:lstm-x-partials")
+        t_gx = self._b.arena_tensor(T_TEMP, "f32", (t * b, 4 * hp), name=f"{op.input_x}:lstm-x-partials")
         t_h = self._b.arena_tensor(T_TEMP, "f32", (2, b, h), name="lstm:h")
         t_c = self._b.arena_tensor(T_TEMP, "f32", (b, h), name="lstm:c")
         outs = []
