@@ -11,7 +11,10 @@ attributes and domains.  ONNX shape inference is not available;
 ``value_info`` leaves untyped, for the operators of the reference's quantised
 model fixtures (the role ONNX shape inference plays in the reference's
 importer, onnx_import.py:2146-2185).  Symbolic dimensions must be bound by the
-caller (``dim_values``).
+caller (``dim_values``): by parameter name (``{"batch": 1}`` fixes every
+axis carrying that name) or by position (``{"images:0": 1}`` fixes axis 0 of
+value ``images``), the two forms of the reference's ``--input-dim``
+(cli.py:992-1001, input_dim_overrides.py).
 
     spec = infer_types(read_onnx("model.onnx", dim_values={"batch": 32}))
 """
@@ -173,9 +176,15 @@ def _value_info(buf: bytes, dim_values: dict[str, int]) -> TensorSpec | None:
                                     dv = _signed(v4)
                                 elif n4 == 2:
                                     dp = v4.decode()
-                            if dv is None:
+                            pos = f"{name}:{len(dims)}"
+                            if pos in dim_values:
+                                dv = dim_values[pos]
+                                if dp is not None:  # a named axis pinned by position pins the name too
+                                    dim_values.setdefault(dp, dv)
+                            elif dv is None:
                                 if dp not in dim_values:
-                                    raise OnnxFormatError(f"value {name}: symbolic dimension {dp!r} needs a value")
+                                    raise OnnxFormatError(f"value {name}: symbolic dimension {len(dims)} ({dp!r}) needs a "
+                                                          f"value (dim_values[{dp!r}] or [{pos!r}])")
                                 dv = dim_values[dp]
                             dims.append(dv)
     if not name or elem not in _DTYPES or not has_shape:

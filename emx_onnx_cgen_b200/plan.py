@@ -1151,3 +1151,45 @@ class B200PlanEmitter:
         if why:
             raise UnsupportedOpError(f"MatMulNBits: {why}")
         self._nbits_emit([op], op.output)
+
+
+# ------------------------------------------------------------------ plan files
+def save_plan(plan: Plan, out_dir, stem: str | None = None) -> dict:
+    """Write ``<stem>.plan`` (the launch plan), ``<stem>.weights`` (the packed
+    weight blob, read by emx_b200_plan_load) and ``<stem>.json`` (graph I/O
+    names, shapes and dtypes, batch, op labels).  Returns the paths."""
+    import json
+    from pathlib import Path
+    out = Path(out_dir)
+    out.mkdir(parents=True, exist_ok=True)
+    stem = stem or plan.name
+    paths = {k: out / f"{stem}.{k}" for k in ("plan", "weights", "json")}
+    paths["plan"].write_bytes(plan.plan_bytes)
+    paths["weights"].write_bytes(plan.weight_bytes)
+    meta = {
+        "name": plan.name, "batch": plan.batch, "arena_bytes": plan.arena_bytes,
+        "inputs": [{"name": n, "shape": list(s), "dtype": d}
+                   for n, s, d in zip(plan.input_names, plan.input_shapes, plan.input_dtypes)],
+        "outputs": [{"name": n, "shape": list(s), "dtype": d}
+                    for n, s, d in zip(plan.output_names, plan.output_shapes, plan.output_dtypes)],
+        "ops": [f"{K.NAMES.get(op.kernel, op.kernel)}: {op.label}" for op in plan.ops],
+    }
+    paths["json"].write_text(json.dumps(meta, indent=1) + "\n")
+    return paths
+
+
+def load_plan(prefix) -> tuple[Plan, str]:
+    """Read the files written by save_plan (``prefix`` without extension):
+    the Plan (without its weight blob) and the weights file path for
+    Session(plan, weights_path=...)."""
+    import json
+    from pathlib import Path
+    prefix = Path(prefix)
+    meta = json.loads(prefix.with_suffix(".json").read_text())
+    plan_bytes = prefix.with_suffix(".plan").read_bytes()
+    ins, outs = meta["inputs"], meta["outputs"]
+    plan = Plan(meta["name"], plan_bytes, b"", tuple(t["name"] for t in ins), tuple(tuple(t["shape"]) for t in ins),
+                tuple(t["dtype"] for t in ins), tuple(t["name"] for t in outs),
+                tuple(tuple(t["shape"]) for t in outs), tuple(t["dtype"] for t in outs), int(meta["batch"]),
+                [PlanOp(0, [], label=s) for s in meta["ops"]], [], int(meta["arena_bytes"]))
+    return plan, str(prefix.with_suffix(".weights"))

@@ -248,6 +248,8 @@ def matmul_nbits_f16(m: int = 64, k: int = 256, n: int = 192, block: int = 32, z
     4-bit packed per block) or "column" (uint8 [N], one per column).  Optional
     fp16 bias [N] ~U(-1, 1); scales fp16 [N][n_blocks] ~U(0.005, 0.02).
     """
+    if zero_points not in ("none", "block", "column"):
+        raise ValueError(f"zero_points must be 'none', 'block' or 'column', not {zero_points!r}")
     rng = np.random.default_rng(weight_seed)
     nb = -(-k // block)
     inits = {"B": rng.integers(0, 256, (n, nb, block // 2)).astype(np.uint8),
