@@ -295,6 +295,8 @@ def ours_arm(args) -> None:
     wl, dom = workload_spec(args.workload)
     plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
     sess = Session(plan, device=local)
+    if args.io_chunks is not None:
+        sess.set_host_io_chunks(args.io_chunks)
     # a real (non-legacy) stream: its handle is what the library launches on and
     # what the timing events are recorded on
     stream = torch.cuda.Stream()
@@ -407,7 +409,7 @@ def ours_arm(args) -> None:
         "metric": "inferences/s", "value": world * 1000.0 / ms, "unit": "inferences/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, **_config(wl)},
+        "config": {"workload": args.workload, **_config(wl), "host_io_chunks": args.io_chunks or 4},
         "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "inferences/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary(),
@@ -453,6 +455,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qconv_stack_int8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--io-chunks", type=int, default=None,
+                    help="batch slices for the e2e run's pipelined host copies (library default 4; 1 = off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -5,6 +5,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -112,6 +113,14 @@ struct emx_plan {
   int* h_hold = nullptr;
   int* d_hold = nullptr;
   int hold_seq = 0;
+  // pipelined host I/O: the batch is split into io_chunks slices whose
+  // upload, kernels and download run on three streams joined by events
+  int io_chunks = 4;
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> ev_in, ev_comp;
+  cudaEvent_t ev_start = nullptr, ev_done = nullptr;
+  void* d_io = nullptr;           // dedicated full-batch staging of every I/O tensor (never aliased)
+  std::vector<size_t> io_off;     // per I/O tensor (inputs, then outputs): offset into d_io
 };
 
 namespace {
@@ -226,6 +235,13 @@ void destroy(emx_plan* p) {
   cudaSetDevice(p->device);
   for (auto& g : p->graphs) cudaGraphExecDestroy(g.exec);
   if (p->h_hold) cudaFreeHost(p->h_hold);
+  for (auto e : p->ev_in) cudaEventDestroy(e);
+  for (auto e : p->ev_comp) cudaEventDestroy(e);
+  if (p->ev_start) cudaEventDestroy(p->ev_start);
+  if (p->ev_done) cudaEventDestroy(p->ev_done);
+  if (p->copy_in) cudaStreamDestroy(p->copy_in);
+  if (p->copy_out) cudaStreamDestroy(p->copy_out);
+  if (p->d_io) cudaFree(p->d_io);
   for (auto e : p->ev_begin) cudaEventDestroy(e);
   for (auto e : p->ev_end) cudaEventDestroy(e);
   if (p->own_stream) cudaStreamDestroy(p->own_stream);
@@ -328,6 +344,142 @@ size_t row_bytes(const PlanTensor& t) {
   return (size_t)(t.nbytes / (uint64_t)t.dims[0]);
 }
 
+// page-locked host memory (cudaHostAlloc / cudaHostRegister): copies from it
+// are asynchronous and can overlap kernels and copies in the other direction
+bool is_pinned_host(const void* ptr) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+constexpr size_t kPipelineMinHostBytes = 1u << 20;
+
+// Whether a run can split its batch into slices whose host copies overlap the
+// kernels: a batchable plan, every output batched on axis 0, every host
+// buffer page-locked, at least 1 MiB crossing the bus, two or more rows.
+bool can_pipeline(const emx_plan* p, const void* const* inputs, void* const* outputs, int64_t count) {
+  if (p->io_chunks < 2 || p->profiling || count < 2 || p->hdr.batch <= 0 || !(p->hdr.flags & EMX_PLAN_BATCHABLE))
+    return false;
+  size_t host_bytes = 0;
+  for (size_t i = 0; i < p->inputs.size(); ++i) {
+    const PlanTensor& t = p->tensors[p->inputs[i]];
+    if (is_device_pointer(inputs[i])) continue;
+    if (!is_pinned_host(inputs[i])) return false;
+    host_bytes += t.batch_axis == 0 ? (size_t)count * row_bytes(t) : (size_t)t.nbytes;
+  }
+  for (size_t i = 0; i < p->outputs.size(); ++i) {
+    const PlanTensor& t = p->tensors[p->outputs[i]];
+    if (t.batch_axis != 0 || row_bytes(t) == 0) return false;
+    if (is_device_pointer(outputs[i])) continue;
+    if (!is_pinned_host(outputs[i])) return false;
+    host_bytes += (size_t)count * row_bytes(t);
+  }
+  return host_bytes >= kPipelineMinHostBytes;
+}
+
+int ensure_pipeline(emx_plan* p) {
+  if (!p->copy_in) CUDA_TRY(cudaStreamCreateWithFlags(&p->copy_in, cudaStreamNonBlocking), "copy-in stream");
+  if (!p->copy_out) CUDA_TRY(cudaStreamCreateWithFlags(&p->copy_out, cudaStreamNonBlocking), "copy-out stream");
+  if (!p->ev_start) CUDA_TRY(cudaEventCreateWithFlags(&p->ev_start, cudaEventDisableTiming), "event");
+  if (!p->ev_done) CUDA_TRY(cudaEventCreateWithFlags(&p->ev_done, cudaEventDisableTiming), "event");
+  while ((int)p->ev_in.size() < p->io_chunks) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    CUDA_TRY(cudaEventCreateWithFlags(&a, cudaEventDisableTiming), "event");
+    p->ev_in.push_back(a);
+    CUDA_TRY(cudaEventCreateWithFlags(&b, cudaEventDisableTiming), "event");
+    p->ev_comp.push_back(b);
+  }
+  if (!p->d_io) {
+    size_t total = 0;
+    p->io_off.clear();
+    for (uint32_t id : p->inputs) { p->io_off.push_back(total); total += (p->tensors[id].nbytes + 255) & ~(size_t)255; }
+    for (uint32_t id : p->outputs) { p->io_off.push_back(total); total += (p->tensors[id].nbytes + 255) & ~(size_t)255; }
+    if (cudaMalloc(&p->d_io, total ? total : 256) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(EMX_ERR_OUT_OF_MEMORY, "host I/O staging of %zu bytes failed", total);
+    }
+  }
+  return EMX_OK;
+}
+
+// The run as `chunks` batch slices: slice i's host inputs are uploaded on
+// copy_in, its kernels run on the caller's stream once they have arrived,
+// and its host outputs are downloaded on copy_out once its kernels are done,
+// so uploads, kernels and downloads of neighbouring slices overlap.  Slices
+// stage through d_io at their own rows, never through the arena, whose
+// regions later kernels reuse.  The caller's stream waits for the last
+// download before the call's work is complete.
+int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, int64_t b0, int64_t count,
+                  cudaStream_t S) {
+  int rc = ensure_pipeline(p);
+  if (rc) return rc;
+  uint8_t* io = static_cast<uint8_t*>(p->d_io);
+  const size_t nin = p->inputs.size();
+  CUDA_TRY(cudaEventRecord(p->ev_start, S), "event record");
+  CUDA_TRY(cudaStreamWaitEvent(p->copy_in, p->ev_start, 0), "stream wait");
+  CUDA_TRY(cudaStreamWaitEvent(p->copy_out, p->ev_start, 0), "stream wait");
+  // inputs without a batch axis: whole, once, ahead of the first slice
+  for (size_t i = 0; i < nin; ++i) {
+    const uint32_t id = p->inputs[i];
+    const PlanTensor& t = p->tensors[id];
+    if (t.batch_axis == 0) continue;
+    if (is_device_pointer(inputs[i])) {
+      p->ptrs[id] = const_cast<void*>(inputs[i]);
+    } else {
+      CUDA_TRY(cudaMemcpyAsync(io + p->io_off[i], inputs[i], t.nbytes, cudaMemcpyHostToDevice, p->copy_in),
+               "input upload");
+      p->ptrs[id] = io + p->io_off[i];
+    }
+  }
+  const int64_t rows = (count + p->io_chunks - 1) / p->io_chunks;
+  int launches = 0;
+  for (int c = 0; c * rows < count; ++c) {
+    const int64_t r0 = b0 + c * rows, rn = std::min<int64_t>(rows, b0 + count - r0);
+    for (size_t i = 0; i < nin; ++i) {
+      const uint32_t id = p->inputs[i];
+      const PlanTensor& t = p->tensors[id];
+      if (t.batch_axis != 0) continue;
+      const size_t rb = row_bytes(t), off = (size_t)r0 * rb;
+      if (is_device_pointer(inputs[i])) {
+        p->ptrs[id] = const_cast<uint8_t*>(static_cast<const uint8_t*>(inputs[i]) + off);
+      } else {
+        uint8_t* dst = io + p->io_off[i] + off;
+        CUDA_TRY(cudaMemcpyAsync(dst, static_cast<const uint8_t*>(inputs[i]) + off, (size_t)rn * rb,
+                                 cudaMemcpyHostToDevice, p->copy_in), "input upload");
+        p->ptrs[id] = dst;
+      }
+    }
+    CUDA_TRY(cudaEventRecord(p->ev_in[c], p->copy_in), "event record");
+    CUDA_TRY(cudaStreamWaitEvent(S, p->ev_in[c], 0), "stream wait");
+    for (size_t i = 0; i < p->outputs.size(); ++i) {
+      const uint32_t id = p->outputs[i];
+      const size_t off = (size_t)r0 * row_bytes(p->tensors[id]);
+      p->ptrs[id] = is_device_pointer(outputs[i]) ? static_cast<uint8_t*>(outputs[i]) + off
+                                                   : io + p->io_off[nin + i] + off;
+    }
+    rc = p->use_graphs ? run_graph(p, rn, S, &launches) : launch_ops(p, rn, S, &launches);
+    if (rc) return rc;
+    CUDA_TRY(cudaEventRecord(p->ev_comp[c], S), "event record");
+    CUDA_TRY(cudaStreamWaitEvent(p->copy_out, p->ev_comp[c], 0), "stream wait");
+    for (size_t i = 0; i < p->outputs.size(); ++i) {
+      if (is_device_pointer(outputs[i])) continue;
+      const uint32_t id = p->outputs[i];
+      const size_t rb = row_bytes(p->tensors[id]), off = (size_t)r0 * rb;
+      CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(outputs[i]) + off, io + p->io_off[nin + i] + off,
+                               (size_t)rn * rb, cudaMemcpyDeviceToHost, p->copy_out), "output download");
+    }
+  }
+  CUDA_TRY(cudaEventRecord(p->ev_done, p->copy_out), "event record");
+  CUDA_TRY(cudaStreamWaitEvent(S, p->ev_done, 0), "stream wait");
+  p->launches_total += launches;
+  p->launches_last = launches;
+  p->events_pending = false;
+  return EMX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -402,6 +554,12 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
   cudaStream_t stream = stream_ ? static_cast<cudaStream_t>(stream_) : p->own_stream;
   p->last_stream = stream;
   p->pending.clear();
+  for (size_t i = 0; i < p->inputs.size(); ++i)
+    if (!inputs[i]) return set_error(EMX_ERR_INVALID_ARGUMENT, "input %zu is NULL", i);
+  for (size_t i = 0; i < p->outputs.size(); ++i)
+    if (!outputs[i]) return set_error(EMX_ERR_INVALID_ARGUMENT, "output %zu is NULL", i);
+  if (full > 0 && can_pipeline(p, inputs, outputs, batch_count))
+    return run_pipelined(p, inputs, outputs, batch_begin, batch_count, stream);
   for (size_t i = 0; i < p->inputs.size(); ++i) {
     const PlanTensor& t = p->tensors[p->inputs[i]];
     const void* src = inputs[i];
@@ -495,6 +653,13 @@ int64_t emx_b200_launch_count(const emx_plan_t* p) { return p ? p->launches_tota
 int emx_b200_set_graphs(emx_plan_t* p, int enable) {
   if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
   p->use_graphs = enable != 0;
+  return EMX_OK;
+}
+
+int emx_b200_set_host_io_chunks(emx_plan_t* p, int chunks) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (chunks < 1 || chunks > 64) return set_error(EMX_ERR_INVALID_ARGUMENT, "host I/O chunks %d not in [1, 64]", chunks);
+  p->io_chunks = chunks;
   return EMX_OK;
 }
 

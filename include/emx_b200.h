@@ -23,8 +23,13 @@
  *   - One plan handle serves one device and is used by one host thread at a
  *     time, the same single-threaded contract as the generated C
  *     (README.md:23 of the reference); multi-GPU = one handle per device.
- *   - No allocation happens after emx_b200_plan_load: the arena holding every
- *     intermediate tensor is sized by the plan.
+ *   - No allocation happens after emx_b200_plan_load (the arena holding every
+ *     intermediate tensor is sized by the plan), with one exception: the
+ *     first run that pipelines page-locked host I/O (see emx_b200_run)
+ *     allocates a staging buffer the size of the plan's inputs and outputs
+ *     and two copy streams, kept until emx_b200_plan_free.
+ *   - Calls on one plan must be ordered on the device (one stream, or
+ *     synchronised between streams): they share the arena.
  */
 #ifndef EMX_B200_H
 #define EMX_B200_H
@@ -70,7 +75,13 @@ int emx_b200_plan_load_mem(const void *plan, size_t plan_len, const void *weight
 /* Run the plan.  inputs[i]/outputs[i] follow the graph's input/output order
  * (the parameter order of the generated `<model>(...)`, c_emitter.py:2297)
  * and may be host or device pointers (detected per pointer).  Host buffers
- * are staged through the arena with cudaMemcpyAsync on `stream`.
+ * are staged through the arena with cudaMemcpyAsync on `stream`; when every
+ * host buffer is page-locked (cudaHostAlloc / cudaHostRegister), at least
+ * 1 MiB crosses the bus, the plan is batchable on axis 0 and the run has two
+ * or more rows, the rows are split into slices (emx_b200_set_host_io_chunks,
+ * default 4) whose uploads, kernels and downloads overlap on two extra
+ * streams; `stream` still orders the whole run (it waits for the last
+ * download).  Results are identical either way.
  * [batch_begin, batch_begin + batch_count) selects rows along axis 0 of every
  * batched input/output (batch_count = -1: the plan's full batch); the
  * pointers address the full tensors.  `stream` is a cudaStream_t (NULL: the
@@ -117,6 +128,11 @@ int emx_b200_op_times(const emx_plan_t *plan, double *ms, int32_t n_ops, int64_t
  * into a graph, later runs with the same addresses replay it with one launch.
  * Off: every run launches the kernels one by one. */
 int emx_b200_set_graphs(emx_plan_t *plan, int enable);
+
+/* Number of batch slices for pipelined host I/O (1..64; 1 = no pipelining,
+ * every host copy then runs on `stream` around the kernels).  Default 4.
+ * No counterpart in the reference (its generated C runs in host memory). */
+int emx_b200_set_host_io_chunks(emx_plan_t *plan, int chunks);
 
 /* Allocation-free standalone QLinearConv, 3x3 kernel, stride 1, pads 1,
  * group 1, no dilation: uint8 NCHW x [n][c][h][w] with x_zero_point 0 or 128,
