@@ -79,14 +79,17 @@ struct QConvTcParams {
 
 constexpr int QC_RSTAGES = 3;  // residual ring depth (tiles)
 
-// Warp roles: warp 0 producer, warps 1..2 MMA issuers (one partial
+// Warp roles: warp 0 producer, warps 1..P MMA issuers (one partial
 // accumulator each: one issuing thread completes a tcgen05.mma every ~150
-// cycles whatever its N, so with N = OC = 64 two issuers keep more of the
-// tensor core busy), warps 4..19 epilogue.
-constexpr int QC_MMA_WARPS = 2;
-constexpr int QC_EPI_WARP0 = 4;
+// cycles whatever its N, so with N = OC = 64 several issuers keep more of the
+// tensor core busy), warp P+1 residual producer, then 16 epilogue warps from
+// the next multiple of 4.  P = 4 while 2 tiles x P partials x OC columns fit
+// the 512 TMEM columns (OC <= 64), else 2.
+constexpr int QC_MMA_WARPS = 4;  // most issuers of any variant
 constexpr int QC_EPI_WARPS = 16;
-constexpr int QC_THREADS = 32 * (QC_EPI_WARP0 + QC_EPI_WARPS);
+__host__ __device__ constexpr int qc_partials(int oc) { return 2 * QC_MMA_WARPS * oc <= 512 ? QC_MMA_WARPS : 256 / oc; }
+__host__ __device__ constexpr int qc_epi_warp0(int oc) { return (qc_partials(oc) + 2 + 3) & ~3; }
+__host__ __device__ constexpr int qc_threads(int oc) { return 32 * (qc_epi_warp0(oc) + QC_EPI_WARPS); }
 constexpr int QC_TILE_M = 128;
 
 // bytes of a clamped integer-valued float (see float_to_byte): gather the low
@@ -143,12 +146,25 @@ __device__ __forceinline__ void qc_load_resid(const QConvTcParams& p, uint32_t (
   }
 }
 
+// G consecutive accumulator columns of this warp's 32 TMEM lanes (asynchronous; tmem_wait_ld before use)
+template <int G>
+__device__ __forceinline__ void qc_tmem_ld(uint32_t taddr, uint32_t (&r)[G]) {
+  if constexpr (G == 8) {
+    tmem_ld8(taddr, r);
+  } else {
+#pragma unroll
+    for (int c = 0; c < G / 16; ++c) tmem_ld16(taddr + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&r[c * 16]));
+  }
+}
+
 template <int CIN, int OC>
-__global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcParams p) {
+__global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConvTcParams p) {
   constexpr int KSTEPS = CIN / 32;  // kind::i8 MMAs (K = 32) per tap
   constexpr int G = OC / 4;         // columns per epilogue warp
   // partial accumulators (= issuing warps) per tile: 2 tiles x P x OC <= 512 TMEM columns
-  constexpr int P = QC_MMA_WARPS;
+  constexpr int P = qc_partials(OC);
+  constexpr int QC_RESID_WARP = P + 1;
+  constexpr int QC_EPI_WARP0 = qc_epi_warp0(OC);
   constexpr uint32_t TMEM_COLS = 512;
   static_assert(G % 8 == 0, "OC must be a multiple of 32");
   extern __shared__ uint8_t smem_raw[];
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
         (void)mbar_wait(&drain[my], 0, nullptr, 0);
       }
     }
-  } else if (warp == 3) {
+  } else if (warp == QC_RESID_WARP) {
     if (lane == 0 && p.has_add && p.r_bulk) {
       // ---------------- residual producer: the tile's residual rows, one bulk copy each
       pdl_wait();  // the residual may come from the preceding kernel
@@ -347,19 +363,30 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       bool ok = mbar_wait(&accf[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      uint32_t pv[P][G];
+      // the PE partial accumulators in use (PE >= 1), summed as they arrive
+      uint32_t v[G];
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * P * OC + col0);
+      {
+        uint32_t t[G];
+        qc_tmem_ld<G>(taddr, v);
+        if (PE > 1) qc_tmem_ld<G>(taddr + OC, t);
+        tmem_wait_ld();
+        if (PE > 1) {
 #pragma unroll
-      for (int pp = 0; pp < P; ++pp) {
-        if constexpr (G == 8) {
-          tmem_ld8(taddr + pp * OC, pv[pp]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < G / 16; ++c)
-            tmem_ld16(taddr + pp * OC + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&pv[pp][c * 16]));
+          for (int c = 0; c < G; ++c) v[c] += t[c];
         }
       }
-      tmem_wait_ld();
+#pragma unroll
+      for (int pp = 2; pp < P; pp += 2) {
+        if (pp < PE) {
+          uint32_t t0[G], t1[G];
+          qc_tmem_ld<G>(taddr + pp * OC, t0);
+          if (pp + 1 < PE) qc_tmem_ld<G>(taddr + (pp + 1) * OC, t1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < G; ++c) v[c] += pp + 1 < PE ? t0[c] + t1[c] : t0[c];
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[acc]);
@@ -368,15 +395,6 @@ __global__ void __launch_bounds__(QC_THREADS, 1) qconv_tc_kernel(const QConvTcPa
       if (rb_on) {
         ok = mbar_wait(&rfull[rs], (uint32_t)(it / QC_RSTAGES) & 1u, p.err, DEV_TIMEOUT_EPILOGUE);
         if (!__all_sync(0xffffffffu, ok)) break;
-      }
-      uint32_t v[G];
-#pragma unroll
-      for (int c = 0; c < G; ++c) {
-        int32_t s = (int32_t)pv[0][c];
-#pragma unroll
-        for (int pp = 1; pp < P; ++pp)
-          if (pp < PE) s += (int32_t)pv[pp][c];
-        v[c] = (uint32_t)s;
       }
 
       // pixel of pitched row q: divisions by Hp*Wp and Wp as multiply-shift
@@ -662,7 +680,8 @@ int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, con
   p.err = ctx.d_error;
   if (p.n_tiles <= 0) return 0;
   const int grid = p.n_tiles < ctx.num_sms ? p.n_tiles : ctx.num_sms;
-  cudaError_t e = launch_pdl(kQcVariants[st->variant].fn, dim3(grid), dim3(QC_THREADS), st->smem_bytes, ctx.stream, p);
+  cudaError_t e = launch_pdl(kQcVariants[st->variant].fn, dim3(grid), dim3(qc_threads(kQcVariants[st->variant].oc)),
+                             st->smem_bytes, ctx.stream, p);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }
