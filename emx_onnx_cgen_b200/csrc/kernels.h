@@ -45,7 +45,8 @@ enum {
   QC_N, QC_CIN, QC_OC, QC_KH, QC_KW, QC_HP, QC_WP, QC_OH, QC_OW, QC_A_SIGNED, QC_Y_ZERO,
   QC_Y_LAYOUT /*0 planar, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,
   QC_HAS_ADD, QC_C_ZERO /*conv-side zero in the add*/, QC_R_ZERO, QC_R_XOR, QC_R_SIGNED, QC_R_HP, QC_R_WP,
-  QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED, QC_X_ROWS, QC_Y_ROWS, QC_R_ROWS
+  QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED, QC_X_ROWS, QC_Y_ROWS, QC_R_ROWS,
+  QC_CHAIN /*first op of a chain: its length L (t[6] = chain state); later members: -1; else 0*/
 };
 enum { QCF_C_SCALE, QCF_R_SCALE, QCF_ADD_SCALE };
 
@@ -109,11 +110,19 @@ enum { QL_COUNT, QL_AXIS_LEN, QL_INNER, QL_SIGNED, QL_ROWS };
 enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
 enum { EWF_ALPHA };
 
+struct OpState;
+
 struct LaunchCtx {
   cudaStream_t stream;
   int* d_error;     // device error word
   int64_t batch;    // rows along axis 0 this run (== plan batch unless sliced); 0: plan not batched
   int num_sms;
+  // the plan's ops and their states, and this op's index: lets an op launch
+  // the ops that follow it together (a chain); null outside a plan
+  const PlanOp* ops = nullptr;
+  const OpState* states = nullptr;
+  size_t n_ops = 0;
+  size_t index = 0;
 };
 
 // Last integer slot of every op: 1 when the op's leading (batch) extent

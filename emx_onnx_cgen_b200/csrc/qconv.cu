@@ -32,8 +32,8 @@
 //     windows in flight per SM (8 stages of one tile each).  The swizzle keeps
 //     the tensor cores' operand reads conflict-free (without it each MMA
 //     waited ~5x its math time on shared memory).
-//   * each CTA takes a contiguous range of tiles (neighbouring windows share
-//     most rows, which stay hot in L2).
+//   * each CTA takes every gridDim.x-th tile: in each round the CTAs load
+//     consecutive windows, which share most rows (hot in L2).
 //   * zero padding must mean "real zero": for zero point 128 on uint8 storage
 //     the producer stores x ^ 0x80 (= x - 128 as int8) and the MMA runs
 //     s8 x s8; for zero point 0 the MMA runs on the raw bytes (u8 or s8).
@@ -43,6 +43,8 @@
 //   * warps: 0 producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-19 epilogue
 //     (four warps per TMEM lane quarter, each taking a quarter of the OC
 //     columns).
+#include <algorithm>
+
 #include "host_util.h"
 #include "kernels.h"
 #include "qmath.cuh"
@@ -91,6 +93,20 @@ __host__ __device__ constexpr int qc_partials(int oc) { return 2 * QC_MMA_WARPS 
 __host__ __device__ constexpr int qc_epi_warp0(int oc) { return (qc_partials(oc) + 2 + 3) & ~3; }
 __host__ __device__ constexpr int qc_threads(int oc) { return 32 * (qc_epi_warp0(oc) + QC_EPI_WARPS); }
 constexpr int QC_TILE_M = 128;
+
+// A chain of up to QC_MAX_CHAIN convolutions run by one launch (see
+// qconv_chain_kernel); layer[0] also carries the geometry every layer shares.
+constexpr int QC_MAX_CHAIN = 8;
+struct QConvChainParams {
+  QConvTcParams layer[QC_MAX_CHAIN];
+  int n_layers;
+  int use_lut;   // a table buffer is in shared memory
+  int use_ring;  // a residual ring is in shared memory
+  int dlo, dhi;  // layer l+1's tile t reads rows layer l's tiles t-dlo .. t+dhi write
+  int rlo, rhi;  // tile t's residual rows were written by tiles t-rlo .. t+rhi
+  unsigned long long* state;  // [0] run epoch, [1] CTAs finished, [2 + t] progress of tile t; null for L = 1
+  int* err;
+};
 
 // bytes of a clamped integer-valued float (see float_to_byte): gather the low
 // byte of four bit patterns into one word.
@@ -157,46 +173,121 @@ __device__ __forceinline__ void qc_tmem_ld(uint32_t taddr, uint32_t (&r)[G]) {
   }
 }
 
+// Chain progress publisher (one thread): tiles every epilogue warp has
+// stored are made visible GPU-wide and their progress words advanced.  One
+// fence (which waits for the stores to drain) covers every tile completed
+// since the last one, so the fences adapt to the backlog, not the tile count.
+__device__ __forceinline__ void qc_publish(const QConvChainParams& cp, const uint32_t* s_stored,
+                                           unsigned long long* progress, int n_tiles, int t_first, int t_step) {
+  int* const err = cp.err;
+  const int L = cp.n_layers;
+  pdl_wait();
+  const unsigned long long epoch = ld_acquire_u64(cp.state);
+  const int per_layer = (n_tiles - t_first + t_step - 1) / t_step;  // tiles of this CTA
+  const uint32_t total = (uint32_t)(per_layer * (L - 1));
+  uint32_t published = 0;
+  uint64_t t_last = globaltimer_ns();
+  uint32_t spins = 0;
+  while (published < total) {
+    uint32_t done = total;
+    for (int w = 0; w < QC_EPI_WARPS; ++w) done = min(done, ld_acquire_cta_u32(&s_stored[w]));
+    if (done > published) {
+      __threadfence();
+      for (uint32_t k = published; k < done; ++k) {
+        const int l = (int)(k / (uint32_t)per_layer);
+        const int tile = t_first + (int)(k % (uint32_t)per_layer) * t_step;
+        st_relaxed_u64(progress + tile, epoch * 64ull + (unsigned)(l + 1));
+      }
+      published = done;
+      t_last = globaltimer_ns();
+      continue;
+    }
+    if ((++spins & 15u) == 0) {
+      if (error_raised(err)) break;
+      if (globaltimer_ns() - t_last > EMX_WAIT_BUDGET_NS) {
+        record_error(err, DEV_TIMEOUT_EPILOGUE);
+        break;
+      }
+    }
+    __nanosleep(32);
+  }
+}
+
+// One launch runs a chain of L convolutions with the same geometry (L = 1:
+// a single convolution).  Every CTA owns the same strided set of tiles in
+// every layer and walks the items (layer, tile) in order.  Layer l+1's tile t
+// reads rows that layer l's tiles t-dlo .. t+dhi write (and residual rows of
+// tiles t-rlo .. t+rhi of an earlier layer), so before loading them the
+// producer waits until those tiles' progress words say "layer l done";
+// the epilogue publishes a tile's progress once all its rows are stored.
+// Progress words carry the run's epoch (layers done + 64 * epoch), so no
+// reset is needed between runs: the last CTA to finish advances the epoch.
+// No layer waits on a later one, and every CTA owns at least one tile (grid
+// <= tiles), so the waits form no cycle; all waits are bounded.
 template <int CIN, int OC>
-__global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConvTcParams p) {
+__global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __grid_constant__ QConvChainParams cp) {
   constexpr int KSTEPS = CIN / 32;  // kind::i8 MMAs (K = 32) per tap
   constexpr int G = OC / 4;         // columns per epilogue warp
   // partial accumulators (= issuing warps) per tile: 2 tiles x P x OC <= 512 TMEM columns
   constexpr int P = qc_partials(OC);
-  constexpr int QC_RESID_WARP = P + 1;
-  constexpr int QC_EPI_WARP0 = qc_epi_warp0(OC);
+  constexpr int RESID_WARP = P + 1;
+  constexpr int EPI_WARP0 = qc_epi_warp0(OC);
+  // the chain's progress publisher: a warp of its own where one is free, else
+  // lane 1 of the residual producer's warp
+  constexpr int PUB_WARP = P + 2 < EPI_WARP0 ? P + 2 : RESID_WARP;
   constexpr uint32_t TMEM_COLS = 512;
   static_assert(G % 8 == 0, "OC must be a multiple of 32");
+  const QConvTcParams& g = cp.layer[0];  // geometry shared by every layer
+  const int L = cp.n_layers;
+  const bool chained = cp.state != nullptr;
+  int* const err = cp.err;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // weights: one buffer, or two for a chain (layer l uses buffer l & 1, so
+  // layer l+1's weights load while layer l's MMAs run)
+  const int wbufs = L > 1 ? 2 : 1;
+  const uint32_t wbuf_bytes = (uint32_t)align_up_dev(g.b_bytes, 1024);
   uint8_t* s_b = smem;
-  uint8_t* s_lut = smem + align_up_dev(p.b_bytes, 1024);  // 64 KB when p.lut
-  uint8_t* s_a = s_lut + (p.lut ? 65536 : 0);
-  float* s_scale = reinterpret_cast<float*>(s_a + (size_t)p.stages * p.stage_bytes);
-  int32_t* s_bias = reinterpret_cast<int32_t*>(s_scale + OC);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_bias + OC);
+  uint8_t* s_lut = smem + (size_t)wbufs * wbuf_bytes;  // 64 KB when cp.use_lut
+  uint8_t* s_a = s_lut + (cp.use_lut ? 65536 : 0);
+  // per epilogue warp, per layer parity: its G scales and biases
+  float* s_scale = reinterpret_cast<float*>(s_a + (size_t)g.stages * g.stage_bytes);
+  int32_t* s_bias = reinterpret_cast<int32_t*>(s_scale + 2 * QC_EPI_WARPS * G);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_bias + 2 * QC_EPI_WARPS * G);
   uint64_t* full = bars;
-  uint64_t* empty = bars + p.stages;
-  uint64_t* accf = bars + 2 * p.stages;
+  uint64_t* empty = bars + g.stages;
+  uint64_t* accf = bars + 2 * g.stages;
   uint64_t* acce = accf + 2;
-  uint64_t* bbar = acce + 2;
-  uint64_t* drain = bbar + 1;  // one per MMA warp
+  uint64_t* bbar = acce + 2;    // [2] weights of a layer landed in buffer b (one phase per layer using b)
+  uint64_t* lbar = bbar + 2;    // table of a layer landed (one phase per layer with a table)
+  uint64_t* wfree = lbar + 1;   // [2] MMAs of a layer using buffer b done: its weights may be replaced
+  // Epilogue warps drift up to two tiles (and two layers) apart, so the
+  // barrier they all arrive on per layer is a ring of 4: a fast warp's next
+  // arrival never lands in a phase a slow warp still owes.
+  uint64_t* lfree = wfree + 2;  // [4] epilogue done with layer l (l % 4): table may be replaced
+  uint64_t* drain = lfree + 4;  // one per MMA warp
   uint64_t* rfull = drain + QC_MMA_WARPS;
   uint64_t* rempty = rfull + QC_RSTAGES;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + QC_RSTAGES);
-  // residual ring after the barrier block (16-byte aligned)
-  uint8_t* s_r = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_holder + 4) + 127) & ~uintptr_t(127));
+  // per epilogue warp: how many published tiles it has stored (monotonic; the publisher reads them)
+  uint32_t* s_stored = tmem_holder + 4;
+  // residual ring after that (128-byte aligned)
+  uint8_t* s_r = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(s_stored + QC_EPI_WARPS) + 127) &
+                                            ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_mma = p.kh * p.kw * KSTEPS;   // MMAs per tile
-  const int PE = n_mma < P ? n_mma : P;     // partials (and issuing warps) in use
-  // contiguous tile range of this CTA
-  const int t_begin = (int)((int64_t)blockIdx.x * p.n_tiles / gridDim.x);
-  const int t_end = (int)((int64_t)(blockIdx.x + 1) * p.n_tiles / gridDim.x);
+  const int n_mma = g.kh * g.kw * KSTEPS;  // MMAs per tile
+  const int PE = n_mma < P ? n_mma : P;    // partials (and issuing warps) in use
+  const int n_tiles = g.n_tiles;
+  // tiles of this CTA in every layer: blockIdx.x, + gridDim.x, ... (strided, so
+  // that a tile's neighbours of the previous layer were done a round earlier
+  // by the neighbouring CTAs, and each round's windows are consecutive rows)
+  const int t_first = blockIdx.x, t_step = gridDim.x;
+  unsigned long long* progress = chained ? cp.state + 2 : nullptr;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
+    for (int s = 0; s < g.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], PE);  // one commit per MMA warp
     }
@@ -204,7 +295,13 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConv
       mbar_init(&accf[a], PE);
       mbar_init(&acce[a], QC_EPI_WARPS);  // one arrive per epilogue warp
     }
-    mbar_init(bbar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bbar[b], 1);
+      mbar_init(&wfree[b], PE);
+    }
+    mbar_init(lbar, 1);
+    for (int r = 0; r < 4; ++r) mbar_init(&lfree[r], QC_EPI_WARPS);
+    for (int w = 0; w < QC_EPI_WARPS; ++w) s_stored[w] = 0;
     for (int w = 0; w < QC_MMA_WARPS; ++w) mbar_init(&drain[w], 1);
     for (int r = 0; r < QC_RSTAGES; ++r) {
       mbar_init(&rfull[r], 1);
@@ -216,12 +313,6 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConv
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= QC_EPI_WARP0) {
-    for (int i = threadIdx.x - 32 * QC_EPI_WARP0; i < OC; i += 32 * QC_EPI_WARPS) {
-      s_scale[i] = p.scale[i];
-      s_bias[i] = p.bias[i];
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -230,43 +321,104 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConv
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: weights once, then one window per tile
-      mbar_arrive_expect_tx(bbar, p.b_bytes + (p.lut ? 65536u : 0u));
-      for (uint32_t off = 0; off < p.b_bytes; off += 16384u) {
-        const uint32_t n = min(16384u, p.b_bytes - off);
-        bulk_load(s_b + off, p.w_img + off, n, bbar);
+      // ---------------- producer: weights, tables and one window per tile.
+      // Weights of layers 0 and 1 load at once; those of layer l+1 after layer
+      // l's windows are issued (into the buffer layer l-1 used).  The table of
+      // the next layer with a fused add loads as soon as the epilogue is done
+      // with the previous table, at the end of the next layer's windows at the
+      // latest (so no barrier runs two phases ahead of its waiter).
+      auto issue_weights = [&](int l) {
+        const int b = l & 1;
+        mbar_arrive_expect_tx(&bbar[b], g.b_bytes);
+        for (uint32_t off = 0; off < g.b_bytes; off += 16384u)
+          bulk_load(s_b + (size_t)b * wbuf_bytes + off, cp.layer[l].w_img + off, min(16384u, g.b_bytes - off),
+                    &bbar[b]);
+      };
+      auto next_lut_layer = [&](int from) {
+        for (int m = from; m < L; ++m)
+          if (cp.layer[m].lut) return m;
+        return L;
+      };
+      auto issue_lut = [&](int m) {
+        mbar_arrive_expect_tx(lbar, 65536u);
+        for (uint32_t off = 0; off < 65536u; off += 16384u) bulk_load(s_lut + off, cp.layer[m].lut + off, 16384u, lbar);
+      };
+      int w_issued = 0, luts = 0;  // weight loads and tables issued so far
+      issue_weights(0);
+      ++w_issued;
+      if (L > 1) {
+        issue_weights(1);
+        ++w_issued;
       }
-      if (p.lut)
-        for (uint32_t off = 0; off < 65536u; off += 16384u) bulk_load(s_lut + off, p.lut + off, 16384u, bbar);
+      int lut_prev = next_lut_layer(0);  // layer whose table is (being) loaded
+      if (lut_prev < L) {
+        issue_lut(lut_prev);
+        ++luts;
+      }
+      int lut_next = lut_prev < L ? next_lut_layer(lut_prev + 1) : L;
       pdl_wait();  // activations come from the preceding kernel
+      const unsigned long long epoch = chained ? ld_acquire_u64(cp.state) : 0ull;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued = 0, parity_of = 0;  // per stage: window issued, and in which phase
-      for (int tile = t_begin; tile < t_end; ++tile) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
+      for (int l = 0; l < L && ok; ++l) {
+        const QConvTcParams& lp = cp.layer[l];
+        for (int tile = t_first; tile < n_tiles; tile += t_step) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (chained && l > 0) {  // the rows of this window are layer l-1 outputs of neighbouring tiles
+            if (!wait_flags_at_least(progress, tile - cp.dlo, tile + cp.dhi, n_tiles, epoch * 64ull + (unsigned)l,
+                                     err, DEV_TIMEOUT_GRID)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+          }
+          const int64_t row0 = (int64_t)tile * QC_TILE_M;
+          uint8_t* dst = s_a + (size_t)stage * g.stage_bytes;
+          if (row0 + g.win_rows > lp.x_rows) {  // the plan guarantees this never happens; never read past a plane
+            record_error(err, DEV_BAD_CONFIG);
+            mbar_arrive(&full[stage]);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], g.win_bytes);
+            bulk_load(dst, lp.x + (uint64_t)row0 * CIN, g.win_bytes, &full[stage]);
+          }
+          issued |= 1u << stage;
+          parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
+          if (++stage == g.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        const int64_t row0 = (int64_t)tile * QC_TILE_M;
-        uint8_t* dst = s_a + (size_t)stage * p.stage_bytes;
-        if (row0 + p.win_rows > p.x_rows) {  // the plan guarantees this never happens; never read past a plane
-          record_error(p.err, DEV_BAD_CONFIG);
-          mbar_arrive(&full[stage]);
-        } else {
-          mbar_arrive_expect_tx(&full[stage], p.win_bytes);
-          bulk_load(dst, p.x + (uint64_t)row0 * CIN, p.win_bytes, &full[stage]);
+        if (!ok) break;
+        if (l + 1 < L && l + 1 >= 2) {  // buffer (l+1) & 1 is free once layer l-1's MMAs are done
+          if (!mbar_wait(&wfree[(l + 1) & 1], (uint32_t)((l - 1) >> 1) & 1u, err, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          issue_weights(l + 1);
+          ++w_issued;
         }
-        issued |= 1u << stage;
-        parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
-        if (++stage == p.stages) {
-          stage = 0;
-          phase ^= 1u;
+        if (lut_next < L && (l >= lut_prev + 1 || lut_next == l + 1)) {
+          if (!mbar_wait(&lfree[lut_prev & 3], (uint32_t)(lut_prev >> 2) & 1u, err, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          issue_lut(lut_next);
+          ++luts;
+          lut_prev = lut_next;
+          lut_next = next_lut_layer(lut_prev + 1);
         }
       }
-      if (!ok) {  // error path: let every window this thread issued land before the CTA exits
-        for (int s2 = 0; s2 < p.stages; ++s2)
+      if (!ok) {  // error path: let every copy this thread issued land before the CTA exits
+        for (int s2 = 0; s2 < g.stages; ++s2)
           if (issued & (1u << s2)) (void)mbar_wait(&full[s2], (parity_of >> s2) & 1u, nullptr, 0);
+        for (int k = w_issued - 2 < 0 ? 0 : w_issued - 2; k < w_issued; ++k)
+          (void)mbar_wait(&bbar[k & 1], (uint32_t)(k >> 1) & 1u, nullptr, 0);
+        if (luts > 0) (void)mbar_wait(lbar, (uint32_t)(luts - 1) & 1u, nullptr, 0);
       }
     }
   } else if (warp >= 1 && warp <= PE) {
@@ -274,215 +426,287 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConv
       // ---------------- MMA issuers: warp 1+j issues MMAs k = j, j+P, j+2P, ...
       // of every tile into partial accumulator j
       const int my = warp - 1;
-      bool ok = mbar_wait(bbar, 0, p.err, DEV_TIMEOUT_MMA);
-      tc_fence_after();
+      bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       const uint32_t a_base = smem_u32(s_a);
-      const uint32_t b_base = smem_u32(s_b);
-      for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
-        const int acc = it & 1;
-        if (!mbar_wait(&acce[acc], ((it >> 1) & 1) ^ 1u, p.err, DEV_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA)) {
+      for (int l = 0; l < L && ok; ++l) {
+        const uint32_t idesc = cp.layer[l].idesc;
+        const int wb = wbufs == 2 ? (l & 1) : 0;
+        const uint32_t b_base = smem_u32(s_b + (size_t)wb * wbuf_bytes);
+        if (!mbar_wait(&bbar[wb], (uint32_t)(wbufs == 2 ? (l >> 1) : l) & 1u, err, DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // MMA number k of the tile accumulates into partial k % P (integer
-        // partial sums are exact in any order; the epilogue adds the P
-        // partials), issued by warp 1 + k % P.
-        const uint32_t d_tmem = tmem_base + (uint32_t)((acc * P + my) * OC);
-        const uint32_t a_stage = a_base + (uint32_t)stage * p.stage_bytes;
-        for (int k = my; k < n_mma; k += PE) {
-          const int tap = k / KSTEPS, s = k - tap * KSTEPS;
-          const int kh = tap / p.kw, kw = tap - kh * p.kw;
-          const uint32_t a_tap = a_stage + (uint32_t)(kh * p.wp + kw) * CIN;
-          const uint32_t b_tap = b_base + (uint32_t)tap * (OC * CIN);
-          const uint64_t adesc = smem_desc_k_swizzled(a_tap + 32u * s, CIN);
-          const uint64_t bdesc = smem_desc_k_swizzled(b_tap + 32u * s, CIN);
-          mma_i8(d_tmem, adesc, bdesc, p.idesc, k >= PE ? 1u : 0u);
+        for (int tile = t_first; tile < n_tiles; tile += t_step, ++it) {
+          const int acc = it & 1;
+          if (!mbar_wait(&acce[acc], ((it >> 1) & 1) ^ 1u, err, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&full[stage], phase, err, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // MMA number k of the tile accumulates into partial k % P (integer
+          // partial sums are exact in any order; the epilogue adds the P
+          // partials), issued by warp 1 + k % P.
+          const uint32_t d_tmem = tmem_base + (uint32_t)((acc * P + my) * OC);
+          const uint32_t a_stage = a_base + (uint32_t)stage * g.stage_bytes;
+          for (int k = my; k < n_mma; k += PE) {
+            const int tap = k / KSTEPS, s = k - tap * KSTEPS;
+            const int kh = tap / g.kw, kw = tap - kh * g.kw;
+            const uint32_t a_tap = a_stage + (uint32_t)(kh * g.wp + kw) * CIN;
+            const uint32_t b_tap = b_base + (uint32_t)tap * (OC * CIN);
+            const uint64_t adesc = smem_desc_k_swizzled(a_tap + 32u * s, CIN);
+            const uint64_t bdesc = smem_desc_k_swizzled(b_tap + 32u * s, CIN);
+            mma_i8(d_tmem, adesc, bdesc, idesc, k >= PE ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          tc_commit(&accf[acc]);
+          if (++stage == g.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        tc_commit(&empty[stage]);
-        tc_commit(&accf[acc]);
-        if (++stage == p.stages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (ok) tc_commit(&wfree[wb]);  // arrives once this warp's MMAs of layer l have read the weights
       }
       if (!ok) {  // error path: wait for this thread's MMAs before TMEM is released
         tc_commit(&drain[my]);
         (void)mbar_wait(&drain[my], 0, nullptr, 0);
       }
     }
-  } else if (warp == QC_RESID_WARP) {
-    if (lane == 0 && p.has_add && p.r_bulk) {
+  } else if (warp == PUB_WARP && PUB_WARP != RESID_WARP) {
+    if (lane == 0 && chained && L > 1) qc_publish(cp, s_stored, progress, n_tiles, t_first, t_step);
+  } else if (warp == RESID_WARP) {
+    if (PUB_WARP == RESID_WARP && lane == 1 && chained && L > 1)
+      qc_publish(cp, s_stored, progress, n_tiles, t_first, t_step);
+    if (lane == 0 && cp.use_ring) {
       // ---------------- residual producer: the tile's residual rows, one bulk copy each
       pdl_wait();  // the residual may come from the preceding kernel
+      const unsigned long long epoch = chained ? ld_acquire_u64(cp.state) : 0ull;
       int rs = 0;
       uint32_t rph = 0, issued = 0, parity_of = 0;
       bool ok = true;
       const uint32_t rbytes = (uint32_t)QC_TILE_M * OC;
-      for (int tile = t_begin; tile < t_end; ++tile) {
-        if (!mbar_wait(&rempty[rs], rph ^ 1u, p.err, DEV_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&rfull[rs], rbytes);
-        bulk_load(s_r + (size_t)rs * rbytes, p.resid + (uint64_t)((int64_t)tile * QC_TILE_M + p.r_off) * OC, rbytes,
-                  &rfull[rs]);
-        issued |= 1u << rs;
-        parity_of = (parity_of & ~(1u << rs)) | (rph << rs);
-        if (++rs == QC_RSTAGES) {
-          rs = 0;
-          rph ^= 1u;
+      for (int l = 0; l < L && ok; ++l) {
+        const QConvTcParams& lp = cp.layer[l];
+        if (!(lp.has_add && lp.r_bulk)) continue;
+        for (int tile = t_first; tile < n_tiles; tile += t_step) {
+          if (!mbar_wait(&rempty[rs], rph ^ 1u, err, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (chained && l > 0) {  // the residual may be an earlier layer's output
+            if (!wait_flags_at_least(progress, tile - cp.rlo, tile + cp.rhi, n_tiles, epoch * 64ull + (unsigned)l,
+                                     err, DEV_TIMEOUT_GRID)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+          }
+          mbar_arrive_expect_tx(&rfull[rs], rbytes);
+          bulk_load(s_r + (size_t)rs * rbytes, lp.resid + (uint64_t)((int64_t)tile * QC_TILE_M + lp.r_off) * OC,
+                    rbytes, &rfull[rs]);
+          issued |= 1u << rs;
+          parity_of = (parity_of & ~(1u << rs)) | (rph << rs);
+          if (++rs == QC_RSTAGES) {
+            rs = 0;
+            rph ^= 1u;
+          }
         }
       }
       if (!ok)
         for (int s2 = 0; s2 < QC_RSTAGES; ++s2)
           if (issued & (1u << s2)) (void)mbar_wait(&rfull[s2], (parity_of >> s2) & 1u, nullptr, 0);
     }
-  } else if (warp >= QC_EPI_WARP0) {
+  } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue: TMEM -> registers -> requant (+ QLinearAdd) -> global
+    const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;
-    const int col0 = ((warp - QC_EPI_WARP0) >> 2) * G;
+    const int col0 = (ew >> 2) * G;
     const int row = quarter * 32 + lane;
-    const int64_t hpwp = (int64_t)p.hp * p.wp;
-    const uint32_t yx4 = (uint32_t)p.y_xor * 0x01010101u;
+    const int64_t hpwp = (int64_t)g.hp * g.wp;
+    auto fetch_consts = [&](int l) {  // this warp's slice of layer l's scales and biases, parity l & 1
+      if (lane < G) {
+        cp_async4(s_scale + ((l & 1) * QC_EPI_WARPS + ew) * G + lane, cp.layer[l].scale + col0 + lane);
+        cp_async4(s_bias + ((l & 1) * QC_EPI_WARPS + ew) * G + lane, cp.layer[l].bias + col0 + lane);
+      }
+      cp_async_commit();
+    };
+    fetch_consts(0);  // plan constants: not written by the preceding kernel
+    if (L > 1) fetch_consts(1);
     pdl_wait();  // residual reads and output writes follow the preceding kernel
-    if (p.lut && !__all_sync(0xffffffffu, mbar_wait(bbar, 0, p.err, DEV_TIMEOUT_EPILOGUE))) {
-      // the add table never arrived (an error is recorded); nothing to do
-    } else {
-    int it = 0;
-    for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+    const unsigned long long epoch = chained ? ld_acquire_u64(cp.state) : 0ull;
+    int it = 0, rit = 0, luts = 0;
+    uint32_t pub = 0;
+    bool ok = true;
+    for (int l = 0; l < L && ok; ++l) {
+      const QConvTcParams& lp = cp.layer[l];
+      // this warp's scales and biases of layer l (its own slice: no cross-warp
+      // barrier), fetched asynchronously one layer ahead
+      float* sc = s_scale + ((l & 1) * QC_EPI_WARPS + ew) * G;
+      int32_t* bi = s_bias + ((l & 1) * QC_EPI_WARPS + ew) * G;
+      __syncwarp();  // every lane is done with layer l-1's slice, which layer l+1 reuses
+      if (l >= 1 && l + 1 < L) fetch_consts(l + 1);
+      if (l + 1 < L)
+        cp_async_wait_group<1>();
+      else
+        cp_async_wait_group<0>();
       __syncwarp();
-      const int acc = it & 1;
-      bool ok = mbar_wait(&accf[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_EPILOGUE);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      // the PE partial accumulators in use (PE >= 1), summed as they arrive
-      uint32_t v[G];
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * P * OC + col0);
-      {
-        uint32_t t[G];
-        qc_tmem_ld<G>(taddr, v);
-        if (PE > 1) qc_tmem_ld<G>(taddr + OC, t);
-        tmem_wait_ld();
-        if (PE > 1) {
-#pragma unroll
-          for (int c = 0; c < G; ++c) v[c] += t[c];
-        }
+      const uint32_t yx4 = (uint32_t)lp.y_xor * 0x01010101u;
+      if (lp.lut) {
+        ok = __all_sync(0xffffffffu, mbar_wait(lbar, (uint32_t)luts & 1u, err, DEV_TIMEOUT_EPILOGUE));
+        ++luts;
+        if (!ok) break;
       }
-#pragma unroll
-      for (int pp = 2; pp < P; pp += 2) {
-        if (pp < PE) {
-          uint32_t t0[G], t1[G];
-          qc_tmem_ld<G>(taddr + pp * OC, t0);
-          if (pp + 1 < PE) qc_tmem_ld<G>(taddr + (pp + 1) * OC, t1);
+      const bool rb_on = lp.has_add && lp.r_bulk;
+      const bool publish = chained && l + 1 < L;
+      for (int tile = t_first; tile < n_tiles; tile += t_step, ++it) {
+        __syncwarp();
+        const int acc = it & 1;
+        ok = mbar_wait(&accf[acc], (it >> 1) & 1, err, DEV_TIMEOUT_EPILOGUE);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // the PE partial accumulators in use (PE >= 1), summed as they arrive
+        uint32_t v[G];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * P * OC + col0);
+        {
+          uint32_t t[G];
+          qc_tmem_ld<G>(taddr, v);
+          if (PE > 1) qc_tmem_ld<G>(taddr + OC, t);
           tmem_wait_ld();
+          if (PE > 1) {
 #pragma unroll
-          for (int c = 0; c < G; ++c) v[c] += pp + 1 < PE ? t0[c] + t1[c] : t0[c];
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[acc]);
-      const bool rb_on = p.has_add && p.r_bulk;
-      const int rs = it % QC_RSTAGES;
-      if (rb_on) {
-        ok = mbar_wait(&rfull[rs], (uint32_t)(it / QC_RSTAGES) & 1u, p.err, DEV_TIMEOUT_EPILOGUE);
-        if (!__all_sync(0xffffffffu, ok)) break;
-      }
-
-      // pixel of pitched row q: divisions by Hp*Wp and Wp as multiply-shift
-      // with host-computed ceil(2^40 / d) (exact for q * d < 2^40, checked on the host)
-      const uint32_t q = (uint32_t)tile * QC_TILE_M + (uint32_t)row;
-      const int n = (int)(((uint64_t)q * p.hpwp_mul) >> 40);
-      const int rem = (int)(q - (uint32_t)n * (uint32_t)hpwp);
-      const int oh = (int)(((uint64_t)(uint32_t)rem * p.wp_mul) >> 40);
-      const int ow = rem - oh * p.wp;
-      if (n < p.batch && oh < p.oh && ow < p.ow) {
-      float r[G];
-#pragma unroll
-      for (int c4 = 0; c4 < G / 4; ++c4) {
-        const float4 sc = *reinterpret_cast<const float4*>(&s_scale[col0 + 4 * c4]);
-        const int4 bi = *reinterpret_cast<const int4*>(&s_bias[col0 + 4 * c4]);
-        r[4 * c4 + 0] = requant_fast((int32_t)v[4 * c4 + 0] + bi.x, sc.x, p.y_m_minus_zero, p.y_lo, p.y_hi);
-        r[4 * c4 + 1] = requant_fast((int32_t)v[4 * c4 + 1] + bi.y, sc.y, p.y_m_minus_zero, p.y_lo, p.y_hi);
-        r[4 * c4 + 2] = requant_fast((int32_t)v[4 * c4 + 2] + bi.z, sc.z, p.y_m_minus_zero, p.y_lo, p.y_hi);
-        r[4 * c4 + 3] = requant_fast((int32_t)v[4 * c4 + 3] + bi.w, sc.w, p.y_m_minus_zero, p.y_lo, p.y_hi);
-      }
-      if (p.has_add) {
-        uint32_t rb[G / 4];
-        if (p.r_bulk) {
-          const uint8_t* rrow = s_r + ((size_t)rs * QC_TILE_M + row) * OC;
-          const int64_t rpix = (int64_t)q + p.r_off;
-          if constexpr (G == 8) {
-            const uint2 t = *reinterpret_cast<const uint2*>(rrow + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
-            rb[0] = t.x;
-            rb[1] = t.y;
-          } else {
-#pragma unroll
-            for (int c = 0; c < G / 16; ++c) {
-              const uint4 t = *reinterpret_cast<const uint4*>(rrow + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
-              rb[4 * c + 0] = t.x;
-              rb[4 * c + 1] = t.y;
-              rb[4 * c + 2] = t.z;
-              rb[4 * c + 3] = t.w;
-            }
+            for (int c = 0; c < G; ++c) v[c] += t[c];
           }
-        } else {
-          qc_load_resid<OC, G>(p, rb, col0, n, oh, ow);
         }
-        if (p.lut) {
-          // out byte = table[(conv byte << 8) | residual byte]
-          uint32_t out[G / 4];
+#pragma unroll
+        for (int pp = 2; pp < P; pp += 2) {
+          if (pp < PE) {
+            uint32_t t0[G], t1[G];
+            qc_tmem_ld<G>(taddr + pp * OC, t0);
+            if (pp + 1 < PE) qc_tmem_ld<G>(taddr + (pp + 1) * OC, t1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < G; ++c) v[c] += pp + 1 < PE ? t0[c] + t1[c] : t0[c];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[acc]);
+        const int rs = rit % QC_RSTAGES;
+        if (rb_on) {
+          ok = mbar_wait(&rfull[rs], (uint32_t)(rit / QC_RSTAGES) & 1u, err, DEV_TIMEOUT_EPILOGUE);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+        }
+
+        // pixel of pitched row q: divisions by Hp*Wp and Wp as multiply-shift
+        // with host-computed ceil(2^40 / d) (exact for q * d < 2^40, checked on the host)
+        const uint32_t q = (uint32_t)tile * QC_TILE_M + (uint32_t)row;
+        const int n = (int)(((uint64_t)q * g.hpwp_mul) >> 40);
+        const int rem = (int)(q - (uint32_t)n * (uint32_t)hpwp);
+        const int oh = (int)(((uint64_t)(uint32_t)rem * g.wp_mul) >> 40);
+        const int ow = rem - oh * g.wp;
+        if (n < g.batch && oh < g.oh && ow < g.ow) {
+          float r[G];
 #pragma unroll
           for (int c4 = 0; c4 < G / 4; ++c4) {
-            uint32_t word = 0;
+            const float4 s4 = *reinterpret_cast<const float4*>(&sc[4 * c4]);
+            const int4 b4 = *reinterpret_cast<const int4*>(&bi[4 * c4]);
+            r[4 * c4 + 0] = requant_fast((int32_t)v[4 * c4 + 0] + b4.x, s4.x, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
+            r[4 * c4 + 1] = requant_fast((int32_t)v[4 * c4 + 1] + b4.y, s4.y, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
+            r[4 * c4 + 2] = requant_fast((int32_t)v[4 * c4 + 2] + b4.z, s4.z, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
+            r[4 * c4 + 3] = requant_fast((int32_t)v[4 * c4 + 3] + b4.w, s4.w, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
+          }
+          uint32_t out[G / 4];
+          if (lp.has_add) {
+            uint32_t rb[G / 4];
+            if (lp.r_bulk) {
+              const uint8_t* rrow = s_r + ((size_t)rs * QC_TILE_M + row) * OC;
+              const int64_t rpix = (int64_t)q + lp.r_off;
+              if constexpr (G == 8) {
+                const uint2 t = *reinterpret_cast<const uint2*>(rrow + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
+                rb[0] = t.x;
+                rb[1] = t.y;
+              } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int c = 4 * c4 + j;
-              const uint32_t ab = float_to_byte(r[c]);
-              const uint32_t bb = ((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu;
-              word |= (uint32_t)s_lut[(ab << 8) | bb] << (8 * j);
+                for (int c = 0; c < G / 16; ++c) {
+                  const uint4 t = *reinterpret_cast<const uint4*>(rrow + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
+                  rb[4 * c + 0] = t.x;
+                  rb[4 * c + 1] = t.y;
+                  rb[4 * c + 2] = t.z;
+                  rb[4 * c + 3] = t.w;
+                }
+              }
+            } else {
+              qc_load_resid<OC, G>(lp, rb, col0, n, oh, ow);
             }
-            out[c4] = word ^ yx4;
+            if (lp.lut) {
+              // out byte = table[(conv byte << 8) | residual byte]
+#pragma unroll
+              for (int c4 = 0; c4 < G / 4; ++c4) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const int c = 4 * c4 + j;
+                  const uint32_t ab = float_to_byte(r[c]);
+                  const uint32_t bb = ((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)lp.r_xor) & 0xFFu;
+                  word |= (uint32_t)s_lut[(ab << 8) | bb] << (8 * j);
+                }
+                out[c4] = word ^ yx4;
+              }
+            } else {
+              if (lp.fast_div) {
+#pragma unroll
+                for (int c = 0; c < G; ++c) {
+                  const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)lp.r_xor) & 0xFFu, lp.r_signed);
+                  r[c] = qadd_fast<true>(r[c], lp.c_zero, lp.c_scale, rv, lp.r_zero, lp.r_scale, lp.add_scale,
+                                         lp.add_inv_scale, lp.add_zero, lp.add_lo, lp.add_hi);
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < G; ++c) {
+                  const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)lp.r_xor) & 0xFFu, lp.r_signed);
+                  r[c] = qadd_fast<false>(r[c], lp.c_zero, lp.c_scale, rv, lp.r_zero, lp.r_scale, lp.add_scale,
+                                          lp.add_inv_scale, lp.add_zero, lp.add_lo, lp.add_hi);
+                }
+              }
+#pragma unroll
+              for (int c4 = 0; c4 < G / 4; ++c4)
+                out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
+            }
+          } else {
+#pragma unroll
+            for (int c4 = 0; c4 < G / 4; ++c4)
+              out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
           }
-          qc_store<OC, G>(p, out, col0, n, oh, ow);
-          goto tile_done;
+          qc_store<OC, G>(lp, out, col0, n, oh, ow);
         }
-        if (p.fast_div) {
-#pragma unroll
-          for (int c = 0; c < G; ++c) {
-            const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
-            r[c] = qadd_fast<true>(r[c], p.c_zero, p.c_scale, rv, p.r_zero, p.r_scale, p.add_scale, p.add_inv_scale,
-                                   p.add_zero, p.add_lo, p.add_hi);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < G; ++c) {
-            const int rv = load_8bit(((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)p.r_xor) & 0xFFu, p.r_signed);
-            r[c] = qadd_fast<false>(r[c], p.c_zero, p.c_scale, rv, p.r_zero, p.r_scale, p.add_scale,
-                                    p.add_inv_scale, p.add_zero, p.add_lo, p.add_hi);
-          }
+        if (rb_on) {  // this warp is done with the tile's residual rows
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rempty[rs]);
+          ++rit;
+        }
+        if (publish) {  // this warp's rows of the tile are stored: tell the publisher
+          fence_proxy_async_global();
+          __syncwarp();
+          ++pub;
+          if (lane == 0) st_release_cta_u32(&s_stored[ew], (uint32_t)pub);
         }
       }
-      uint32_t out[G / 4];
-#pragma unroll
-      for (int c4 = 0; c4 < G / 4; ++c4)
-        out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
-      qc_store<OC, G>(p, out, col0, n, oh, ow);
-      }
-    tile_done:
-      if (rb_on) {  // this warp is done with the tile's residual rows
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rempty[rs]);
-      }
-    }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&lfree[l & 3]);  // this warp is done with layer l's table
     }
   }
 
@@ -491,6 +715,16 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_tc_kernel(const QConv
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (chained && threadIdx.x == 0) {
+    // the last CTA to finish advances the run epoch (read by the next run after its pdl_wait)
+    __threadfence();
+    const unsigned long long done = atomicAdd(cp.state + 1, 1ull);
+    if (done == gridDim.x - 1) {
+      cp.state[1] = 0ull;
+      __threadfence();
+      atomicAdd(cp.state, 1ull);
+    }
   }
 }
 
@@ -523,25 +757,28 @@ struct QConvTcState {
 };
 static_assert(sizeof(QConvTcState) <= sizeof(OpState), "state fits");
 
-typedef void (*QcKernel)(const QConvTcParams);
+typedef void (*QcKernel)(const QConvChainParams);
 struct QcVariant {
   int cin, oc;
   QcKernel fn;
 };
 static const QcVariant kQcVariants[] = {
-    {32, 32, qconv_tc_kernel<32, 32>},   {32, 64, qconv_tc_kernel<32, 64>},
-    {64, 32, qconv_tc_kernel<64, 32>},   {64, 64, qconv_tc_kernel<64, 64>},
-    {64, 128, qconv_tc_kernel<64, 128>}, {128, 64, qconv_tc_kernel<128, 64>},
-    {128, 128, qconv_tc_kernel<128, 128>},
+    {32, 32, qconv_chain_kernel<32, 32>},   {32, 64, qconv_chain_kernel<32, 64>},
+    {64, 32, qconv_chain_kernel<64, 32>},   {64, 64, qconv_chain_kernel<64, 64>},
+    {64, 128, qconv_chain_kernel<64, 128>}, {128, 64, qconv_chain_kernel<128, 64>},
+    {128, 128, qconv_chain_kernel<128, 128>},
 };
+constexpr size_t QC_SMEM_BUDGET = 210 * 1024;
+constexpr size_t QC_SMEM_MAX = 227 * 1024;
 
+// Shared memory of qconv_chain_kernel (the layout at its top).
 static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_bytes, int oc, bool resid_ring,
-                               bool lut) {
+                               bool lut, int wbufs = 1) {
   size_t s = 1024;  // alignment slack
-  s += align_up(b_bytes, 1024) + (lut ? 65536 : 0);
+  s += (size_t)wbufs * align_up(b_bytes, 1024) + (lut ? 65536 : 0);
   s += (size_t)stages * stage_bytes;
-  s += (size_t)oc * 8;
-  s += (size_t)(2 * stages + 5 + QC_MMA_WARPS + 2 * QC_RSTAGES) * 8 + 16;
+  s += (size_t)2 * QC_EPI_WARPS * (oc / 4) * 8;  // per-warp scales + biases, two layer parities
+  s += (size_t)(2 * stages + 4 + 5 + 4 + QC_MMA_WARPS + 2 * QC_RSTAGES) * 8 + 16 + 4 * QC_EPI_WARPS;
   if (resid_ring) s += 128 + (size_t)QC_RSTAGES * QC_TILE_M * oc;
   return s;
 }
@@ -638,7 +875,7 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
   if (op.ip[QC_X_ROWS] < rows_needed)
     return fail(msg, n, 2, "input planes have %lld rows, windows need %lld", (long long)op.ip[QC_X_ROWS],
                 (long long)rows_needed);
-  const size_t budget = 210 * 1024;
+  const size_t budget = QC_SMEM_BUDGET;
   int stages = 8;
   // fused-add helpers in shared memory only where at least 4 window stages remain
   bool lut = op.ip[QC_HAS_ADD] != 0 && op.t[5] >= 0;
@@ -650,10 +887,11 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
   while (stages > 2 && qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc, ring, lut) > budget) --stages;
   st->stages = stages;
   st->smem_bytes = qconv_smem_bytes(st->b_bytes, stages, st->stage_bytes, oc, ring, lut);
-  if (st->smem_bytes > 227 * 1024)
+  if (st->smem_bytes > QC_SMEM_MAX)
     return fail(msg, n, 5, "QLinearConv tensor-core path needs %zu B smem", st->smem_bytes);
+  // a chain launch may combine a table and a residual ring of different members: allow the maximum
   cudaError_t e = cudaFuncSetAttribute(kQcVariants[st->variant].fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)st->smem_bytes);
+                                       (int)QC_SMEM_MAX);
   if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   st->fast_div = 0;
   if (op.ip[QC_HAS_ADD]) {
@@ -673,15 +911,117 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
   return 0;
 }
 
-int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, const LaunchCtx& ctx, int* launches) {
-  const QConvTcState* st = reinterpret_cast<const QConvTcState*>(st_);
-  QConvTcParams p{};
+static int floor_div(int64_t a, int64_t b) { return (int)(a >= 0 ? a / b : -((-a + b - 1) / b)); }
+
+// One member launched alone (a chain of one).
+static int launch_single(const PlanOp& op, void* const* ptrs, const QConvTcState* st, const LaunchCtx& ctx,
+                         int* launches) {
+  QConvChainParams cp{};
+  QConvTcParams& p = cp.layer[0];
   fill_params(p, op, ptrs, st, eff_batch(ctx, op, op.ip[QC_N]));
-  p.err = ctx.d_error;
   if (p.n_tiles <= 0) return 0;
+  cp.n_layers = 1;
+  cp.use_lut = p.lut != nullptr;
+  cp.use_ring = p.has_add && p.r_bulk;
+  cp.err = ctx.d_error;
   const int grid = p.n_tiles < ctx.num_sms ? p.n_tiles : ctx.num_sms;
   cudaError_t e = launch_pdl(kQcVariants[st->variant].fn, dim3(grid), dim3(qc_threads(kQcVariants[st->variant].oc)),
-                             st->smem_bytes, ctx.stream, p);
+                             st->smem_bytes, ctx.stream, cp);
+  ++*launches;
+  return e == cudaSuccess ? 0 : 4;
+}
+
+// The chain headed by `op` (ctx.index) as one launch; false when the members
+// do not qualify (the caller then launches them one by one).
+static bool build_chain(const PlanOp& op, void* const* ptrs, const LaunchCtx& ctx, int L, QConvChainParams& cp,
+                        size_t* smem, const QConvTcState** head_st) {
+  const QConvTcState* st0 = reinterpret_cast<const QConvTcState*>(&ctx.states[ctx.index]);
+  *head_st = st0;
+  if (L > QC_MAX_CHAIN || op.t[6] < 0) return false;
+  const int64_t batch = eff_batch(ctx, op, op.ip[QC_N]);
+  bool any_lut = false, any_add = false;
+  for (int k = 0; k < L; ++k) {
+    const PlanOp& m = ctx.ops[ctx.index + k];
+    const QConvTcState* st = reinterpret_cast<const QConvTcState*>(&ctx.states[ctx.index + k]);
+    if (m.kernel != op.kernel || st->variant != st0->variant) return false;
+    for (int f : {QC_N, QC_CIN, QC_OC, QC_KH, QC_KW, QC_HP, QC_WP, QC_OH, QC_OW})
+      if (m.ip[f] != op.ip[f]) return false;
+    if (k > 0 && m.t[0] != ctx.ops[ctx.index + k - 1].t[4]) return false;  // layer k reads layer k-1's output
+    if (k + 1 < L && m.ip[QC_Y_LAYOUT] != 0) return false;
+    QConvTcParams& p = cp.layer[k];
+    fill_params(p, m, ptrs, st, batch);
+    if (p.has_add) {  // chained adds read their residual rows by bulk copy (the ring)
+      any_add = true;
+      if (m.ip[QC_R_HP] != m.ip[QC_HP] || m.ip[QC_R_WP] != m.ip[QC_WP]) return false;
+      p.r_off = (int64_t)p.r_pt * p.wp + p.r_pl;
+      const int64_t last_row = (int64_t)((m.ip[QC_N] * (int64_t)p.hp * p.wp + QC_TILE_M - 1) / QC_TILE_M) *
+                                   QC_TILE_M + p.r_off;
+      if (last_row > m.ip[QC_R_ROWS]) return false;
+      p.r_bulk = 1;
+      p.lut = m.t[5] >= 0 ? (const uint8_t*)ptrs[m.t[5]] : nullptr;
+      any_lut = any_lut || p.lut != nullptr;
+    }
+  }
+  // shared memory: weights + (table) + ring + as many window stages as fit, at least 2
+  const QConvTcParams& g = cp.layer[0];
+  const int oc = (int)op.ip[QC_OC];
+  // (two weight buffers; a window takes well under a tile's MMA time to land, so 3 stages keep the MMAs fed)
+  bool lut = any_lut;
+  if (lut && qconv_smem_bytes(st0->b_bytes, 3, st0->stage_bytes, oc, any_add, true, 2) > QC_SMEM_MAX) lut = false;
+  int stages = 8;
+  while (stages > 2 && qconv_smem_bytes(st0->b_bytes, stages, st0->stage_bytes, oc, any_add, lut, 2) > QC_SMEM_MAX)
+    --stages;
+  *smem = qconv_smem_bytes(st0->b_bytes, stages, st0->stage_bytes, oc, any_add, lut, 2);
+  if (*smem > QC_SMEM_MAX) return false;
+  for (int k = 0; k < L; ++k) {
+    cp.layer[k].stages = stages;
+    if (!lut) cp.layer[k].lut = nullptr;
+  }
+  cp.n_layers = L;
+  cp.use_lut = lut;
+  cp.use_ring = any_add;
+  // rows of layer l's window, written by layer l-1 at output row q + off for pitched row q
+  const int kh = g.kh, kw = g.kw;
+  const int64_t win_true = QC_TILE_M + (int64_t)(kh - 1) * g.wp + kw - 1;
+  int dlo = 0, dhi = 0;
+  for (int k = 0; k + 1 < L; ++k) {
+    const QConvTcParams& p = cp.layer[k];
+    const int64_t off = (int64_t)p.y_pt * p.y_wp + p.y_pl;
+    if (p.y_hp != g.hp || p.y_wp != g.wp) return false;  // the next layer reads it in the shared geometry
+    dlo = std::max(dlo, -floor_div(-off, QC_TILE_M));
+    dhi = std::max(dhi, floor_div(win_true - 1 - off, QC_TILE_M));
+  }
+  cp.dlo = dlo;
+  cp.dhi = dhi;
+  cp.rlo = 0;  // a chained residual has the shared geometry: tile t's rows are tile t's outputs
+  cp.rhi = 0;
+  cp.state = (unsigned long long*)ptrs[op.t[6]];
+  cp.err = ctx.d_error;
+  return true;
+}
+
+int launch_qconv_tc(const PlanOp& op, void* const* ptrs, const OpState* st_, const LaunchCtx& ctx, int* launches) {
+  const QConvTcState* st = reinterpret_cast<const QConvTcState*>(st_);
+  const int64_t chain = op.ip[QC_CHAIN];
+  if (chain < 0) return 0;  // a chain member: launched by the chain's first op
+  if (chain <= 1) return launch_single(op, ptrs, st, ctx, launches);
+  if (!ctx.ops || ctx.index + (size_t)chain > ctx.n_ops) return 5;
+  QConvChainParams cp{};
+  size_t smem = 0;
+  const QConvTcState* st0 = nullptr;
+  if (!build_chain(op, ptrs, ctx, (int)chain, cp, &smem, &st0)) {
+    for (int k = 0; k < chain; ++k) {
+      int rc = launch_single(ctx.ops[ctx.index + k], ptrs,
+                             reinterpret_cast<const QConvTcState*>(&ctx.states[ctx.index + k]), ctx, launches);
+      if (rc) return rc;
+    }
+    return 0;
+  }
+  const int n_tiles = cp.layer[0].n_tiles;
+  if (n_tiles <= 0) return 0;
+  const int grid = n_tiles < ctx.num_sms ? n_tiles : ctx.num_sms;
+  cudaError_t e = launch_pdl(kQcVariants[st0->variant].fn, dim3(grid), dim3(qc_threads(kQcVariants[st0->variant].oc)),
+                             smem, ctx.stream, cp);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }

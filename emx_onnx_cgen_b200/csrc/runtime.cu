@@ -259,9 +259,13 @@ void destroy(emx_plan* p) {
 // events measure kernels rather than host launch gaps.
 int launch_ops(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches) {
   emx::LaunchCtx ctx{stream, p->d_error, run_batch, p->num_sms};
+  ctx.ops = p->ops.data();
+  ctx.states = p->states.data();
+  ctx.n_ops = p->ops.size();
   const int seq = ++p->hold_seq;
   if (p->profiling) emx::launch_hold(p->d_hold, seq, p->d_error, stream);
   for (size_t i = 0; i < p->ops.size(); ++i) {
+    ctx.index = i;
     if (p->profiling) cudaEventRecord(p->ev_begin[i], stream);
     int rc = p->entries[i]->launch(p->ops[i], p->ptrs.data(), &p->states[i], ctx, launches);
     if (p->profiling) cudaEventRecord(p->ev_end[i], stream);

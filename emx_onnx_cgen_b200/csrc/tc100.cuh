@@ -98,6 +98,70 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// ----------------------------------------------------------------- cross-CTA flags
+// Generic-proxy writes of this thread are ordered before later async-proxy
+// (bulk copy) accesses to global memory, and vice versa.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_cta_u32(uint32_t* smem_p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(smem_p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_cta_u32(const uint32_t* smem_p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(smem_p)) : "memory");
+  return v;
+}
+
+// Wait until flags[i] >= target for every i in [lo, hi] (clipped to [0, n)).
+// The flags are read 8 at a time with independent loads (one memory round
+// trip for a typical range), then any that are not there yet are polled.
+// Returns false (recording `code`) when the budget runs out or another role
+// already failed.
+__device__ __forceinline__ bool wait_flags_at_least(const unsigned long long* flags, int lo, int hi, int n,
+                                                    unsigned long long target, int* err, int code) {
+  if (lo < 0) lo = 0;
+  if (hi > n - 1) hi = n - 1;
+  for (int base = lo; base <= hi; base += 8) {
+    unsigned long long v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = base + j <= hi ? ld_acquire_u64(flags + base + j) : target;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (v[j] >= target) continue;
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_u64(flags + base + j) < target) {
+        if ((++spins & 15u) == 0) {
+          if (error_raised(err)) return false;
+          if (globaltimer_ns() - t0 > EMX_WAIT_BUDGET_NS) {
+            record_error(err, code);
+            return false;
+          }
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  return true;
+}
+
 // ----------------------------------------------------------------- TMA / bulk
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y) {
@@ -115,6 +179,16 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
           smem_u32(smem_dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+// 4-byte asynchronous copy global -> shared (cp.async), grouped by commit.
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Plain (untiled) bulk copy global -> shared; dst/src 16-byte aligned, bytes % 16 == 0.

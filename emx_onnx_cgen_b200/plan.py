@@ -329,14 +329,18 @@ class _Padded:
 class B200PlanEmitter:
     """Emit target producing a B200 launch plan from a LoweredModel."""
 
-    def __init__(self, *, use_tensor_cores: bool = True, nbits_rounded_dequant: bool = False):
+    def __init__(self, *, use_tensor_cores: bool = True, nbits_rounded_dequant: bool = False,
+                 chain_convs: bool = True):
         """``nbits_rounded_dequant``: MatMulNBits multiplies fp16-rounded
         dequantised weights (one MMA per K slice, about 2x the throughput)
         instead of the exact hi + lo split; outputs then differ from the
         reference by up to ~2^-12 of sum_k |a_k * deq_k| rather than by
-        summation order only."""
+        summation order only.  ``chain_convs``: consecutive tensor-core
+        convolutions of one geometry run as one persistent launch (outputs
+        are identical either way)."""
         self.use_tensor_cores = use_tensor_cores
         self.nbits_rounded_dequant = nbits_rounded_dequant
+        self.chain_convs = chain_convs
 
     # ------------------------------------------------------------------ entry
     def emit_plan(self, model) -> Plan:
@@ -381,6 +385,8 @@ class B200PlanEmitter:
         for name in out_names:
             if name not in self._written_outputs:
                 raise UnsupportedOpError(f"graph output {name} is not produced by any op")
+        if self.chain_convs:
+            self._mark_qconv_chains()
         if batch > 0 and not b.all_batched:
             # some op's leading extent is not the batch: the plan runs whole only
             batch, flags = 0, 0
@@ -750,6 +756,55 @@ class B200PlanEmitter:
                    batched=n == self._batch)
         if padded_out is False and out_name in self._need_pad:
             self._padded_of(out_name)  # consumers also need the NHWC copy
+
+    # ------------------------------------------------------------------ conv chains
+    QC_MAX_CHAIN = 8
+    _QC_GEOMETRY = ("QC_N", "QC_CIN", "QC_OC", "QC_KH", "QC_KW", "QC_HP", "QC_WP", "QC_OH", "QC_OW")
+
+    def _mark_qconv_chains(self):
+        """Consecutive tensor-core convolutions where each reads the previous
+        one's (swizzled NHWC) output, with one geometry, run as one persistent
+        launch: the first op gets QC_CHAIN = length and a zeroed state tensor
+        (run epoch, finished CTAs, one progress word per 128-row tile), the
+        others QC_CHAIN = -1.  Fused adds in a chain must read a residual in
+        the same padded geometry."""
+        ops = self._b.ops
+        geom = [getattr(K, f) for f in self._QC_GEOMETRY]
+
+        def member_ok(o, head):
+            if o.kernel != K.K_QCONV_TC or any(o.ip.get(f) != head.ip.get(f) for f in geom):
+                return False
+            if o.ip.get(K.IP_BATCHED_SLOT) != head.ip.get(K.IP_BATCHED_SLOT):
+                return False
+            if o.ip.get(K.QC_HAS_ADD) and (o.ip.get(K.QC_R_HP) != o.ip[K.QC_HP] or o.ip.get(K.QC_R_WP) != o.ip[K.QC_WP]):
+                return False
+            return True
+
+        i = 0
+        while i < len(ops):
+            head = ops[i]
+            if not member_ok(head, head):
+                i += 1
+                continue
+            j = i
+            while (j + 1 < len(ops) and j + 1 - i < self.QC_MAX_CHAIN and member_ok(ops[j + 1], head)
+                   and ops[j + 1].tensors[0] == ops[j].tensors[4] and ops[j].ip.get(K.QC_Y_LAYOUT, 0) == 0
+                   and ops[j].ip.get(K.QC_Y_HP) == head.ip[K.QC_HP] and ops[j].ip.get(K.QC_Y_WP) == head.ip[K.QC_WP]):
+                j += 1
+            n_layers = j - i + 1
+            if n_layers > 1:
+                ip = head.ip
+                q_end = (ip[K.QC_N] - 1) * ip[K.QC_HP] * ip[K.QC_WP] + (ip[K.QC_OH] - 1) * ip[K.QC_WP] + ip[K.QC_OW]
+                n_tiles = -(-q_end // 128)
+                t_state = self._b.arena_tensor(T_TEMP, "u8", (8 * (2 + n_tiles),), name=f"conv-chain{i}:state")
+                head.tensors = head.tensors + [-1] * (7 - len(head.tensors))
+                head.tensors[6] = t_state
+                head.ip[K.QC_CHAIN] = n_layers
+                head.label += f" [chain of {n_layers}: one launch]"
+                for k in range(i + 1, j + 1):
+                    ops[k].ip[K.QC_CHAIN] = -1
+                    ops[k].label += " [in chain]"
+            i = j + 1
 
     # ------------------------------------------------------------------ QLinearAdd (standalone)
     def _emit_QLinearAddOp(self, i, op):

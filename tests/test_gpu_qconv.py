@@ -4,7 +4,7 @@ the CPU restatement at sizes and parameters the fixtures do not cover."""
 import numpy as np
 import pytest
 
-from emx_onnx_cgen_b200 import workloads as W
+from emx_onnx_cgen_b200 import kernel_ids as K, workloads as W
 from emx_onnx_cgen_b200.runtime import Session
 from golden_util import cases, load
 from gpu_util import assert_bitexact, plan_for, require_gpu
@@ -73,7 +73,8 @@ def test_batch_slices_and_device_pointers():
     s.run_ptrs([xd.data_ptr()], [yd.data_ptr()], stream=st.cuda_stream)
     s.sync()
     assert_bitexact(yd.cpu().numpy(), ref, "device pointers")
-    assert s.info().launches_per_run == 5
+    # the layout kernel, then the four convolutions as one chain launch
+    assert s.info().launches_per_run == sum(1 for op in s.plan.ops if op.ip.get(K.QC_CHAIN, 0) >= 0) == 2
 
 
 def test_graph_replay_matches_direct_launches():
@@ -109,3 +110,32 @@ def test_repeated_runs_are_identical():
     a = s.run(x)["Y"]
     for _ in range(3):
         assert_bitexact(s.run(x)["Y"], a, "rerun")
+
+
+@pytest.mark.parametrize("kw", [
+    dict(batch=4, channels=64, height=56, width=56, n_convs=5, wscale_range=(0.0001, 0.001)),
+    dict(batch=3, channels=64, height=20, width=20, n_convs=2),
+    dict(batch=2, channels=32, height=7, width=130, n_convs=3, wscale_range=(0.0001, 0.001)),
+    dict(batch=1, channels=128, height=9, width=23, n_convs=4, wscale_range=(0.00002, 0.0002)),
+    dict(batch=33, channels=64, height=8, width=8, n_convs=6, wscale_range=(0.0001, 0.001)),
+])
+def test_chain_matches_separate_launches_and_port(kw):
+    """A conv stack run as one persistent launch (layers ordered by per-tile
+    progress words) gives the bytes of one launch per conv and of the CPU
+    restatement, on every run (the progress words carry a run epoch)."""
+    require_gpu()
+    wl = W.qconv_stack_int8(**kw)
+    x = wl.make_inputs(5)
+    ref = oracle.run_graph(wl.graph, x)["Y"]
+    chained = plan_for(wl)
+    heads = [op for op in chained.ops if op.ip.get(K.QC_CHAIN, 0) > 1]
+    assert len(heads) == 1 and heads[0].ip[K.QC_CHAIN] == kw["n_convs"], chained.describe()
+    s = Session(chained)
+    for run in range(3):
+        assert_bitexact(s.run(x)["Y"], ref, f"chained run {run} {kw}")
+    sep = plan_for(wl, chain_convs=False)
+    assert not any(op.ip.get(K.QC_CHAIN, 0) for op in sep.ops)
+    assert_bitexact(Session(sep).run(x)["Y"], ref, f"separate {kw}")
+    # a second input through the same chained session: nothing of the first run leaks
+    x2 = wl.make_inputs(6)
+    assert_bitexact(s.run(x2)["Y"], oracle.run_graph(wl.graph, x2)["Y"], f"chained second input {kw}")
