@@ -652,18 +652,19 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
               qc_load_resid<OC, G>(lp, rb, col0, n, oh, ow);
             }
             if (lp.lut) {
-              // out byte = table[(conv byte << 8) | residual byte]
+              // out byte = table[(conv byte << 8) | residual byte]: the conv
+              // bytes packed four to a word, the 16-bit indices of two
+              // channels built by one byte permute from the two words
+              const uint32_t rx4 = (uint32_t)lp.r_xor * 0x01010101u;
 #pragma unroll
               for (int c4 = 0; c4 < G / 4; ++c4) {
-                uint32_t word = 0;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const int c = 4 * c4 + j;
-                  const uint32_t ab = float_to_byte(r[c]);
-                  const uint32_t bb = ((rb[c >> 2] >> (8 * (c & 3))) ^ (uint32_t)lp.r_xor) & 0xFFu;
-                  word |= (uint32_t)s_lut[(ab << 8) | bb] << (8 * j);
-                }
-                out[c4] = word ^ yx4;
+                const uint32_t cw = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]);
+                const uint32_t rw = rb[c4] ^ rx4;
+                const uint32_t t01 = __byte_perm(rw, cw, 0x5140);  // [r0, c0, r1, c1]
+                const uint32_t t23 = __byte_perm(rw, cw, 0x7362);  // [r2, c2, r3, c3]
+                const uint32_t b0 = s_lut[t01 & 0xFFFFu], b1 = s_lut[t01 >> 16];
+                const uint32_t b2 = s_lut[t23 & 0xFFFFu], b3 = s_lut[t23 >> 16];
+                out[c4] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410) ^ yx4;
               }
             } else {
               if (lp.fast_div) {
