@@ -271,9 +271,11 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + QC_RSTAGES);
   // per epilogue warp: how many published tiles it has stored (monotonic; the publisher reads them)
   uint32_t* s_stored = tmem_holder + 4;
+  // per MMA k of a tile: byte offsets of its A (window) and B (weights) operands
+  uint32_t* s_koff = s_stored + QC_EPI_WARPS;  // [2 * MMAs per tile]
   // residual ring after that (128-byte aligned)
-  uint8_t* s_r = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(s_stored + QC_EPI_WARPS) + 127) &
-                                            ~uintptr_t(127));
+  uint8_t* s_r = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(s_koff + 2 * g.kh * g.kw * KSTEPS) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -302,6 +304,12 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
     mbar_init(lbar, 1);
     for (int r = 0; r < 4; ++r) mbar_init(&lfree[r], QC_EPI_WARPS);
     for (int w = 0; w < QC_EPI_WARPS; ++w) s_stored[w] = 0;
+    for (int k = 0; k < g.kh * g.kw * KSTEPS; ++k) {
+      const int tap = k / KSTEPS, s = k - tap * KSTEPS;
+      const int kh = tap / g.kw, kw = tap - kh * g.kw;
+      s_koff[2 * k] = (uint32_t)(kh * g.wp + kw) * CIN + 32u * s;
+      s_koff[2 * k + 1] = (uint32_t)tap * (OC * CIN) + 32u * s;
+    }
     for (int w = 0; w < QC_MMA_WARPS; ++w) mbar_init(&drain[w], 1);
     for (int r = 0; r < QC_RSTAGES; ++r) {
       mbar_init(&rfull[r], 1);
@@ -457,12 +465,8 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
           const uint32_t d_tmem = tmem_base + (uint32_t)((acc * P + my) * OC);
           const uint32_t a_stage = a_base + (uint32_t)stage * g.stage_bytes;
           for (int k = my; k < n_mma; k += PE) {
-            const int tap = k / KSTEPS, s = k - tap * KSTEPS;
-            const int kh = tap / g.kw, kw = tap - kh * g.kw;
-            const uint32_t a_tap = a_stage + (uint32_t)(kh * g.wp + kw) * CIN;
-            const uint32_t b_tap = b_base + (uint32_t)tap * (OC * CIN);
-            const uint64_t adesc = smem_desc_k_swizzled(a_tap + 32u * s, CIN);
-            const uint64_t bdesc = smem_desc_k_swizzled(b_tap + 32u * s, CIN);
+            const uint64_t adesc = smem_desc_k_swizzled(a_stage + s_koff[2 * k], CIN);
+            const uint64_t bdesc = smem_desc_k_swizzled(b_base + s_koff[2 * k + 1], CIN);
             mma_i8(d_tmem, adesc, bdesc, idesc, k >= PE ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
@@ -780,6 +784,7 @@ static size_t qconv_smem_bytes(uint32_t b_bytes, int stages, uint32_t stage_byte
   s += (size_t)stages * stage_bytes;
   s += (size_t)2 * QC_EPI_WARPS * (oc / 4) * 8;  // per-warp scales + biases, two layer parities
   s += (size_t)(2 * stages + 4 + 5 + 4 + QC_MMA_WARPS + 2 * QC_RSTAGES) * 8 + 16 + 4 * QC_EPI_WARPS;
+  s += (size_t)8 * (b_bytes / (32u * (uint32_t)oc));  // MMA operand offsets: 2 words per MMA of a tile
   if (resid_ring) s += 128 + (size_t)QC_RSTAGES * QC_TILE_M * oc;
   return s;
 }
