@@ -33,13 +33,32 @@ __device__ __forceinline__ void xc_cp16(float* dst, const float* src, bool valid
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
+// cp.async with an L2 cache policy (createpolicy), e.g. evict-last for a
+// matrix that every step re-reads while a larger stream passes through L2
+__device__ __forceinline__ void xc_cp16_policy(float* dst, const float* src, bool valid, uint64_t policy) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(d), "l"(src),
+               "r"(valid ? 16 : 0), "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 __device__ __forceinline__ void xc_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void xc_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int BM, int BN, int RM, int RN, int BK, int S>
+// B_KEEP: B's rows are loaded with an L2 evict-last policy (B re-read by later launches).
+template <int BM, int BN, int RM, int RN, int BK, int S, bool B_KEEP = false>
 struct ExactChain {
   static_assert(RN % 2 == 0 && BK % 4 == 0 && RM >= 1, "tile shape");
   static constexpr int TX = BN / RN, TY = BM / RM, NT = TX * TY;
@@ -58,7 +77,10 @@ struct ExactChain {
       } else {
         const int r = row - BM;
         const bool ok = n0 + r < N && k < K;
-        xc_cp16(Bs + r * PITCH + 4 * cq, ok ? B + (size_t)(n0 + r) * ldb + k : B, ok);
+        if constexpr (B_KEEP)
+          xc_cp16_policy(Bs + r * PITCH + 4 * cq, ok ? B + (size_t)(n0 + r) * ldb + k : B, ok, l2_policy_evict_last());
+        else
+          xc_cp16(Bs + r * PITCH + 4 * cq, ok ? B + (size_t)(n0 + r) * ldb + k : B, ok);
       }
     }
   }

@@ -30,6 +30,15 @@
 
 namespace emx {
 
+__device__ __forceinline__ void st_evict_first(float* p, float v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
+}
+__device__ __forceinline__ float ld_evict_first(const float* p, uint64_t pol) {
+  float v;
+  asm volatile("ld.global.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol) : "memory");
+  return v;
+}
+
 // ---- 1. x-part partial sums: Gx[m][n] = sum_i X[m][i] * Wp[n][i] (m = t*B + b, n gate column)
 using GxChain = ExactChain<64, 64, 4, 4, 32, 4>;
 constexpr int GX_BM = 64, GX_BN = 64;
@@ -45,6 +54,9 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
   for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = 0;  // +0.0f pairs
   GxChain::run(x, K, wp, K, M, N, K, m0, n0, acc, xc_smem);
   const int tx = threadIdx.x % GxChain::TX, ty = threadIdx.x / GxChain::TX;
+  // the partials (T*B x 4Hp floats, read once by their step) must not push the
+  // recurrent matrix that every step re-reads out of L2
+  const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int m = m0 + ty * 4 + r;
@@ -54,7 +66,7 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int n = n0 + GxChain::col(tx, c, h);
-        if (n < N) gx[(size_t)m * N + n] = h ? xc_hi(acc[r][c]) : xc_lo(acc[r][c]);
+        if (n < N) st_evict_first(gx + (size_t)m * N + n, h ? xc_hi(acc[r][c]) : xc_lo(acc[r][c]), pol);
       }
   }
 }
@@ -62,7 +74,7 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
 // ---- 2. one recurrent step.  A 64-column tile holds LS_TILE_UNITS = 16 units:
 // thread tx's four columns tx + g*16 are gates g = i, o, f, c of unit
 // tile*16 + tx, so the cell update runs in the thread that owns the chains.
-using StChain = ExactChain<32, 64, 4, 4, 32, 4>;
+using StChain = ExactChain<32, 64, 4, 4, 32, 4, true>;  // R kept in L2 across steps
 constexpr int ST_BM = 32, ST_BN = 64;
 static_assert(StChain::TX == LS_TILE_UNITS && ST_BN == 4 * LS_TILE_UNITS, "gate tile layout");
 
@@ -89,13 +101,14 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
   pdl_launch_dependents();
   uint64_t acc[4][2];
   const float* g0 = p.gx + (size_t)p.t * p.B * p.N;
+  const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
   for (int r = 0; r < 4; ++r) {  // continue the chains after their x terms
     const int m = m0 + ty * 4 + r;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
     if (m < p.B)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) g[q] = g0[(size_t)m * p.N + n0 + tx + q * StChain::TX];
+      for (int q = 0; q < 4; ++q) g[q] = ld_evict_first(g0 + (size_t)m * p.N + n0 + tx + q * StChain::TX, pol);
     acc[r][0] = xc_pack(g[0], g[1]);
     acc[r][1] = xc_pack(g[2], g[3]);
   }

@@ -121,6 +121,7 @@ struct emx_plan {
   cudaEvent_t ev_start = nullptr, ev_done = nullptr;
   void* d_io = nullptr;           // dedicated full-batch staging of every I/O tensor (never aliased)
   std::vector<size_t> io_off;     // per I/O tensor (inputs, then outputs): offset into d_io
+  std::vector<int> in_kind, out_kind;  // this run's buffers: MEM_DEVICE / MEM_PINNED / MEM_PAGEABLE
 };
 
 namespace {
@@ -333,13 +334,19 @@ int run_graph(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches
   return EMX_OK;
 }
 
-bool is_device_pointer(const void* ptr) {
+// Where a caller's buffer lives: device (or managed) memory is used in place;
+// page-locked host memory can be copied asynchronously (and pipelined);
+// pageable host memory is staged with ordinary copies.
+enum MemKind { MEM_DEVICE = 0, MEM_PINNED = 1, MEM_PAGEABLE = 2 };
+
+int mem_kind(const void* ptr) {
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
     cudaGetLastError();
-    return false;
+    return MEM_PAGEABLE;
   }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return MEM_DEVICE;
+  return a.type == cudaMemoryTypeHost ? MEM_PINNED : MEM_PAGEABLE;
 }
 
 // bytes of one batch row along axis 0 (tensor must be batched)
@@ -348,37 +355,26 @@ size_t row_bytes(const PlanTensor& t) {
   return (size_t)(t.nbytes / (uint64_t)t.dims[0]);
 }
 
-// page-locked host memory (cudaHostAlloc / cudaHostRegister): copies from it
-// are asynchronous and can overlap kernels and copies in the other direction
-bool is_pinned_host(const void* ptr) {
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return a.type == cudaMemoryTypeHost;
-}
-
 constexpr size_t kPipelineMinHostBytes = 1u << 20;
 
 // Whether a run can split its batch into slices whose host copies overlap the
 // kernels: a batchable plan, every output batched on axis 0, every host
 // buffer page-locked, at least 1 MiB crossing the bus, two or more rows.
-bool can_pipeline(const emx_plan* p, const void* const* inputs, void* const* outputs, int64_t count) {
+bool can_pipeline(const emx_plan* p, int64_t count) {
   if (p->io_chunks < 2 || p->profiling || count < 2 || p->hdr.batch <= 0 || !(p->hdr.flags & EMX_PLAN_BATCHABLE))
     return false;
   size_t host_bytes = 0;
   for (size_t i = 0; i < p->inputs.size(); ++i) {
     const PlanTensor& t = p->tensors[p->inputs[i]];
-    if (is_device_pointer(inputs[i])) continue;
-    if (!is_pinned_host(inputs[i])) return false;
+    if (p->in_kind[i] == MEM_DEVICE) continue;
+    if (p->in_kind[i] != MEM_PINNED) return false;
     host_bytes += t.batch_axis == 0 ? (size_t)count * row_bytes(t) : (size_t)t.nbytes;
   }
   for (size_t i = 0; i < p->outputs.size(); ++i) {
     const PlanTensor& t = p->tensors[p->outputs[i]];
     if (t.batch_axis != 0 || row_bytes(t) == 0) return false;
-    if (is_device_pointer(outputs[i])) continue;
-    if (!is_pinned_host(outputs[i])) return false;
+    if (p->out_kind[i] == MEM_DEVICE) continue;
+    if (p->out_kind[i] != MEM_PINNED) return false;
     host_bytes += (size_t)count * row_bytes(t);
   }
   return host_bytes >= kPipelineMinHostBytes;
@@ -430,7 +426,7 @@ int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, 
     const uint32_t id = p->inputs[i];
     const PlanTensor& t = p->tensors[id];
     if (t.batch_axis == 0) continue;
-    if (is_device_pointer(inputs[i])) {
+    if (p->in_kind[i] == MEM_DEVICE) {
       p->ptrs[id] = const_cast<void*>(inputs[i]);
     } else {
       CUDA_TRY(cudaMemcpyAsync(io + p->io_off[i], inputs[i], t.nbytes, cudaMemcpyHostToDevice, p->copy_in),
@@ -447,7 +443,7 @@ int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, 
       const PlanTensor& t = p->tensors[id];
       if (t.batch_axis != 0) continue;
       const size_t rb = row_bytes(t), off = (size_t)r0 * rb;
-      if (is_device_pointer(inputs[i])) {
+      if (p->in_kind[i] == MEM_DEVICE) {
         p->ptrs[id] = const_cast<uint8_t*>(static_cast<const uint8_t*>(inputs[i]) + off);
       } else {
         uint8_t* dst = io + p->io_off[i] + off;
@@ -461,7 +457,7 @@ int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, 
     for (size_t i = 0; i < p->outputs.size(); ++i) {
       const uint32_t id = p->outputs[i];
       const size_t off = (size_t)r0 * row_bytes(p->tensors[id]);
-      p->ptrs[id] = is_device_pointer(outputs[i]) ? static_cast<uint8_t*>(outputs[i]) + off
+      p->ptrs[id] = p->out_kind[i] == MEM_DEVICE ? static_cast<uint8_t*>(outputs[i]) + off
                                                    : io + p->io_off[nin + i] + off;
     }
     rc = p->use_graphs ? run_graph(p, rn, S, &launches) : launch_ops(p, rn, S, &launches);
@@ -469,7 +465,7 @@ int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, 
     CUDA_TRY(cudaEventRecord(p->ev_comp[c], S), "event record");
     CUDA_TRY(cudaStreamWaitEvent(p->copy_out, p->ev_comp[c], 0), "stream wait");
     for (size_t i = 0; i < p->outputs.size(); ++i) {
-      if (is_device_pointer(outputs[i])) continue;
+      if (p->out_kind[i] == MEM_DEVICE) continue;
       const uint32_t id = p->outputs[i];
       const size_t rb = row_bytes(p->tensors[id]), off = (size_t)r0 * rb;
       CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(outputs[i]) + off, io + p->io_off[nin + i] + off,
@@ -562,7 +558,11 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
     if (!inputs[i]) return set_error(EMX_ERR_INVALID_ARGUMENT, "input %zu is NULL", i);
   for (size_t i = 0; i < p->outputs.size(); ++i)
     if (!outputs[i]) return set_error(EMX_ERR_INVALID_ARGUMENT, "output %zu is NULL", i);
-  if (full > 0 && can_pipeline(p, inputs, outputs, batch_count))
+  p->in_kind.resize(p->inputs.size());
+  p->out_kind.resize(p->outputs.size());
+  for (size_t i = 0; i < p->inputs.size(); ++i) p->in_kind[i] = mem_kind(inputs[i]);
+  for (size_t i = 0; i < p->outputs.size(); ++i) p->out_kind[i] = mem_kind(outputs[i]);
+  if (full > 0 && can_pipeline(p, batch_count))
     return run_pipelined(p, inputs, outputs, batch_begin, batch_count, stream);
   for (size_t i = 0; i < p->inputs.size(); ++i) {
     const PlanTensor& t = p->tensors[p->inputs[i]];
@@ -574,7 +574,7 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
       bytes = (size_t)batch_count * row_bytes(t);
     }
     void* staging = static_cast<uint8_t*>(p->d_arena) + t.offset;
-    if (is_device_pointer(src)) {
+    if (p->in_kind[i] == MEM_DEVICE) {
       p->ptrs[p->inputs[i]] = const_cast<uint8_t*>(static_cast<const uint8_t*>(src) + off);
     } else {
       CUDA_TRY(cudaMemcpyAsync(staging, static_cast<const uint8_t*>(src) + off, bytes, cudaMemcpyHostToDevice, stream),
@@ -592,7 +592,7 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
       bytes = (size_t)batch_count * row_bytes(t);
     }
     void* staging = static_cast<uint8_t*>(p->d_arena) + t.offset;
-    if (is_device_pointer(dst)) {
+    if (p->out_kind[i] == MEM_DEVICE) {
       p->ptrs[p->outputs[i]] = static_cast<uint8_t*>(dst) + off;
     } else {
       p->ptrs[p->outputs[i]] = staging;
