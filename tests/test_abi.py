@@ -79,4 +79,6 @@ def test_null_arguments():
     assert lib.emx_b200_plan_load_mem(None, 0, None, 0, 0, None) == 1
     assert lib.emx_b200_run(None, None, None, 0, -1, None) == 1
     assert lib.emx_b200_sync(None) == 1
+    assert lib.emx_b200_set_host_io_chunks(None, 4) == 1
+    assert lib.emx_b200_set_graphs(None, 1) == 1
     lib.emx_b200_plan_free(None)

@@ -86,3 +86,41 @@ def test_weight_image_layout():
                 for j in range(cin // 16):
                     pos = j ^ phase
                     assert np.array_equal(img[tap, oc, 16 * pos:16 * pos + 16], w[oc, 16 * j:16 * j + 16, kh, kw])
+
+
+def _chain_marks(plan):
+    return [(K.NAMES[o.kernel], o.ip.get(K.QC_CHAIN, 0)) for o in plan.ops]
+
+
+def test_conv_stack_is_one_chain():
+    """Consecutive same-geometry convolutions, each reading the previous
+    one's output, form one chain: the first op carries the length and a
+    zero-initialised state tensor (epoch, finished CTAs, one progress word per
+    128-row tile), the others are marked as members."""
+    plan = B200PlanEmitter().emit_plan(lowering.lower(W.qconv_stack_int8().graph))
+    assert _chain_marks(plan) == [("pad_nhwc", 0), ("qconv_tc", 4), ("qconv_tc", -1), ("qconv_tc", -1),
+                                  ("qconv_tc", -1)]
+    head = plan.ops[1]
+    state = plan.tensors[head.tensors[6]]
+    n, hp, wp, oh, ow = (head.ip[k] for k in (K.QC_N, K.QC_HP, K.QC_WP, K.QC_OH, K.QC_OW))
+    q_end = (n - 1) * hp * wp + (oh - 1) * wp + ow
+    assert state.nbytes == 8 * (2 + -(-q_end // 128))
+    # every member reads the previous member's output
+    for a, b in zip(plan.ops[1:], plan.ops[2:]):
+        assert b.tensors[0] == a.tensors[4]
+
+
+@pytest.mark.parametrize("n_convs", [1, 2, 3, 9])
+def test_chain_lengths_and_opt_out(n_convs):
+    wl = W.qconv_stack_int8(batch=2, channels=32, height=8, width=8, n_convs=n_convs)
+    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    marks = [m for _, m in _chain_marks(plan)[1:]]
+    if n_convs == 1:
+        assert marks == [0]
+    else:  # chains hold at most 8 convolutions; a lone remainder runs on its own (0)
+        heads = [m for m in marks if m > 0]
+        assert sum(heads) + marks.count(0) == n_convs and all(1 < h <= 8 for h in heads)
+        assert marks.count(-1) == sum(heads) - len(heads)
+        assert heads[0] == min(n_convs, 8)
+    plain = B200PlanEmitter(chain_convs=False).emit_plan(lowering.lower(wl.graph))
+    assert all(m == 0 for _, m in _chain_marks(plain))
