@@ -14,7 +14,12 @@ over ranks.
   timed step, max over ranks.
 * ``e2e``    -- the same step through the C-ABI with pinned HOST buffers:
   host->device input copy, the plan, device->host output copy, all inside the
-  timed region.
+  timed region.  Default ``--host-io overlap``: K steps issued back to back
+  with the library's overlapped-runs mode (step k+1's upload and step k-1's
+  download overlap step k's kernels), timed from an event before the first
+  step to an event after the last step's download (emx_b200_join), / K;
+  ``--host-io slices``: each step on its own, its batch cut into slices whose
+  copies overlap its kernels, timed step by step.
 * ``roofline`` -- the dominant kernel's algorithmic work per launch / its mean
   CUDA-event duration (per-op events inside the library), against the
   measured peaks.
@@ -322,6 +327,19 @@ def ours_arm(args) -> None:
         if world > 1:
             dist.barrier()
 
+    def timed_overlap(ins, outs, steps):
+        # K steps back to back; the stream waits for the last download before e1
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            flush.fill_(1)
+            sess.run_ptrs(ins, outs, stream=sptr)
+        sess.join(sptr)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sess.sync()
+        return e0.elapsed_time(e1) / steps
+
     def timed(ins, outs, steps):
         ev = []
         for _ in range(steps):
@@ -361,7 +379,19 @@ def ours_arm(args) -> None:
         ms = timed(in_d, out_d, args.steps)
         launches = sess.launch_count() - launches_before
     barrier()
-    ms_e2e = timed(in_h, out_h, args.steps)
+    if args.host_io == "overlap":
+        sess.set_host_io_overlap(True)
+        for _ in range(max(4, args.warmup)):  # both staging sets' graphs
+            flush.fill_(3)
+            sess.run_ptrs(in_h, out_h, stream=sptr)
+        sess.join(sptr)
+        torch.cuda.synchronize()
+        sess.sync()
+        barrier()
+        ms_e2e = timed_overlap(in_h, out_h, args.steps)
+        sess.set_host_io_overlap(False)
+    else:
+        ms_e2e = timed(in_h, out_h, args.steps)
     barrier()
     ms = max_over_ranks(ms)
     ms_e2e = max_over_ranks(ms_e2e)
@@ -411,7 +441,9 @@ def ours_arm(args) -> None:
         "metric": "inferences/s", "value": world * 1000.0 / ms, "unit": "inferences/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, **_config(wl), "host_io_chunks": args.io_chunks or 4},
+        "config": {"workload": args.workload, **_config(wl),
+                   "host_io": ("overlapped runs (two staging sets)" if args.host_io == "overlap"
+                               else f"{args.io_chunks or 4} batch slices per run")},
         "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "inferences/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary(),
@@ -457,6 +489,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qconv_stack_int8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--host-io", choices=["overlap", "slices"], default="overlap",
+                    help="e2e host copies: overlap consecutive steps (default) or slice each step's batch")
     ap.add_argument("--io-chunks", type=int, default=None,
                     help="batch slices for the e2e run's pipelined host copies (library default 4; 1 = off)")
     args = ap.parse_args()

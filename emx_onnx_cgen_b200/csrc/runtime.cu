@@ -122,6 +122,14 @@ struct emx_plan {
   void* d_io = nullptr;           // dedicated full-batch staging of every I/O tensor (never aliased)
   std::vector<size_t> io_off;     // per I/O tensor (inputs, then outputs): offset into d_io
   std::vector<int> in_kind, out_kind;  // this run's buffers: MEM_DEVICE / MEM_PINNED / MEM_PAGEABLE
+  // overlapped runs (opt-in): runs with page-locked host buffers alternate two
+  // staging sets, so run k+1's upload and run k-1's download overlap run k's
+  // kernels; the caller's stream does not wait for the downloads
+  bool io_overlap = false;
+  void* d_io2[2] = {nullptr, nullptr};
+  cudaEvent_t ov_h2d[2] = {nullptr, nullptr}, ov_comp[2] = {nullptr, nullptr}, ov_d2h[2] = {nullptr, nullptr};
+  uint64_t ov_seq = 0;
+  cudaEvent_t ov_last = nullptr;  // download-complete event of the latest overlapped run
 };
 
 namespace {
@@ -243,6 +251,12 @@ void destroy(emx_plan* p) {
   if (p->copy_in) cudaStreamDestroy(p->copy_in);
   if (p->copy_out) cudaStreamDestroy(p->copy_out);
   if (p->d_io) cudaFree(p->d_io);
+  for (int k = 0; k < 2; ++k) {
+    if (p->d_io2[k]) cudaFree(p->d_io2[k]);
+    if (p->ov_h2d[k]) cudaEventDestroy(p->ov_h2d[k]);
+    if (p->ov_comp[k]) cudaEventDestroy(p->ov_comp[k]);
+    if (p->ov_d2h[k]) cudaEventDestroy(p->ov_d2h[k]);
+  }
   for (auto e : p->ev_begin) cudaEventDestroy(e);
   for (auto e : p->ev_end) cudaEventDestroy(e);
   if (p->own_stream) cudaStreamDestroy(p->own_stream);
@@ -480,6 +494,113 @@ int run_pipelined(emx_plan* p, const void* const* inputs, void* const* outputs, 
   return EMX_OK;
 }
 
+// Overlapped runs need every host buffer page-locked (device buffers are used in place).
+bool can_overlap(const emx_plan* p) {
+  if (!p->io_overlap || p->profiling) return false;
+  bool any_host = false;
+  for (int k : p->in_kind) {
+    if (k == MEM_PAGEABLE) return false;
+    any_host = any_host || k == MEM_PINNED;
+  }
+  for (int k : p->out_kind) {
+    if (k == MEM_PAGEABLE) return false;
+    any_host = any_host || k == MEM_PINNED;
+  }
+  return any_host;
+}
+
+int ensure_overlap(emx_plan* p) {
+  if (!p->copy_in) CUDA_TRY(cudaStreamCreateWithFlags(&p->copy_in, cudaStreamNonBlocking), "copy-in stream");
+  if (!p->copy_out) CUDA_TRY(cudaStreamCreateWithFlags(&p->copy_out, cudaStreamNonBlocking), "copy-out stream");
+  if (p->io_off.empty()) {
+    size_t total = 0;
+    for (uint32_t id : p->inputs) { p->io_off.push_back(total); total += (p->tensors[id].nbytes + 255) & ~(size_t)255; }
+    for (uint32_t id : p->outputs) { p->io_off.push_back(total); total += (p->tensors[id].nbytes + 255) & ~(size_t)255; }
+  }
+  size_t total = 0;
+  for (size_t i = 0; i < p->inputs.size(); ++i) total = p->io_off[i] + ((p->tensors[p->inputs[i]].nbytes + 255) & ~(size_t)255);
+  for (size_t i = 0; i < p->outputs.size(); ++i)
+    total = std::max(total, p->io_off[p->inputs.size() + i] + ((p->tensors[p->outputs[i]].nbytes + 255) & ~(size_t)255));
+  for (int k = 0; k < 2; ++k) {
+    if (!p->d_io2[k] && cudaMalloc(&p->d_io2[k], total ? total : 256) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(EMX_ERR_OUT_OF_MEMORY, "overlapped host I/O staging of 2 x %zu bytes failed", total);
+    }
+    if (!p->ov_h2d[k]) CUDA_TRY(cudaEventCreateWithFlags(&p->ov_h2d[k], cudaEventDisableTiming), "event");
+    if (!p->ov_comp[k]) CUDA_TRY(cudaEventCreateWithFlags(&p->ov_comp[k], cudaEventDisableTiming), "event");
+    if (!p->ov_d2h[k]) CUDA_TRY(cudaEventCreateWithFlags(&p->ov_d2h[k], cudaEventDisableTiming), "event");
+  }
+  return EMX_OK;
+}
+
+// One overlapped run on staging set k = run number % 2: the upload (copy_in)
+// waits only until the run two back has finished reading set k's inputs, the
+// kernels (caller's stream) wait for their upload, for the previous run's
+// kernels (the arena is shared) and for set k's previous download, and the
+// download (copy_out) waits for the kernels.  The caller's stream is not made
+// to wait for the download: emx_b200_join / emx_b200_sync do that.
+int run_overlapped(emx_plan* p, const void* const* inputs, void* const* outputs, int64_t b0, int64_t count,
+                   cudaStream_t S) {
+  int rc = ensure_overlap(p);
+  if (rc) return rc;
+  const int k = (int)(p->ov_seq & 1u);
+  const bool have_prev = p->ov_seq > 0, have_two_back = p->ov_seq > 1;
+  ++p->ov_seq;
+  uint8_t* io = static_cast<uint8_t*>(p->d_io2[k]);
+  const size_t nin = p->inputs.size();
+  const int64_t full = p->hdr.batch;
+  if (have_two_back) CUDA_TRY(cudaStreamWaitEvent(p->copy_in, p->ov_comp[k], 0), "stream wait");
+  for (size_t i = 0; i < nin; ++i) {
+    const uint32_t id = p->inputs[i];
+    const PlanTensor& t = p->tensors[id];
+    size_t off = 0, bytes = t.nbytes;
+    if (full > 0 && t.batch_axis == 0) {
+      off = (size_t)b0 * row_bytes(t);
+      bytes = (size_t)count * row_bytes(t);
+    }
+    if (p->in_kind[i] == MEM_DEVICE) {
+      p->ptrs[id] = const_cast<uint8_t*>(static_cast<const uint8_t*>(inputs[i]) + off);
+    } else {
+      CUDA_TRY(cudaMemcpyAsync(io + p->io_off[i], static_cast<const uint8_t*>(inputs[i]) + off, bytes,
+                               cudaMemcpyHostToDevice, p->copy_in), "input upload");
+      p->ptrs[id] = io + p->io_off[i];
+    }
+  }
+  CUDA_TRY(cudaEventRecord(p->ov_h2d[k], p->copy_in), "event record");
+  CUDA_TRY(cudaStreamWaitEvent(S, p->ov_h2d[k], 0), "stream wait");
+  if (have_prev) CUDA_TRY(cudaStreamWaitEvent(S, p->ov_comp[k ^ 1], 0), "stream wait");
+  if (have_two_back) CUDA_TRY(cudaStreamWaitEvent(S, p->ov_d2h[k], 0), "stream wait");
+  for (size_t i = 0; i < p->outputs.size(); ++i) {
+    const uint32_t id = p->outputs[i];
+    const PlanTensor& t = p->tensors[id];
+    const size_t off = (full > 0 && t.batch_axis == 0) ? (size_t)b0 * row_bytes(t) : 0;
+    p->ptrs[id] = p->out_kind[i] == MEM_DEVICE ? static_cast<uint8_t*>(outputs[i]) + off : io + p->io_off[nin + i];
+  }
+  int launches = 0;
+  const int64_t run_batch = full > 0 ? count : 0;
+  rc = p->use_graphs ? run_graph(p, run_batch, S, &launches) : launch_ops(p, run_batch, S, &launches);
+  if (rc) return rc;
+  CUDA_TRY(cudaEventRecord(p->ov_comp[k], S), "event record");
+  CUDA_TRY(cudaStreamWaitEvent(p->copy_out, p->ov_comp[k], 0), "stream wait");
+  for (size_t i = 0; i < p->outputs.size(); ++i) {
+    if (p->out_kind[i] == MEM_DEVICE) continue;
+    const PlanTensor& t = p->tensors[p->outputs[i]];
+    size_t off = 0, bytes = t.nbytes;
+    if (full > 0 && t.batch_axis == 0) {
+      off = (size_t)b0 * row_bytes(t);
+      bytes = (size_t)count * row_bytes(t);
+    }
+    CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(outputs[i]) + off, io + p->io_off[nin + i], bytes,
+                             cudaMemcpyDeviceToHost, p->copy_out), "output download");
+  }
+  CUDA_TRY(cudaEventRecord(p->ov_d2h[k], p->copy_out), "event record");
+  p->ov_last = p->ov_d2h[k];
+  p->launches_total += launches;
+  p->launches_last = launches;
+  p->events_pending = false;
+  return EMX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -562,6 +683,7 @@ int emx_b200_run(emx_plan_t* p, const void* const* inputs, void* const* outputs,
   p->out_kind.resize(p->outputs.size());
   for (size_t i = 0; i < p->inputs.size(); ++i) p->in_kind[i] = mem_kind(inputs[i]);
   for (size_t i = 0; i < p->outputs.size(); ++i) p->out_kind[i] = mem_kind(outputs[i]);
+  if (can_overlap(p)) return run_overlapped(p, inputs, outputs, batch_begin, batch_count, stream);
   if (full > 0 && can_pipeline(p, batch_count))
     return run_pipelined(p, inputs, outputs, batch_begin, batch_count, stream);
   for (size_t i = 0; i < p->inputs.size(); ++i) {
@@ -620,6 +742,8 @@ int emx_b200_sync(emx_plan_t* p) {
   if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
   CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
   CUDA_TRY(cudaStreamSynchronize(p->last_stream ? p->last_stream : p->own_stream), "stream synchronize");
+  if (p->copy_in) CUDA_TRY(cudaStreamSynchronize(p->copy_in), "stream synchronize");
+  if (p->copy_out) CUDA_TRY(cudaStreamSynchronize(p->copy_out), "stream synchronize");
   if (p->events_pending) {
     for (size_t i = 0; i < p->ops.size(); ++i) {
       float ms = 0.f;
@@ -657,6 +781,20 @@ int64_t emx_b200_launch_count(const emx_plan_t* p) { return p ? p->launches_tota
 int emx_b200_set_graphs(emx_plan_t* p, int enable) {
   if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
   p->use_graphs = enable != 0;
+  return EMX_OK;
+}
+
+int emx_b200_set_host_io_overlap(emx_plan_t* p, int enable) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  p->io_overlap = enable != 0;
+  return EMX_OK;
+}
+
+int emx_b200_join(emx_plan_t* p, void* stream_) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  cudaStream_t stream = stream_ ? static_cast<cudaStream_t>(stream_) : p->own_stream;
+  if (p->ov_last) CUDA_TRY(cudaStreamWaitEvent(stream, p->ov_last, 0), "stream wait");
   return EMX_OK;
 }
 

@@ -25,7 +25,7 @@ STATUS_NAMES = {0: "EMX_OK", 1: "EMX_ERR_INVALID_ARGUMENT", 2: "EMX_ERR_PLAN_FOR
 EXPORTED = ("emx_b200_version", "emx_b200_last_error", "emx_b200_plan_load", "emx_b200_plan_load_mem",
             "emx_b200_run", "emx_b200_sync", "emx_b200_plan_free", "emx_b200_plan_info",
             "emx_b200_launch_count", "emx_b200_set_profiling", "emx_b200_op_times", "emx_b200_set_graphs",
-            "emx_b200_set_host_io_chunks")
+            "emx_b200_set_host_io_chunks", "emx_b200_set_host_io_overlap", "emx_b200_join")
 
 
 class EmxError(RuntimeError):
@@ -70,6 +70,10 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.emx_b200_set_graphs.restype = i32
         lib.emx_b200_set_host_io_chunks.argtypes = [vp, i32]
         lib.emx_b200_set_host_io_chunks.restype = i32
+        lib.emx_b200_set_host_io_overlap.argtypes = [vp, i32]
+        lib.emx_b200_set_host_io_overlap.restype = i32
+        lib.emx_b200_join.argtypes = [vp, vp]
+        lib.emx_b200_join.restype = i32
         lib.emx_b200_op_times.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
                                           ctypes.POINTER(i64)]
         for name in ("emx_b200_plan_load", "emx_b200_plan_load_mem", "emx_b200_run", "emx_b200_sync",
@@ -141,6 +145,14 @@ class Session:
 
     def set_graphs(self, enable: bool) -> None:
         _check(self.lib.emx_b200_set_graphs(self.handle, 1 if enable else 0))
+
+    def set_host_io_overlap(self, enable: bool) -> None:
+        """Overlap consecutive runs' uploads, kernels and downloads (page-locked host buffers)."""
+        _check(self.lib.emx_b200_set_host_io_overlap(self.handle, 1 if enable else 0))
+
+    def join(self, stream: int = 0) -> None:
+        """Make `stream` wait for every download of the overlapped runs issued so far."""
+        _check(self.lib.emx_b200_join(self.handle, ctypes.c_void_p(stream) if stream else None))
 
     def set_host_io_chunks(self, chunks: int) -> None:
         """Batch slices for pipelined page-locked host I/O (1 = off)."""

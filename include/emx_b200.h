@@ -134,6 +134,23 @@ int emx_b200_set_graphs(emx_plan_t *plan, int enable);
  * No counterpart in the reference (its generated C runs in host memory). */
 int emx_b200_set_host_io_chunks(emx_plan_t *plan, int chunks);
 
+/* Overlapped runs (default off).  When on, a run whose host buffers are all
+ * page-locked stages through one of two alternating device buffer sets: its
+ * upload (on a copy stream) starts as soon as the run two back has read that
+ * set, its kernels (on `stream`) follow their upload and the previous run's
+ * kernels, its download (on a second copy stream) follows its kernels -- so
+ * consecutive runs overlap each other's uploads, kernels and downloads.
+ * `stream` is NOT made to wait for the download: emx_b200_join(plan, s)
+ * makes stream s wait for every download issued so far, and emx_b200_sync
+ * waits for everything.  Host buffers must stay valid and unmodified until
+ * then.  No counterpart in the reference (its generated C runs in host
+ * memory). */
+int emx_b200_set_host_io_overlap(emx_plan_t *plan, int enable);
+
+/* Make `stream` (NULL: the plan's own stream) wait until every download of
+ * the plan's overlapped runs issued so far is complete. */
+int emx_b200_join(emx_plan_t *plan, void *stream);
+
 /* Allocation-free standalone QLinearConv, 3x3 kernel, stride 1, pads 1,
  * group 1, no dilation: uint8 NCHW x [n][c][h][w] with x_zero_point 0 or 128,
  * int8 OIHW weights [oc][c][3][3] with per-output-channel fp32 scales

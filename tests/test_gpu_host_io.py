@@ -115,3 +115,42 @@ def test_chunk_count_is_validated():
     for bad in (0, 65, -1):
         with pytest.raises(EmxError):
             s.set_host_io_chunks(bad)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_overlapped_runs(name):
+    """Overlapped mode: five runs issued back to back on one stream, each with
+    its own page-locked buffers and no synchronisation in between (uploads,
+    kernels and downloads of neighbouring runs overlap through two staging
+    sets); after join + sync every output equals its device-buffer run."""
+    require_gpu()
+    import torch
+    wl = CASES[name]()
+    plan = plan_for(wl)
+    s = Session(plan)
+    inputs = [wl.make_inputs(20 + k) for k in range(5)]
+    refs = [_device_reference(torch, s, plan, x) for x in inputs]
+    s.set_host_io_overlap(True)
+    st = torch.cuda.Stream()
+    bufs = [_buffers(torch, plan, x) for x in inputs]
+    for hin, hout in bufs:
+        s.run_ptrs([t.data_ptr() for t in hin], [t.data_ptr() for t in hout], stream=st.cuda_stream)
+    s.join(st.cuda_stream)
+    st.synchronize()
+    for k, ((_, hout), ref) in enumerate(zip(bufs, refs)):
+        for got, exp, n in zip(hout, ref, plan.output_names):
+            assert_bitexact(got.numpy(), exp, f"{name} overlapped run {k} {n}")
+    s.sync()
+    # a row range through the overlapped path, then back to the default mode
+    b0, cnt = 1, plan.batch - 2
+    hin, hout = _buffers(torch, plan, inputs[0])
+    s.run_ptrs([t.data_ptr() for t in hin], [t.data_ptr() for t in hout], batch_begin=b0, batch_count=cnt)
+    s.sync()
+    for got, exp, n in zip(hout, refs[0], plan.output_names):
+        assert_bitexact(got.numpy()[b0:b0 + cnt], exp[b0:b0 + cnt], f"{name} overlapped rows {n}")
+    s.set_host_io_overlap(False)
+    hin, hout = _buffers(torch, plan, inputs[1])
+    s.run_ptrs([t.data_ptr() for t in hin], [t.data_ptr() for t in hout])
+    s.sync()
+    for got, exp, n in zip(hout, refs[1], plan.output_names):
+        assert_bitexact(got.numpy(), exp, f"{name} after overlap {n}")
