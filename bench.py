@@ -14,7 +14,8 @@ over ranks.
   timed step, max over ranks.
 * ``e2e``    -- the same step through the C-ABI with pinned HOST buffers:
   host->device input copy, the plan, device->host output copy, all inside the
-  timed region.  Default ``--host-io overlap``: K steps issued back to back
+  timed region.  ``--host-io overlap`` (what ``auto``, the default, picks when
+  a step moves at least 1 MiB): K steps issued back to back
   with the library's overlapped-runs mode (step k+1's upload and step k-1's
   download overlap step k's kernels), timed from an event before the first
   step to an event after the last step's download (emx_b200_join), / K;
@@ -379,7 +380,10 @@ def ours_arm(args) -> None:
         ms = timed(in_d, out_d, args.steps)
         launches = sess.launch_count() - launches_before
     barrier()
-    if args.host_io == "overlap":
+    host_io = args.host_io
+    if host_io == "auto":  # overlapping runs pays when copies are worth hiding (the library's 1 MiB slicing threshold)
+        host_io = "overlap" if h2d + d2h >= (1 << 20) else "slices"
+    if host_io == "overlap":
         sess.set_host_io_overlap(True)
         for _ in range(max(4, args.warmup)):  # both staging sets' graphs
             flush.fill_(3)
@@ -442,8 +446,8 @@ def ours_arm(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"], "data": "synthetic",
         "config": {"workload": args.workload, **_config(wl),
-                   "host_io": ("overlapped runs (two staging sets)" if args.host_io == "overlap"
-                               else f"{args.io_chunks or 4} batch slices per run")},
+                   "host_io": ("overlapped runs (two staging sets)" if host_io == "overlap"
+                               else f"one run at a time ({args.io_chunks or 4} batch slices when >= 1 MiB moves)")},
         "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "inferences/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary(),
@@ -489,8 +493,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qconv_stack_int8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--host-io", choices=["overlap", "slices"], default="overlap",
-                    help="e2e host copies: overlap consecutive steps (default) or slice each step's batch")
+    ap.add_argument("--host-io", choices=["auto", "overlap", "slices"], default="auto",
+                    help="e2e host copies: overlap consecutive steps, or one step at a time (its batch sliced); "
+                         "auto: overlap when a step moves >= 1 MiB")
     ap.add_argument("--io-chunks", type=int, default=None,
                     help="batch slices for the e2e run's pipelined host copies (library default 4; 1 = off)")
     args = ap.parse_args()
