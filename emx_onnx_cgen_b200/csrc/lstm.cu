@@ -74,8 +74,9 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
 // ---- 2. one recurrent step.  A 64-column tile holds LS_TILE_UNITS = 16 units:
 // thread tx's four columns tx + g*16 are gates g = i, o, f, c of unit
 // tile*16 + tx, so the cell update runs in the thread that owns the chains.
-using StChain = ExactChain<32, 64, 4, 4, 32, 4, true>;  // R kept in L2 across steps
-constexpr int ST_BM = 32, ST_BN = 64;
+constexpr int ST_RM = 4;  // batch rows per thread (8 warps' rows = the CTA's ST_BM)
+using StChain = ExactChain<8 * ST_RM, 64, ST_RM, 4, 32, 4, true>;  // R kept in L2 across steps
+constexpr int ST_BM = 8 * ST_RM, ST_BN = 64;
 static_assert(StChain::TX == LS_TILE_UNITS && ST_BN == 4 * LS_TILE_UNITS, "gate tile layout");
 
 struct LstmStepParams {
@@ -99,12 +100,12 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
   const int tx = threadIdx.x % StChain::TX, ty = threadIdx.x / StChain::TX;
   pdl_wait();  // h_prev and c come from the previous step
   pdl_launch_dependents();
-  uint64_t acc[4][2];
+  uint64_t acc[ST_RM][2];
   const float* g0 = p.gx + (size_t)p.t * p.B * p.N;
   const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {  // continue the chains after their x terms
-    const int m = m0 + ty * 4 + r;
+  for (int r = 0; r < ST_RM; ++r) {  // continue the chains after their x terms
+    const int m = m0 + ty * ST_RM + r;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
     if (m < p.B)
 #pragma unroll
@@ -119,8 +120,8 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
 #pragma unroll
   for (int q = 0; q < 4; ++q) bs[q] = p.bsum[n0 + tx + q * StChain::TX];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int b = m0 + ty * 4 + r;
+  for (int r = 0; r < ST_RM; ++r) {
+    const int b = m0 + ty * ST_RM + r;
     if (b >= p.B) continue;
     const float gi = __fadd_rn(xc_lo(acc[r][0]), bs[0]);
     const float go = __fadd_rn(xc_hi(acc[r][0]), bs[1]);
