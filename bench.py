@@ -25,7 +25,8 @@ over ranks.
   CUDA-event duration (per-op events inside the library), against the
   measured peaks.
 * ``cpu_baseline`` -- the reference's own generated C (``oracle/_ref``, gcc
-  -O2) on the host cores, rank 0 at N=1 only, on a bounded sample.
+  -O2) on the host cores (one row-slice per core), rank 0 at N=1 only, on a
+  bounded sample; ``single_thread`` inside it: the same C on one core.
 
 ``--impl reference`` times that reference C as the whole arm (rank 0 only).
 """
@@ -209,8 +210,10 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU reference
-def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, warmup: int = 0):
-    """Run the reference's generated C (oracle/_ref) on all host cores.
+def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, warmup: int = 0,
+                         threads: int | None = None):
+    """Run the reference's generated C (oracle/_ref) on all host cores (or on
+    ``threads`` of them; 1 = the generated C single-threaded, as emitted).
 
     Returns (list of per-step seconds, rows per step, threads).  One step runs
     ``threads`` independent row-slices in parallel, one per thread; ctypes
@@ -222,7 +225,7 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
     model = RefCModel(dom["ref_tag"])
     wl = W.BUILDERS[idx["builder"]](**idx["kwargs"])
     cores = len(os.sched_getaffinity(0))
-    threads = max(1, min(cores, dom["full_rows"] // dom["ref_rows"]))
+    threads = max(1, min(threads or cores, dom["full_rows"] // dom["ref_rows"]))
     per_thread = [wl.make_inputs(s) for s in range(threads)]
     outs = [None] * threads
 
@@ -252,6 +255,14 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
 
 
 # ----------------------------------------------------------------------------- arms
+def single_thread_baseline(dom: dict, seconds: float = 6.0) -> dict:
+    """The generated C single-threaded on a bounded sample (at least one row-slice)."""
+    times, rows, _ = cpu_reference_sample(dom, seconds, threads=1)
+    sec = sum(times) / len(times)
+    return {"value": rows / dom["full_rows"] / sec, "unit": "inferences/s", "cores": 1,
+            "sample": f"{len(times)} steps x {rows} of {dom['full_rows']} batch rows, one thread"}
+
+
 def reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -270,7 +281,8 @@ def reference_arm(args) -> None:
         "data": "synthetic", "config": {"workload": args.workload, **_config(wl)},
         "cpu_baseline": {"value": value, "unit": "inferences/s", "cores": threads, "kind": "reference",
                          "sample": f"{rows} of {dom['full_rows']} batch rows per step, reference generated C "
-                                   f"(gcc -std=c99 -O2), one row-slice per thread"},
+                                   f"(gcc -std=c99 -O2), one row-slice per thread",
+                         "single_thread": single_thread_baseline(dom)},
         "e2e": {"value": value, "unit": "inferences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -461,7 +473,8 @@ def ours_arm(args) -> None:
                 "value": rows / dom["full_rows"] / sec, "unit": "inferences/s", "cores": threads,
                 "kind": "reference",
                 "sample": f"{len(times)} steps x {rows} of {dom['full_rows']} batch rows, reference generated C "
-                          f"(gcc -std=c99 -O2), one row-slice per thread"}
+                          f"(gcc -std=c99 -O2), one row-slice per thread",
+                "single_thread": single_thread_baseline(dom)}
         except Exception as exc:  # the GPU number stands without it
             line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
     if rank == 0:
