@@ -11,7 +11,8 @@
 //   Conv (fp32)    templates/conv_op.c.j2: acc = bias; in-bounds taps in
 //                  (ic, kh, kw) order, acc += x * w (separately rounded, no FMA).
 //   Softmax (fp32) templates/softmax_op.c.j2: fmaxf chain, expf, sequential float
-//                  sum, division (one warp per row; the sum stays sequential).
+//                  sum, division (one warp per row; the sum stays sequential;
+//                  contiguous rows are staged in shared memory).
 //   QuantizeLinear / DequantizeLinear  templates/quantize_linear_op.c.j2,
 //                  dequantize_linear_op.c.j2: per tensor or per axis index.
 // Integer work is exact in any order; the float steps use explicitly rounded
@@ -188,12 +189,254 @@ __global__ void softmax_f32_kernel(const float* __restrict__ x, float* __restric
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     for (int64_t a = lane; a < axis; a += 32) y[base + a * inner] = expf(__fsub_rn(x[base + a * inner], mx));
     __syncwarp();
+    // the reference's sequential sum (k ascending, one rounding per add); the
+    // next 16 terms are loaded ahead so the chain waits on adds, not on loads
     float sum = 0.0f;
-    if (lane == 0)
-      for (int64_t a = 0; a < axis; ++a) sum = __fadd_rn(sum, y[base + a * inner]);
+    if (lane == 0) {
+      int64_t a = 0;
+      for (; a + 16 <= axis; a += 16) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = y[base + (a + j) * inner];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, v[j]);
+      }
+      for (; a < axis; ++a) sum = __fadd_rn(sum, y[base + a * inner]);
+    }
     sum = __shfl_sync(0xffffffffu, sum, 0);
     for (int64_t a = lane; a < axis; a += 32) y[base + a * inner] = __fdiv_rn(y[base + a * inner], sum);
     __syncwarp();
+  }
+}
+
+// Contiguous rows (inner == 1) that fit in shared memory: a block stages one
+// row per warp, so x is read once and y written once (the strided kernel above
+// re-reads y twice).  The arithmetic is the same statement for statement: the
+// fmaxf reduction, expf(x - max) stored, the sequential sum, the division.
+// The sums of the block's rows run side by side in the lanes of warp 0 (lane r
+// adds row r's terms in order, four per shared-memory load, the next loads
+// issued before the current adds), so a row's add chain costs a quarter of a
+// warp instruction per term rather than a whole one.  Row r starts at
+// r * stride floats with stride = 4 (mod 32), which puts the lanes' loads in
+// different banks.
+constexpr int SMX_ROWS = 4;
+constexpr int64_t SMX_MAX_BYTES = 200 * 1024;
+constexpr int SMX_MIN_ROWS_PER_SM = 12;
+
+__device__ __forceinline__ void cp_async16_cg(float* smem_dst, const float* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+template <bool VEC>
+__global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t axis,
+                                    int64_t stride) {
+  extern __shared__ __align__(16) float smx[];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nr = blockDim.x >> 5;
+  float* s = smx + warp * stride;
+  float* s_sum = smx + nr * stride;
+  const int n = (int)axis;
+  for (int64_t g = blockIdx.x; g * nr < rows; g += gridDim.x) {
+    const int64_t row = g * nr + warp;
+    const bool live = row < rows;
+    float mx = 0.0f;
+    if (live) {
+      const float* xr = x + row * axis;
+      // the whole row in flight at once: asynchronous copies into the row's
+      // shared-memory slot, no registers held while they land
+      if (VEC) {
+        for (int a = lane; a < (n >> 2); a += 32) cp_async16_cg(s + 4 * a, xr + 4 * a);
+      } else {
+        for (int a = lane; a < n; a += 32) cp_async4(s + a, xr + a);
+      }
+      cp_async_commit();
+      cp_async_wait_group<0>();
+      __syncwarp();
+      mx = s[0];  // fmaxf is order-free (NaN ignored) up to the sign of zero, which cannot change x - max
+      if (VEC) {
+        for (int a = lane; a < (n >> 2); a += 32) {
+          const float4 v = reinterpret_cast<const float4*>(s)[a];
+          mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, v.x), v.y), v.z), v.w);
+        }
+      } else {
+        for (int a = lane; a < n; a += 32) mx = fmaxf(mx, s[a]);
+      }
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (VEC) {
+        for (int a = lane; a < (n >> 2); a += 32) {
+          float4 v = reinterpret_cast<float4*>(s)[a];
+          v.x = expf(__fsub_rn(v.x, mx));
+          v.y = expf(__fsub_rn(v.y, mx));
+          v.z = expf(__fsub_rn(v.z, mx));
+          v.w = expf(__fsub_rn(v.w, mx));
+          reinterpret_cast<float4*>(s)[a] = v;
+        }
+      } else {
+        for (int a = lane; a < n; a += 32) s[a] = expf(__fsub_rn(s[a], mx));
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && lane < nr && g * nr + lane < rows) {
+      const float* sr = smx + lane * stride;
+      const float4* s4 = reinterpret_cast<const float4*>(sr);
+      const int n16 = n >> 4;
+      float sum = 0.0f;
+      float4 v[4];
+      if (n16 > 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = s4[j];
+      }
+      for (int q = 0; q < n16; ++q) {
+        float4 w[4];
+        const int nq = q + 1 < n16 ? q + 1 : q;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = s4[4 * nq + j];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v[j].x), v[j].y), v[j].z), v[j].w);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = w[j];
+      }
+      for (int a = 16 * n16; a < n; ++a) sum = __fadd_rn(sum, sr[a]);
+      s_sum[lane] = sum;
+    }
+    __syncthreads();
+    if (live) {
+      const float sum = s_sum[warp];
+      float* yr = y + row * axis;
+      if (VEC) {
+        for (int a = lane; a < (n >> 2); a += 32) {
+          float4 v = reinterpret_cast<const float4*>(s)[a];
+          v.x = __fdiv_rn(v.x, sum);
+          v.y = __fdiv_rn(v.y, sum);
+          v.z = __fdiv_rn(v.z, sum);
+          v.w = __fdiv_rn(v.w, sum);
+          __stcs(reinterpret_cast<float4*>(yr) + a, v);
+        }
+      } else {
+        for (int a = lane; a < n; a += 32) __stcs(yr + a, __fdiv_rn(s[a], sum));
+      }
+    }
+    // the next group's stores into row `warp` follow this warp's own reads;
+    // the next sums are written only after the next group's first barrier
+  }
+}
+
+// Contiguous rows of a multiple of four floats: the exponentials are staged in
+// y itself (L2-resident between the passes) instead of shared memory, so a
+// block holds no row in shared memory and six blocks per SM keep 24 rows in
+// flight.  Per group of SMX_ROWS rows: each warp reads its row's max (pass 1,
+// HBM), writes expf(x - max) into y (pass 2, x again from L2); lanes 0..3 of
+// warp 0 add their rows' terms in order, streamed through a per-lane cp.async
+// ring (SML_ST chunks of SML_CH floats, SML_ST - 1 in flight); each warp then
+// divides its row in place (pass 3).  Same statements as the kernels above.
+constexpr int SML_CH = 64;
+constexpr int SML_ST = 6;
+constexpr int SML_LANE = SML_ST * SML_CH + 4;  // = 4 (mod 32): the lanes' rings sit in different banks
+constexpr int SML_BLOCKS_PER_SM = 6;
+constexpr int SML_LOADS = 4;   // passes 2 and 3 (L2)
+constexpr int SML_LOADS_HBM = 6;  // pass 1
+
+__global__ void __launch_bounds__(32 * SMX_ROWS, SML_BLOCKS_PER_SM) softmax_stream_kernel(const float* __restrict__ x,
+                                                                       float* __restrict__ y, int64_t rows,
+                                                                       int64_t axis) {
+  __shared__ __align__(16) float ring[SMX_ROWS * SML_LANE];
+  __shared__ float s_sum[SMX_ROWS];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = (int)axis, n4 = n >> 2;
+  for (int64_t g = blockIdx.x; g * SMX_ROWS < rows; g += gridDim.x) {
+    const int64_t row = g * SMX_ROWS + warp;
+    const bool live = row < rows;
+    if (live) {
+      const float4* xr = reinterpret_cast<const float4*>(x + row * axis);
+      float4* yr = reinterpret_cast<float4*>(y + row * axis);
+      float mx = x[row * axis];  // fmaxf is order-free (NaN ignored) up to the sign of zero
+      for (int a0 = lane; a0 < n4; a0 += 32 * SML_LOADS_HBM) {
+        float4 v[SML_LOADS_HBM];
+#pragma unroll
+        for (int j = 0; j < SML_LOADS_HBM; ++j)
+          if (a0 + 32 * j < n4) v[j] = xr[a0 + 32 * j];
+#pragma unroll
+        for (int j = 0; j < SML_LOADS_HBM; ++j)
+          if (a0 + 32 * j < n4) mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, v[j].x), v[j].y), v[j].z), v[j].w);
+      }
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      for (int a0 = lane; a0 < n4; a0 += 32 * SML_LOADS) {
+        float4 v[SML_LOADS];
+#pragma unroll
+        for (int j = 0; j < SML_LOADS; ++j)
+          if (a0 + 32 * j < n4) v[j] = __ldcs(xr + a0 + 32 * j);
+#pragma unroll
+        for (int j = 0; j < SML_LOADS; ++j)
+          if (a0 + 32 * j < n4) {
+            v[j].x = expf(__fsub_rn(v[j].x, mx));
+            v[j].y = expf(__fsub_rn(v[j].y, mx));
+            v[j].z = expf(__fsub_rn(v[j].z, mx));
+            v[j].w = expf(__fsub_rn(v[j].w, mx));
+            yr[a0 + 32 * j] = v[j];
+          }
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && lane < SMX_ROWS && g * SMX_ROWS + lane < rows) {
+      const float* er = y + (g * SMX_ROWS + lane) * axis;
+      float* rg = ring + lane * SML_LANE;
+      const int nch = (n + SML_CH - 1) / SML_CH;
+      // chunk c goes to ring slot c % SML_ST; issued after the adds of chunk
+      // c - SML_ST + 1, so the slot it overwrites was read one chunk earlier
+      auto issue = [&](int c) {
+        if (c < nch) {
+          const int b0 = c * SML_CH, cnt = min(SML_CH, n - b0) >> 2;
+          float* dst = rg + (c % SML_ST) * SML_CH;
+          for (int j = 0; j < cnt; ++j) cp_async16_cg(dst + 4 * j, er + b0 + 4 * j);
+        }
+        cp_async_commit();
+      };
+#pragma unroll
+      for (int c = 0; c < SML_ST - 1; ++c) issue(c);
+      float sum = 0.0f;
+      for (int c = 0; c < nch; ++c) {
+        cp_async_wait_group<SML_ST - 2>();
+        const float* src = rg + (c % SML_ST) * SML_CH;
+        const int cnt = min(SML_CH, n - c * SML_CH);
+        if (cnt == SML_CH) {
+#pragma unroll
+          for (int j = 0; j < SML_CH / 4; ++j) {
+            const float4 v = reinterpret_cast<const float4*>(src)[j];
+            sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
+          }
+        } else {
+          for (int k = 0; k < cnt; ++k) sum = __fadd_rn(sum, src[k]);
+        }
+        issue(c + SML_ST - 1);
+      }
+      cp_async_wait_group<0>();
+      s_sum[lane] = sum;
+    }
+    __syncthreads();
+    if (live) {
+      const float sum = s_sum[warp];
+      float4* yr = reinterpret_cast<float4*>(y + row * axis);
+      for (int a0 = lane; a0 < n4; a0 += 32 * SML_LOADS) {
+        float4 v[SML_LOADS];
+#pragma unroll
+        for (int j = 0; j < SML_LOADS; ++j)
+          if (a0 + 32 * j < n4) v[j] = __ldcg(yr + a0 + 32 * j);
+#pragma unroll
+        for (int j = 0; j < SML_LOADS; ++j)
+          if (a0 + 32 * j < n4) {
+            v[j].x = __fdiv_rn(v[j].x, sum);
+            v[j].y = __fdiv_rn(v[j].y, sum);
+            v[j].z = __fdiv_rn(v[j].z, sum);
+            v[j].w = __fdiv_rn(v[j].w, sum);
+            __stcs(yr + a0 + 32 * j, v[j]);
+          }
+      }
+    }
   }
 }
 
@@ -204,10 +447,48 @@ int launch_softmax_f32(const PlanOp& op, void* const* ptrs, const OpState*, cons
                             : outer_full;
   const int64_t rows = outer * op.ip[SM_INNER];
   if (rows == 0 || op.ip[SM_AXIS] == 0) return 0;
+  const int64_t axis = op.ip[SM_AXIS];
+  const float* x = (const float*)ptrs[op.t[0]];
+  float* y = (float*)ptrs[op.t[1]];
+  const bool vec = (axis & 3) == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0;
+  // rows staged in shared memory while at least SMX_MIN_ROWS_PER_SM fit per
+  // SM; longer rows of a multiple of four floats stream through L2
+  // (shared-memory row stride 4 (mod 32) floats: 16-byte rows, and the summing
+  // lanes read different banks)
+  const int64_t stride = ((axis + 31) & ~int64_t(31)) + 4;
+  const bool fits = op.ip[SM_INNER] == 1 && (stride + 1) * 4 <= SMX_MAX_BYTES;
+  int nr = 1, per_sm = 0;
+  size_t smem = 0;
+  void (*fn)(const float*, float*, int64_t, int64_t, int64_t) =
+      vec ? softmax_rows_kernel<true> : softmax_rows_kernel<false>;
+  if (fits) {
+    nr = (stride + 1) * 4 * SMX_ROWS <= SMX_MAX_BYTES ? SMX_ROWS : 1;
+    smem = (size_t)(stride * nr + nr) * 4;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 32 * nr, smem);
+    if (e != cudaSuccess) return 4;
+  }
+  if (op.ip[SM_INNER] == 1 && vec && axis < (int64_t(1) << 30) && (int64_t)per_sm * nr < SMX_MIN_ROWS_PER_SM) {
+    const int64_t blocks64 = (rows + SMX_ROWS - 1) / SMX_ROWS;
+    const int64_t cap = 148 * SML_BLOCKS_PER_SM;
+    const int blocks = (int)(blocks64 < cap ? blocks64 : cap);
+    cudaError_t e =
+        launch_pdl(softmax_stream_kernel, dim3(blocks), dim3(32 * SMX_ROWS), 0, ctx.stream, x, y, rows, axis);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
+  if (fits) {
+    const int64_t blocks64 = (rows + nr - 1) / nr;
+    const int64_t cap = 148 * (int64_t)(per_sm > 0 ? per_sm : 1);
+    const int blocks = (int)(blocks64 < cap ? blocks64 : cap);
+    cudaError_t e = launch_pdl(fn, dim3(blocks), dim3(32 * nr), smem, ctx.stream, x, y, rows, axis, stride);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
   const int64_t blocks64 = (rows + 7) / 8;
   const int blocks = (int)(blocks64 < 148 * 32 ? blocks64 : 148 * 32);
-  cudaError_t e = launch_pdl(softmax_f32_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const float*)ptrs[op.t[0]],
-                             (float*)ptrs[op.t[1]], rows, op.ip[SM_AXIS], op.ip[SM_INNER]);
+  cudaError_t e =
+      launch_pdl(softmax_f32_kernel, dim3(blocks), dim3(256), 0, ctx.stream, x, y, rows, axis, op.ip[SM_INNER]);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }

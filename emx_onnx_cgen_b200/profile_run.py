@@ -1,6 +1,6 @@
 """Run one workload's launch plan a few times on cuda:0 (the command profilers wrap).
 
-    python -m emx_onnx_cgen_b200.profile_run --workload qconv_stack_int8 --iters 5 [--batch 8]
+    python -m emx_onnx_cgen_b200.profile_run --workload qconv_stack_int8 --iters 5 [--batch 8] [--kw JSON]
 
 Device-resident inputs, no host copies, one synchronisation at the end, so a
 profiler sees only this library's kernels after the first plan load.  Prints
@@ -25,8 +25,9 @@ def main() -> None:
     ap.add_argument("--workload", default="qconv_stack_int8")
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch/rows (0: default)")
+    ap.add_argument("--kw", default="", help='builder arguments as JSON, e.g. \'{"shape": [16384, 4096]}\'')
     args = ap.parse_args()
-    kw = {}
+    kw = {k: tuple(v) if isinstance(v, list) else v for k, v in json.loads(args.kw).items()} if args.kw else {}
     if args.batch:
         key = {"qconv_stack_int8": "batch", "mlp_fp32": "m", "llama_mlp_int4": "m", "attention_fp16": "batch",
                "lstm_fp32": "batch"}[args.workload]

@@ -51,7 +51,13 @@ def test_exact_vs_port(wl):
         assert_bitexact(out[k], v, k)
 
 
-@pytest.mark.parametrize("shape,axis", [((64, 1000), -1), ((8, 300, 5), 1), ((2, 3, 4, 50), 3), ((1, 1), 0)])
+# rows staged in shared memory: (64, 1000), (300, 4096) and (10, 4) four-float copies, (5, 4097) and
+# (2, 3, 4, 50) scalar, (2, 20001) one row per block; rows too long for twelve per SM stream through
+# L2: (7, 20000) and (3, 60000), both ending in a partial chunk; (2, 60001) and (8, 300, 5) take the
+# strided kernel
+@pytest.mark.parametrize("shape,axis", [((64, 1000), -1), ((300, 4096), 1), ((7, 20000), 1), ((3, 60000), 1),
+                                        ((10, 4), 1), ((5, 4097), -1), ((2, 20001), 1), ((2, 60001), 1),
+                                        ((8, 300, 5), 1), ((2, 3, 4, 50), 3), ((1, 1), 0)])
 def test_softmax_vs_port(shape, axis):
     require_gpu()
     wl = W.softmax_f32(shape, axis)
