@@ -90,10 +90,13 @@ enum { ATF_SCALE };
 enum { LS_T, LS_B, LS_I, LS_H };
 enum { LS_TILE_UNITS = 16 };
 
-// ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y
+// ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y;
+//      tensor-core plans add t[3]=B^T [N][K] u8, t[4]=B's column sums [N] i32, t[5]=A's row sums [M] i32
+//      (scratch); with QM_B_PACKED (B an initializer) t[3] and t[4] are weights packed by the planner,
+//      otherwise scratch the run fills
 enum {
   QM_M, QM_K, QM_N, QM_A_SIGNED, QM_B_SIGNED, QM_A_ZERO, QM_B_ZERO, QM_QUANTIZED, QM_USE_INT, QM_FRAC_BITS,
-  QM_MULT, QM_Y_ZERO, QM_Y_SIGNED, QM_ROWS_PER_BATCH
+  QM_MULT, QM_Y_ZERO, QM_Y_SIGNED, QM_ROWS_PER_BATCH, QM_B_PACKED
 };
 enum { QMF_SCALE };
 
@@ -181,7 +184,11 @@ int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCt
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_lstm_f32(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_lstm_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+struct QMatMulParams;
+int prepare_qmatmul(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_qmatmul(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_qgemm_tc();
+int launch_qgemm_tc(const PlanOp&, void* const*, const LaunchCtx&, const QMatMulParams&, int*);
 int launch_conv_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_softmax_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_quant(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);

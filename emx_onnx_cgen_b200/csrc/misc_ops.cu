@@ -20,6 +20,7 @@
 // where the reference calls glibc's.
 #include "host_util.h"
 #include "kernels.h"
+#include "qmatmul.cuh"
 #include "tc100.cuh"
 
 namespace emx {
@@ -29,18 +30,6 @@ __device__ __forceinline__ int32_t load8(const uint8_t* p, int64_t i, int is_sig
 }
 
 // ------------------------------------------------------------------ QLinearMatMul / MatMulInteger
-struct QMatMulParams {
-  const uint8_t* a;
-  const uint8_t* b;
-  void* y;
-  int64_t m;
-  int k, n, a_signed, b_signed, za, zb;
-  // requantisation (QLinearMatMul only)
-  int quantized, use_int, frac_bits, zy, y_signed;
-  int64_t mult;
-  float scale;
-};
-
 __global__ void qmatmul_kernel(const QMatMulParams p) {
   pdl_wait();
   pdl_launch_dependents();
@@ -52,27 +41,16 @@ __global__ void qmatmul_kernel(const QMatMulParams p) {
   for (int k = 0; k < p.k; ++k)
     acc += (load8(arow, k, p.a_signed) - p.za) * (load8(p.b, (int64_t)k * p.n + n, p.b_signed) - p.zb);
   const int64_t o = m * p.n + n;
-  if (!p.quantized) {
+  if (!p.quantized)
     reinterpret_cast<int32_t*>(p.y)[o] = acc;
-    return;
-  }
-  int64_t q;
-  if (p.use_int) {
-    int64_t r = (int64_t)acc * p.mult;
-    if (p.frac_bits > 0) {
-      const uint64_t mag = r < 0 ? (uint64_t)(-r) : (uint64_t)r;
-      uint64_t quo = mag >> p.frac_bits;
-      const uint64_t rem = mag & ((1ull << p.frac_bits) - 1ull), half = 1ull << (p.frac_bits - 1);
-      if (rem > half || (rem == half && (quo & 1ull))) ++quo;
-      r = r < 0 ? -(int64_t)quo : (int64_t)quo;
-    }
-    q = r + (int64_t)p.zy;
-  } else {
-    q = __double2ll_rn(__dadd_rn(__dmul_rn((double)acc, (double)p.scale), (double)p.zy));
-  }
-  const int64_t lo = p.y_signed ? -128 : 0, hi = p.y_signed ? 127 : 255;
-  q = q < lo ? lo : (q > hi ? hi : q);
-  reinterpret_cast<uint8_t*>(p.y)[o] = (uint8_t)q;
+  else
+    reinterpret_cast<uint8_t*>(p.y)[o] = qm_requant(acc, p);
+}
+
+int prepare_qmatmul(const PlanOp& op, void* const*, OpState*, int, char* msg, size_t n) {
+  if (op.n_tensors > 5 && op.t[3] >= 0 && prepare_qgemm_tc())
+    return fail(msg, n, 4, "cudaFuncSetAttribute (QLinearMatMul tensor-core kernel) failed");
+  return 0;
 }
 
 int launch_qmatmul(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
@@ -96,6 +74,10 @@ int launch_qmatmul(const PlanOp& op, void* const* ptrs, const OpState*, const La
   p.y_signed = (int)op.ip[QM_Y_SIGNED];
   p.scale = (float)op.fp[QMF_SCALE];
   if (p.m <= 0 || p.n <= 0) return 0;
+  if (op.n_tensors > 5 && op.t[3] >= 0 && op.t[4] >= 0 && op.t[5] >= 0) {  // planned for the tensor cores
+    const int r = launch_qgemm_tc(op, ptrs, ctx, p, launches);
+    if (r >= 0) return r;
+  }
   dim3 grid((unsigned)((p.n + 31) / 32), (unsigned)((p.m + 7) / 8));
   if (grid.y > 65535u) return 5;
   cudaError_t e = launch_pdl(qmatmul_kernel, grid, dim3(256), 0, ctx.stream, p);

@@ -52,8 +52,8 @@ const KernelEntry kKernels[] = {
     {emx::K_MUL_F16, nullptr, emx::launch_mul_f16, "mul_f16"},
     {emx::K_LSTM_F32, emx::prepare_lstm_f32, emx::launch_lstm_f32, "lstm_f32"},
     {emx::K_ATTENTION_F16, emx::prepare_attention, emx::launch_attention, "attention_f16"},
-    {emx::K_QLINEAR_MATMUL, nullptr, emx::launch_qmatmul, "qlinear_matmul"},
-    {emx::K_MATMUL_INTEGER, nullptr, emx::launch_qmatmul, "matmul_integer"},
+    {emx::K_QLINEAR_MATMUL, emx::prepare_qmatmul, emx::launch_qmatmul, "qlinear_matmul"},
+    {emx::K_MATMUL_INTEGER, emx::prepare_qmatmul, emx::launch_qmatmul, "matmul_integer"},
     {emx::K_CONV_F32, nullptr, emx::launch_conv_f32, "conv_f32"},
     {emx::K_SOFTMAX_F32, nullptr, emx::launch_softmax_f32, "softmax_f32"},
     {emx::K_QUANTIZE_LINEAR, nullptr, emx::launch_quant, "quantize_linear"},

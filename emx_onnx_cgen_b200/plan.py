@@ -961,7 +961,24 @@ class B200PlanEmitter:
         else:
             y = self._dest(op.output, "i32", tuple(op.output_shape))
             kern = K.K_MATMUL_INTEGER
-        self._b.op(kern, [a, b_, y], ip, fp, label=f"{op.output} ({what})", batched=batched)
+        tensors, label = [a, b_, y], f"{op.output} ({what})"
+        k, n, m = int(op.k), int(op.n), int(op.m)
+        if self.use_tensor_cores and k % 16 == 0 and 16 <= k <= 32768:
+            # tcgen05 kind::i8 path: B^T [N][K] (the K-major operand) and B's column sums -- packed
+            # once here when B is an initializer, else filled by every run -- and A's row sums
+            if op.input1 in self._consts:
+                bc = self._consts[op.input1].reshape(k, n)
+                tensors += [self._b.weight(np.ascontiguousarray(bc.T).view(np.uint8), "u8",
+                                           f"{op.output}:b-transposed"),
+                            self._b.weight(bc.astype(np.int64).sum(axis=0).astype(np.int32), "i32",
+                                           f"{op.output}:b-column-sums")]
+                ip[K.QM_B_PACKED] = 1
+            else:
+                tensors += [self._b.arena_tensor(T_TEMP, "u8", (n, k), name=f"{op.output}:b-transposed"),
+                            self._b.arena_tensor(T_TEMP, "i32", (n,), name=f"{op.output}:b-column-sums")]
+            tensors.append(self._b.arena_tensor(T_TEMP, "i32", (m,), name=f"{op.output}:a-row-sums"))
+            label += " [tensor cores]"
+        self._b.op(kern, tensors, ip, fp, label=label, batched=batched)
 
     def _emit_QLinearMatMulOp(self, i, op):
         self._emit_matmul8(op, True)

@@ -60,6 +60,11 @@ CASES = [
     ("qmm_m3_k17_n9_u8b", "qlinear_matmul_u8", dict(m=3, k=17, n=9, a_zero=100, b_dtype="u8", b_zero=120), 1),
     ("qmm_m4_k20_n7_intrequant", "qlinear_matmul_u8", dict(m=4, k=20, n=7, scales=(0.5, 0.25, 4.0)), 2),
     ("mmi_m4_k33_n10", "matmul_integer_u8", dict(m=4, k=33, n=10), 0),
+    # K a multiple of 16: the tensor-core path
+    ("qmm_m6_k64_n40", "qlinear_matmul_u8", dict(m=6, k=64, n=40), 3),
+    ("qmm_m5_k48_n20_u8b_intrequant", "qlinear_matmul_u8",
+     dict(m=5, k=48, n=20, a_zero=7, b_dtype="u8", b_zero=130, scales=(0.5, 0.25, 4.0)), 4),
+    ("mmi_m4_k32_n24", "matmul_integer_u8", dict(m=4, k=32, n=24), 1),
     ("conv_b2_c4_9x7_s2", "conv_f32", dict(batch=2, cin=4, cout=6, h=9, w=7, stride=2, pad=1), 0),
     ("conv_b1_c4_8x8_g2_d2", "conv_f32", dict(batch=1, cin=4, cout=4, h=8, w=8, pad=2, dilation=2, group=2), 1),
     ("softmax_4x37", "softmax_f32", dict(shape=(4, 37)), 0),

@@ -51,6 +51,70 @@ def test_exact_vs_port(wl):
         assert_bitexact(out[k], v, k)
 
 
+# K a multiple of 16 (<= 32768): tcgen05 kind::i8 with the zero points restored in the epilogue.
+# Partial row / column tiles, each zero-point combination (row sums, column sums, both, none),
+# both requantisations, scalar and vector stores, signed and unsigned B.
+@pytest.mark.parametrize("wl", [
+    W.qlinear_matmul_u8(m=300, k=512, n=200),
+    W.qlinear_matmul_u8(m=257, k=1024, n=513, a_zero=0, b_dtype="u8", b_zero=77),
+    W.qlinear_matmul_u8(m=129, k=272, n=96, a_zero=9, b_dtype="u8", b_zero=250, scales=(0.25, 0.125, 2.0)),
+    W.matmul_integer_u8(m=384, k=2048, n=256, a_zero=128, b_zero=3),
+    W.matmul_integer_u8(m=100, k=32, n=20, a_zero=0, b_zero=0),
+    W.matmul_integer_u8(m=1, k=16, n=1, a_zero=255, b_zero=-128),
+], ids=lambda w: w.name + str(sorted(w.params.items()))[:60])
+def test_qmatmul_tensor_cores_vs_port(wl):
+    require_gpu()
+    plan = plan_for(wl)
+    assert "[tensor cores]" in plan.ops[0].label
+    x = wl.make_inputs(5)
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan).run(x)
+    for k, v in ref.items():
+        assert_bitexact(out[k], v, k)
+
+
+@pytest.mark.parametrize("quantized", [False, True])
+def test_qmatmul_tensor_cores_runtime_b(quantized):
+    """B a graph input rather than an initializer: B^T and its column sums are
+    written by a preparation launch every run."""
+    require_gpu()
+    m, k, n = 200, 320, 72
+    if quantized:
+        inits = {"a_s": np.asarray(0.02, np.float32).reshape(()), "a_z": np.asarray(17, np.uint8).reshape(()),
+                 "b_s": np.asarray(0.01, np.float32).reshape(()), "b_z": np.asarray(-9, np.int8).reshape(()),
+                 "y_s": np.asarray(0.7, np.float32).reshape(()), "y_z": np.asarray(3, np.uint8).reshape(())}
+        node = NodeSpec("QLinearMatMul", "qmm", ("A", "a_s", "a_z", "B", "b_s", "b_z", "y_s", "y_z"), ("Y",))
+        out = TensorSpec("Y", "u8", (m, n))
+    else:
+        inits = {"a_z": np.asarray(200, np.uint8).reshape(()), "b_z": np.asarray(5, np.int8).reshape(())}
+        node = NodeSpec("MatMulInteger", "mmi", ("A", "B", "a_z", "b_z"), ("Y",))
+        out = TensorSpec("Y", "i32", (m, n))
+    g = GraphSpec("qmm_runtime_b", [TensorSpec("A", "u8", (m, k)), TensorSpec("B", "i8", (k, n))], [out], [node],
+                  initializers=inits, opset_imports=(("", 10),))
+    wl = W.Workload("qmm_runtime_b", g, None, {"A": 0, "Y": 0}, {})
+    plan = plan_for(wl)
+    assert "[tensor cores]" in plan.ops[0].label
+    rng = np.random.default_rng(11)
+    x = {"A": rng.integers(0, 256, (m, k)).astype(np.uint8), "B": rng.integers(-128, 128, (k, n)).astype(np.int8)}
+    ref = oracle.run_graph(g, x)
+    sess = Session(plan)
+    for _ in range(2):  # the second run recomputes B^T and the column sums from zero
+        got = sess.run(x)
+        assert_bitexact(got["Y"], ref["Y"], "Y")
+
+
+def test_qmatmul_tensor_cores_largest_k():
+    """K = 32768 with every A byte 255: the largest raw sums the path admits."""
+    require_gpu()
+    wl = W.matmul_integer_u8(m=130, k=32768, n=40, a_zero=0, b_zero=0)
+    plan = plan_for(wl)
+    assert "[tensor cores]" in plan.ops[0].label
+    x = {"A": np.full((130, 32768), 255, np.uint8)}
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan).run(x)
+    assert_bitexact(out["Y"], ref["Y"], "Y")
+
+
 # rows staged in shared memory: (64, 1000), (300, 4096) and (10, 4) four-float copies, (5, 4097) and
 # (2, 3, 4, 50) scalar, (2, 20001) one row per block; rows too long for twelve per SM stream through
 # L2: (7, 20000) and (3, 60000), both ending in a partial chunk; (2, 60001) and (8, 300, 5) take the
