@@ -101,7 +101,10 @@ enum {
 enum { QMF_SCALE };
 
 // ---- K_CONV_F32: t[0]=X NCHW, t[1]=W OIHW, t[2]=bias|-1, t[3]=Y
-enum { CF_N, CF_C, CF_H, CF_W, CF_OC, CF_KH, CF_KW, CF_OH, CF_OW, CF_SH, CF_SW, CF_PT, CF_PL, CF_DH, CF_DW, CF_GROUP };
+enum {
+  CF_N, CF_C, CF_H, CF_W, CF_OC, CF_KH, CF_KW, CF_OH, CF_OW, CF_SH, CF_SW, CF_PT, CF_PL, CF_DH, CF_DW, CF_GROUP,
+  CF_ZERO_TAPS_OK  // 1: out-of-image taps may be added as x = 0 (finite weights, no -0 bias)
+};
 
 // ---- K_SOFTMAX_F32: t[0]=X, t[1]=Y; shape viewed as [outer][axis][inner]
 enum { SM_OUTER, SM_AXIS, SM_INNER, SM_OUTER_PER_BATCH };

@@ -9,7 +9,8 @@
 //                  expression sa * sb / sy; clamp.
 //   MatMulInteger  templates/matmul_integer_op.c.j2: int32 sum of (a - za)(b - zb).
 //   Conv (fp32)    templates/conv_op.c.j2: acc = bias; in-bounds taps in
-//                  (ic, kh, kw) order, acc += x * w (separately rounded, no FMA).
+//                  (ic, kh, kw) order, acc += x * w (separately rounded, no FMA);
+//                  tiled through shared memory, 16 outputs per thread.
 //   Softmax (fp32) templates/softmax_op.c.j2: fmaxf chain, expf, sequential float
 //                  sum, division (one warp per row; the sum stays sequential;
 //                  contiguous rows are staged in shared memory).
@@ -92,6 +93,7 @@ struct ConvF32Params {
   const float* bias;
   float* y;
   int n, c, h, wd, oc, kh, kw, oh, ow, sh, sw, pt, pl, dh, dw, group;
+  int zero_taps_ok;  // out-of-image taps may be added as zeros (planner-checked weights and bias)
 };
 
 __global__ void conv2d_f32_kernel(const ConvF32Params p) {
@@ -125,6 +127,165 @@ __global__ void conv2d_f32_kernel(const ConvF32Params p) {
   }
 }
 
+// Tiled form, for kernels of at most CT_MAX_TAPS taps: a block computes CT_OC
+// output channels of one group x CT_P output pixels of one image; thread
+// (tx = t % 16, ty = t / 16) owns channels ty*CT_RI .. +CT_RI-1 and pixels tx + 16j
+// (j < 4).  Per input channel, ascending, the block stages in shared memory
+// the input value of every (tap, pixel) and the weight of every (tap,
+// channel); each thread then adds its 16 outputs' terms tap by tap (kh, kw
+// ascending), multiply and add rounded separately, so every output sees the
+// reference's statements in the reference's order.  A tap outside the image
+// is skipped, as in the reference (not added as zero: acc + (+0) turns -0 into
+// +0, and 0 * inf is NaN), through a per-pixel bit mask computed once per
+// block (warps whose pixels are all interior skip the test, and so does every
+// warp when the planner found that adding x = 0 for those taps cannot change
+// a result: finite weights and no -0 bias; the taps are then staged as zeros).  The next
+// channel's entries arrive by cp.async while the current one is summed (two
+// shared-memory buffers).  3 x 3 kernels get the tap loop unrolled.
+constexpr int CT_RI = 4;  // output channels per thread
+constexpr int CT_OC = 8 * CT_RI, CT_P = 64, CT_THREADS = 128, CT_MAX_TAPS = 32;
+
+// One input channel's terms for a thread's CT_RI channels x 4 pixels, taps in
+// order; CHECK: test each (pixel, tap) against the in-image mask (border
+// pixels), otherwise every tap is in the image.
+template <int TAPS, bool CHECK>
+__device__ __forceinline__ void conv_tile_channel(float (&acc)[CT_RI][4], const float* xsb, const float* wsb, int taps_rt,
+                                                  const uint32_t (&msk)[4], int tx, int ty) {
+  const int taps = TAPS > 0 ? TAPS : taps_rt;
+#pragma unroll
+  for (int tap = 0; tap < taps; ++tap) {
+    float wv[CT_RI];
+#pragma unroll
+    for (int i = 0; i < CT_RI; i += 4) {
+      const float4 w4 = *reinterpret_cast<const float4*>(wsb + tap * CT_OC + ty * CT_RI + i);
+      wv[i] = w4.x;
+      wv[i + 1] = w4.y;
+      wv[i + 2] = w4.z;
+      wv[i + 3] = w4.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (!CHECK || ((msk[j] >> tap) & 1u)) {
+        const float xv = xsb[tap * CT_P + tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < CT_RI; ++i) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv, wv[i]));
+      }
+    }
+  }
+}
+
+template <int TAPS>
+__global__ void __launch_bounds__(CT_THREADS) conv2d_f32_tiled_kernel(const ConvF32Params p, int p_tiles,
+                                                                      int oc_tiles) {
+  __shared__ __align__(16) float xs[2][CT_MAX_TAPS * CT_P];   // [tap][pixel]
+  __shared__ __align__(16) float ws[2][CT_MAX_TAPS * CT_OC];  // [tap][channel]
+  __shared__ int s_base[CT_P];                                // iy0 * W + ix0 of each pixel
+  __shared__ uint32_t s_mask[CT_P];                           // bit tap: the tap reads inside the image
+  __shared__ int s_tapoff[CT_MAX_TAPS];                       // kh * dh * W + kw * dw
+  pdl_wait();
+  pdl_launch_dependents();
+  const int taps = p.kh * p.kw;
+  const int gic = p.c / p.group, goc = p.oc / p.group;
+  const int npix = p.oh * p.ow;
+  int bid = blockIdx.x;
+  const int ptile = bid % p_tiles;
+  bid /= p_tiles;
+  const int otile = bid % oc_tiles;
+  bid /= oc_tiles;
+  const int g = bid % p.group, b = bid / p.group;
+  const int p0 = ptile * CT_P, oc0 = otile * CT_OC;
+  const int t = threadIdx.x;
+  if (t < CT_P) {
+    const int pix = p0 + t;
+    uint32_t m = 0;
+    int base = 0;
+    if (pix < npix) {
+      const int oy = pix / p.ow, ox = pix - oy * p.ow;
+      const int iy0 = oy * p.sh - p.pt, ix0 = ox * p.sw - p.pl;
+      base = iy0 * p.wd + ix0;
+      for (int a = 0; a < p.kh; ++a)
+        for (int c = 0; c < p.kw; ++c) {
+          const int iy = iy0 + a * p.dh, ix = ix0 + c * p.dw;
+          if (iy >= 0 && iy < p.h && ix >= 0 && ix < p.wd) m |= 1u << (a * p.kw + c);
+        }
+    }
+    s_base[t] = base;
+    s_mask[t] = m;
+  } else if (t - CT_P < taps) {
+    const int tap = t - CT_P, a = tap / p.kw, c = tap - a * p.kw;
+    s_tapoff[tap] = a * p.dh * p.wd + c * p.dw;
+  }
+  __syncthreads();
+
+  const int64_t plane = (int64_t)p.h * p.wd;
+  const float* xb = p.x + ((int64_t)b * p.c + (int64_t)g * gic) * plane;
+  const float* wb = p.w + (int64_t)(g * goc + oc0) * gic * taps;  // OIHW
+  // asynchronous 4-byte copies of one input channel's entries into buffer
+  // `buf`; entries of taps outside the image are never read, so not copied
+  auto issue = [&](int ic, int buf) {
+    const float* xc = xb + (int64_t)ic * plane;
+    for (int e = t; e < taps * CT_P; e += CT_THREADS) {
+      const int tap = e / CT_P, px = e % CT_P;
+      if ((s_mask[px] >> tap) & 1u)
+        cp_async4(&xs[buf][e], xc + s_base[px] + s_tapoff[tap]);
+      else if (p.zero_taps_ok)
+        xs[buf][e] = 0.0f;
+    }
+    for (int e = t; e < taps * CT_OC; e += CT_THREADS) {
+      const int tap = e / CT_OC, o = e % CT_OC;
+      if (oc0 + o < goc)
+        cp_async4(&ws[buf][e], wb + ((int64_t)o * gic + ic) * taps + tap);
+      else
+        ws[buf][e] = 0.0f;
+    }
+    cp_async_commit();
+  };
+
+  const int tx = t & 15, ty = t >> 4;
+  float acc[CT_RI][4];
+  uint32_t msk[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) msk[j] = s_mask[tx + 16 * j];
+  const uint32_t all_taps = taps == 32 ? 0xFFFFFFFFu : (1u << taps) - 1u;
+  // warp-uniform, so a warp never runs both forms
+  const bool interior =
+      p.zero_taps_ok || __all_sync(0xffffffffu, (msk[0] & msk[1] & msk[2] & msk[3]) == all_taps);
+#pragma unroll
+  for (int i = 0; i < CT_RI; ++i) {
+    const int o = oc0 + ty * CT_RI + i;
+    const float bias = p.bias && o < goc ? p.bias[g * goc + o] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = bias;
+  }
+  issue(0, 0);
+  for (int ic = 0; ic < gic; ++ic) {
+    const int buf = ic & 1;
+    if (ic + 1 < gic) {
+      issue(ic + 1, buf ^ 1);
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
+    }
+    __syncthreads();  // every thread's copies of channel ic have landed
+    if (interior)
+      conv_tile_channel<TAPS, false>(acc, xs[buf], ws[buf], taps, msk, tx, ty);
+    else
+      conv_tile_channel<TAPS, true>(acc, xs[buf], ws[buf], taps, msk, tx, ty);
+    __syncthreads();  // channel ic read by all before the next issue refills this buffer
+  }
+#pragma unroll
+  for (int i = 0; i < CT_RI; ++i) {
+    const int o = oc0 + ty * CT_RI + i;
+    if (o >= goc) continue;
+    float* yo = p.y + ((int64_t)b * p.oc + g * goc + o) * npix;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int pix = p0 + tx + 16 * j;
+      if (pix < npix) yo[pix] = acc[i][j];
+    }
+  }
+}
+
 int launch_conv_f32(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   ConvF32Params p{};
   p.x = (const float*)ptrs[op.t[0]];
@@ -147,8 +308,22 @@ int launch_conv_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   p.dh = (int)op.ip[CF_DH];
   p.dw = (int)op.ip[CF_DW];
   p.group = (int)op.ip[CF_GROUP];
+  p.zero_taps_ok = (int)op.ip[CF_ZERO_TAPS_OK];
   const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;
   if (total == 0) return 0;
+  if (p.kh * p.kw <= CT_MAX_TAPS && p.c / p.group > 0) {
+    const int64_t p_tiles = ((int64_t)p.oh * p.ow + CT_P - 1) / CT_P;
+    const int64_t oc_tiles = (p.oc / p.group + CT_OC - 1) / CT_OC;
+    const int64_t blocks = (int64_t)p.n * p.group * oc_tiles * p_tiles;
+    if (blocks < (int64_t(1) << 31)) {
+      void (*fn)(ConvF32Params, int, int) =
+          p.kh * p.kw == 9 ? conv2d_f32_tiled_kernel<9> : conv2d_f32_tiled_kernel<0>;
+      cudaError_t e =
+          launch_pdl(fn, dim3((unsigned)blocks), dim3(CT_THREADS), 0, ctx.stream, p, (int)p_tiles, (int)oc_tiles);
+      ++*launches;
+      return e == cudaSuccess ? 0 : 4;
+    }
+  }
   const int64_t blocks64 = (total + 255) / 256;
   const int blocks = (int)(blocks64 < 148 * 64 ? blocks64 : 148 * 64);
   cudaError_t e = launch_pdl(conv2d_f32_kernel, dim3(blocks), dim3(256), 0, ctx.stream, p);

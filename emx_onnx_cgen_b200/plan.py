@@ -997,7 +997,15 @@ class B200PlanEmitter:
         oh, ow = op.out_spatial
         y = self._dest(op.output, "f32", (n, int(op.out_channels), oh, ow))
         kh, kw = op.kernel_shape
-        self._b.op(K.K_CONV_F32, [x, w, t_b, y], {
+        # Adding x * w = +-0 for a tap outside the image equals skipping it (the reference
+        # skips) unless the accumulator is -0, which needs a -0 bias, or w is inf/NaN
+        # (0 * inf = NaN).  With constant weights that rule both out, the kernel may stage
+        # zeros for such taps and drop the per-tap test.
+        zero_taps_ok = op.weights in self._consts and bool(np.isfinite(self._consts[op.weights]).all())
+        if zero_taps_ok and op.bias is not None:
+            bias = self._consts.get(op.bias)
+            zero_taps_ok = bias is not None and not bool(((bias == 0) & np.signbit(bias)).any())
+        self._b.op(K.K_CONV_F32, [x, w, t_b, y], {K.CF_ZERO_TAPS_OK: int(zero_taps_ok),
             K.CF_N: n, K.CF_C: c, K.CF_H: h, K.CF_W: wd, K.CF_OC: int(op.out_channels), K.CF_KH: kh, K.CF_KW: kw,
             K.CF_OH: oh, K.CF_OW: ow, K.CF_SH: op.strides[0], K.CF_SW: op.strides[1], K.CF_PT: op.pads[0],
             K.CF_PL: op.pads[1], K.CF_DH: op.dilations[0], K.CF_DW: op.dilations[1], K.CF_GROUP: int(op.group)},

@@ -133,6 +133,38 @@ def test_softmax_vs_port(shape, axis):
     assert int(ulp_diff_f32(out, ref).max(initial=0)) <= SOFTMAX_MAX_ULP
 
 
+@pytest.mark.parametrize("wl", [
+    W.conv_f32(batch=2, cin=40, cout=70, h=23, w=19, kernel=3, pad=1),         # partial channel / pixel tiles
+    W.conv_f32(batch=1, cin=8, cout=8, h=9, w=9, kernel=7, pad=3),              # 49 taps: untiled kernel
+    W.conv_f32(batch=2, cin=12, cout=36, h=15, w=13, kernel=5, stride=3, pad=2, dilation=2, group=4),
+], ids=lambda w: w.name + str(sorted(w.params.items()))[:60])
+def test_conv_f32_tiled_vs_port(wl):
+    require_gpu()
+    x = wl.make_inputs(6)
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan_for(wl)).run(x)
+    assert_bitexact(out["Y"], ref["Y"], "Y")
+
+
+def test_conv_f32_skipped_taps():
+    """Taps outside the image are skipped, not added as zero: an output whose
+    taps all fall outside keeps a -0.0 bias, and an infinite weight over an
+    in-image zero gives NaN only where the reference multiplies."""
+    require_gpu()
+    wl = W.conv_f32(batch=1, cin=3, cout=5, h=6, w=6, kernel=3, pad=3)
+    wl.graph.initializers["bias"] = np.full(5, -0.0, np.float32)
+    w = wl.graph.initializers["W"].copy()
+    w[1, 2, 0, 0] = np.inf
+    w[3, 0, 2, 1] = -np.inf
+    wl.graph.initializers["W"] = w
+    x = wl.make_inputs(7)
+    x["X"][0, :, ::2, ::3] = 0.0
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan_for(wl)).run(x)
+    assert np.signbit(ref["Y"][0, :, 0, 0]).all()  # the corner output sees no tap
+    assert_bitexact(out["Y"], ref["Y"], "Y")
+
+
 def test_quantize_per_axis_and_specials():
     require_gpu()
     shape = (3, 4, 10)

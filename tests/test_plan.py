@@ -124,3 +124,23 @@ def test_chain_lengths_and_opt_out(n_convs):
         assert heads[0] == min(n_convs, 8)
     plain = B200PlanEmitter(chain_convs=False).emit_plan(lowering.lower(wl.graph))
     assert all(m == 0 for _, m in _chain_marks(plain))
+
+
+def test_conv_f32_zero_taps_flag():
+    """Out-of-image taps may be staged as zeros only when that cannot change a
+    result: finite weights and no -0.0 bias entry."""
+    def flag(bias=None, w_patch=None):
+        wl = W.conv_f32(batch=1, cin=2, cout=3, h=5, w=5, kernel=3, pad=1)
+        if bias is not None:
+            wl.graph.initializers["bias"] = np.asarray(bias, np.float32)
+        if w_patch is not None:
+            w = wl.graph.initializers["W"].copy()
+            w[0, 0, 0, 0] = w_patch
+            wl.graph.initializers["W"] = w
+        return B200PlanEmitter().emit_plan(lowering.lower(wl.graph)).ops[0].ip[K.CF_ZERO_TAPS_OK]
+
+    assert flag() == 1
+    assert flag(bias=[0.0, 1.0, -2.0]) == 1
+    assert flag(bias=[0.5, -0.0, 1.0]) == 0
+    assert flag(w_patch=np.inf) == 0
+    assert flag(w_patch=np.nan) == 0
