@@ -678,6 +678,49 @@ __global__ void dequantize_linear_kernel(const uint8_t* __restrict__ x, const fl
   }
 }
 
+// Per-tensor scale and zero point, four elements per thread (16-byte float
+// side, 4-byte byte side), the same statements per element.
+__global__ void quantize_linear_x4_kernel(const float4* __restrict__ x, const float* __restrict__ scale,
+                                          const uint8_t* __restrict__ zp, uint32_t* __restrict__ y, int64_t n4,
+                                          int y_signed) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const float lo = y_signed ? -128.0f : 0.0f, hi = y_signed ? 127.0f : 255.0f;
+  const float s = scale[0], z = zp ? (float)load8(zp, 0, y_signed) : 0.0f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldcs(x + i);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float r = __fadd_rn(rintf(__fdiv_rn(f[j], s)), z);
+      r = fminf(fmaxf(r, lo), hi);
+      const uint8_t b = y_signed ? (uint8_t)(int8_t)r : (uint8_t)r;
+      w |= (uint32_t)b << (8 * j);
+    }
+    __stcs(reinterpret_cast<unsigned int*>(y + i), w);
+  }
+}
+
+__global__ void dequantize_linear_x4_kernel(const uint32_t* __restrict__ x, const float* __restrict__ scale,
+                                            const uint8_t* __restrict__ zp, float4* __restrict__ y, int64_t n4,
+                                            int x_signed) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const float s = scale[0], z = zp ? (float)load8(zp, 0, x_signed) : 0.0f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = __ldcs(reinterpret_cast<const unsigned int*>(x + i));
+    float f[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t b = (w >> (8 * j)) & 0xFFu;
+      const float q = x_signed ? (float)(int32_t)(int8_t)b : (float)b;
+      f[j] = __fmul_rn(__fsub_rn(q, z), s);
+    }
+    __stcs(y + i, make_float4(f[0], f[1], f[2], f[3]));
+  }
+}
+
 int launch_quant(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int64_t rows = op.ip[QL_ROWS];
   const int64_t count = rows > 0 && op.ip[IP_BATCHED] && ctx.batch > 0 ? op.ip[QL_COUNT] / rows * ctx.batch
@@ -686,7 +729,21 @@ int launch_quant(const PlanOp& op, void* const* ptrs, const OpState*, const Laun
   const int64_t blocks64 = (count + 255) / 256;
   const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
   const uint8_t* zp = op.t[2] >= 0 ? (const uint8_t*)ptrs[op.t[2]] : nullptr;
+  const void* xp = ptrs[op.t[0]];
+  void* yp = ptrs[op.t[3]];
   cudaError_t e;
+  if (op.ip[QL_AXIS_LEN] <= 1 && count % 4 == 0 && ((uintptr_t)xp & 15) == 0 && ((uintptr_t)yp & 15) == 0) {
+    const int64_t n4 = count / 4, b64 = (n4 + 255) / 256;
+    const int b4 = (int)(b64 < 148 * 16 ? b64 : 148 * 16);
+    if (op.kernel == K_QUANTIZE_LINEAR)
+      e = launch_pdl(quantize_linear_x4_kernel, dim3(b4), dim3(256), 0, ctx.stream, (const float4*)xp,
+                     (const float*)ptrs[op.t[1]], zp, (uint32_t*)yp, n4, (int)op.ip[QL_SIGNED]);
+    else
+      e = launch_pdl(dequantize_linear_x4_kernel, dim3(b4), dim3(256), 0, ctx.stream, (const uint32_t*)xp,
+                     (const float*)ptrs[op.t[1]], zp, (float4*)yp, n4, (int)op.ip[QL_SIGNED]);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
   if (op.kernel == K_QUANTIZE_LINEAR)
     e = launch_pdl(quantize_linear_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const float*)ptrs[op.t[0]],
                    (const float*)ptrs[op.t[1]], zp, (uint8_t*)ptrs[op.t[3]], count, op.ip[QL_AXIS_LEN],

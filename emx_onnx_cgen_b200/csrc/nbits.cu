@@ -543,6 +543,23 @@ __global__ void mul_f16_kernel(const uint16_t* __restrict__ a, const uint16_t* _
     y[i] = mul_f16(a[i], b[i]);
 }
 
+// Eight fp16 values per thread (16-byte loads and stores), same statements.
+__global__ void mul_f16_x8_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b, uint4* __restrict__ y,
+                                  int64_t n8) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 va = __ldcs(a + i), vb = __ldcs(b + i);
+    const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+    uint32_t wy[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      wy[j] = (uint32_t)mul_f16((uint16_t)(wa[j] & 0xFFFFu), (uint16_t)(wb[j] & 0xFFFFu)) |
+              ((uint32_t)mul_f16((uint16_t)(wa[j] >> 16), (uint16_t)(wb[j] >> 16)) << 16);
+    __stcs(y + i, make_uint4(wy[0], wy[1], wy[2], wy[3]));
+  }
+}
+
 static int64_t ew_count(const PlanOp& op, const LaunchCtx& ctx) {
   const int64_t rows = op.ip[EW_ROWS];
   if (rows > 0 && op.ip[IP_BATCHED] && ctx.batch > 0) return op.ip[EW_COUNT] / rows * ctx.batch;
@@ -565,8 +582,17 @@ int launch_mul_f16(const PlanOp& op, void* const* ptrs, const OpState*, const La
   if (count == 0) return 0;
   const int64_t blocks64 = (count + 255) / 256;
   const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
-  cudaError_t e = launch_pdl(mul_f16_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const uint16_t*)ptrs[op.t[0]],
-                             (const uint16_t*)ptrs[op.t[1]], (uint16_t*)ptrs[op.t[2]], count);
+  const void *a = ptrs[op.t[0]], *b = ptrs[op.t[1]];
+  void* y = ptrs[op.t[2]];
+  cudaError_t e;
+  if (count % 8 == 0 && (((uintptr_t)a | (uintptr_t)b | (uintptr_t)y) & 15) == 0) {
+    const int64_t n8 = count / 8, b64 = (n8 + 255) / 256;
+    e = launch_pdl(mul_f16_x8_kernel, dim3((unsigned)(b64 < 148 * 16 ? b64 : 148 * 16)), dim3(256), 0, ctx.stream,
+                   (const uint4*)a, (const uint4*)b, (uint4*)y, n8);
+  } else {
+    e = launch_pdl(mul_f16_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const uint16_t*)a, (const uint16_t*)b,
+                   (uint16_t*)y, count);
+  }
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }

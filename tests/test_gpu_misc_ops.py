@@ -165,6 +165,22 @@ def test_conv_f32_skipped_taps():
     assert_bitexact(out["Y"], ref["Y"], "Y")
 
 
+@pytest.mark.parametrize("out_dtype,zero,scale", [("u8", 128, 0.02), ("i8", -7, 0.05)])
+def test_quant_dequant_per_tensor_x4(out_dtype, zero, scale):
+    """Per-tensor scale, element count a multiple of 4: four values per thread,
+    with ties, out-of-range values, infinities and NaN among them."""
+    require_gpu()
+    wl = W.quant_dequant((64, 100), out_dtype=out_dtype, zero=zero, scale=scale)
+    x = wl.make_inputs(8)
+    flat = x["X"].reshape(-1)
+    flat[:8] = np.array([0.5, 1.5, -2.5, 1e6, -1e6, np.inf, -np.inf, np.nan], np.float32) * np.float32(scale)
+    flat[-3:] = [np.nan, -0.0, 2.5 * scale]
+    ref = oracle.run_graph(wl.graph, x)
+    out = Session(plan_for(wl)).run(x)
+    for k, v in ref.items():
+        assert_bitexact(out[k], v, k)
+
+
 def test_quantize_per_axis_and_specials():
     require_gpu()
     shape = (3, 4, 10)

@@ -110,10 +110,11 @@ def test_swish_all_fp16_values():
     assert_bitexact(out, ref, "swish over all fp16")
 
 
-@pytest.mark.parametrize("alpha", [1.0, 0.5, 1.702])
-def test_swish_mul_vs_port(alpha):
+# (123, 77): the one-value-per-thread Mul; (64, 96): eight fp16 values per thread
+@pytest.mark.parametrize("alpha,shape", [(1.0, (123, 77)), (0.5, (123, 77)), (1.702, (123, 77)), (1.0, (64, 96))])
+def test_swish_mul_vs_port(alpha, shape):
     require_gpu()
-    wl = W.swish_mul_f16((123, 77), alpha)
+    wl = W.swish_mul_f16(shape, alpha)
     x = wl.make_inputs(3)
     x["Z"][0, :5] = [np.inf, -np.inf, np.nan, -0.0, 65504]
     ref = oracle.run_graph(wl.graph, x)
