@@ -112,7 +112,8 @@ enum { SM_OUTER, SM_AXIS, SM_INNER, SM_OUTER_PER_BATCH };
 // ---- K_QUANTIZE_LINEAR / K_DEQUANTIZE_LINEAR: t[0]=X, t[1]=scale f32 [axis_len], t[2]=zero point|-1, t[3]=Y
 enum { QL_COUNT, QL_AXIS_LEN, QL_INNER, QL_SIGNED, QL_ROWS };
 
-// ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), last=y
+// ---- elementwise (K_RELU_F32, K_SWISH_F16, K_MUL_F16): t[0]=x, (t[1]=x2), then y;
+//      K_SWISH_F16 may add t[2] = 65536-entry fp16 table (arena, filled at load: Swish of every fp16 value)
 enum { EW_COUNT, EW_ROWS /*compiled rows along axis 0 (0: not batched)*/ };
 enum { EWF_ALPHA };
 
@@ -183,6 +184,7 @@ void launch_hold(const int* flag, int seq, int* err, cudaStream_t stream);
 int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_nbits(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_swish_f16(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_lstm_f32(const PlanOp&, void* const*, OpState*, int, char*, size_t);

@@ -560,6 +560,52 @@ __global__ void mul_f16_x8_kernel(const uint4* __restrict__ a, const uint4* __re
   }
 }
 
+// Standalone Swish through a table: an fp16 input has 65536 values, so the
+// plan reserves a 128 KB table per Swish op that load time fills with
+// swish_f16_fast of every input (the function the direct kernel evaluates,
+// so the results are the same bits); a run is then a gather.  Persistent
+// blocks copy the table into shared memory once and stream the tensor in
+// 16-byte pieces (eight values per thread).
+constexpr int SW_TABLE = 65536;
+constexpr int SW_THREADS = 1024;
+
+__global__ void swish_table_kernel(uint16_t* __restrict__ table, float alpha) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < SW_TABLE; i += gridDim.x * blockDim.x)
+    table[i] = swish_f16_fast((uint16_t)i, alpha);
+}
+
+__global__ void __launch_bounds__(SW_THREADS) swish_f16_table_kernel(const uint4* __restrict__ x,
+                                                                     uint4* __restrict__ y,
+                                                                     const uint4* __restrict__ table, int64_t n8) {
+  extern __shared__ uint4 s_table[];  // SW_TABLE fp16 values
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < SW_TABLE / 8; i += SW_THREADS) s_table[i] = table[i];  // filled at load time
+  __syncthreads();
+  pdl_wait();
+  const uint16_t* t = reinterpret_cast<const uint16_t*>(s_table);
+  for (int64_t i = blockIdx.x * (int64_t)SW_THREADS + threadIdx.x; i < n8; i += (int64_t)gridDim.x * SW_THREADS) {
+    const uint4 v = __ldcs(x + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = (uint32_t)t[w[j] & 0xFFFFu] | ((uint32_t)t[w[j] >> 16] << 16);
+    __stcs(y + i, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+int prepare_swish_f16(const PlanOp& op, void* const* ptrs, OpState*, int, char* msg, size_t n) {
+  if (op.n_tensors < 3 || op.t[2] < 0) return 0;
+  cudaError_t e = cudaFuncSetAttribute(swish_f16_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SW_TABLE * 2);
+  if (e == cudaSuccess) {
+    swish_table_kernel<<<64, 1024>>>((uint16_t*)ptrs[op.t[2]], (float)op.fp[EWF_ALPHA]);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(msg, n, 4, "Swish table: %s", cudaGetErrorString(e));
+  return 0;
+}
+
 static int64_t ew_count(const PlanOp& op, const LaunchCtx& ctx) {
   const int64_t rows = op.ip[EW_ROWS];
   if (rows > 0 && op.ip[IP_BATCHED] && ctx.batch > 0) return op.ip[EW_COUNT] / rows * ctx.batch;
@@ -569,10 +615,20 @@ static int64_t ew_count(const PlanOp& op, const LaunchCtx& ctx) {
 int launch_swish_f16(const PlanOp& op, void* const* ptrs, const OpState*, const LaunchCtx& ctx, int* launches) {
   const int64_t count = ew_count(op, ctx);
   if (count == 0) return 0;
+  const void* x = ptrs[op.t[0]];
+  void* y = ptrs[op.t[1]];
+  if (op.n_tensors > 2 && op.t[2] >= 0 && count % 8 == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0) {
+    const int64_t n8 = count / 8, b64 = (n8 + SW_THREADS - 1) / SW_THREADS;
+    cudaError_t e = launch_pdl(swish_f16_table_kernel, dim3((unsigned)(b64 < ctx.num_sms ? b64 : ctx.num_sms)),
+                               dim3(SW_THREADS), (size_t)SW_TABLE * 2, ctx.stream, (const uint4*)x, (uint4*)y,
+                               (const uint4*)ptrs[op.t[2]], n8);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
   const int64_t blocks64 = (count + 255) / 256;
   const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
-  cudaError_t e = launch_pdl(swish_f16_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const uint16_t*)ptrs[op.t[0]],
-                             (uint16_t*)ptrs[op.t[1]], count, (float)op.fp[EWF_ALPHA]);
+  cudaError_t e = launch_pdl(swish_f16_kernel, dim3(blocks), dim3(256), 0, ctx.stream, (const uint16_t*)x,
+                             (uint16_t*)y, count, (float)op.fp[EWF_ALPHA]);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }

@@ -892,7 +892,9 @@ class B200PlanEmitter:
             self._b.op(K.K_RELU_F32, [x, y], ip, label=op.output, batched=rows > 0)
         elif fn == "SWISH" and dt == "f16":
             alpha = float(np.float16(float(op.params[0]) if getattr(op, "params", ()) else 1.0))
-            self._b.op(K.K_SWISH_F16, [x, y], ip, {K.EWF_ALPHA: alpha}, label=op.output, batched=rows > 0)
+            # 128 KB table of Swish over every fp16 value, filled once at load time
+            table = self._b.arena_tensor(T_TEMP, "u8", (2 * 65536,), name=f"{op.output}:swish-table")
+            self._b.op(K.K_SWISH_F16, [x, y, table], ip, {K.EWF_ALPHA: alpha}, label=op.output, batched=rows > 0)
         else:
             raise UnsupportedOpError(f"Unary {fn} on {dt} has no B200 kernel")
 
