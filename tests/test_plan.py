@@ -144,3 +144,49 @@ def test_conv_f32_zero_taps_flag():
     assert flag(bias=[0.5, -0.0, 1.0]) == 0
     assert flag(w_patch=np.inf) == 0
     assert flag(w_patch=np.nan) == 0
+
+
+def _weight(plan, tid, dtype):
+    t = plan.tensors[tid]
+    return np.frombuffer(plan.weight_bytes[t.offset:t.offset + t.nbytes], dtype=dtype).reshape(t.shape)
+
+
+@pytest.mark.parametrize("b_dtype", ["i8", "u8"])
+def test_qmatmul_tensor_core_plan_packs_constant_b(b_dtype):
+    """K a multiple of 16 with B an initializer: B^T [N][K] and B's column sums
+    (signed per B's type) are packed into the weights; A's row sums are scratch."""
+    from emx_onnx_cgen_b200.plan import T_TEMP, T_WEIGHT
+    wl = W.qlinear_matmul_u8(m=40, k=96, n=24, b_dtype=b_dtype, b_zero=3)
+    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    op = plan.ops[0]
+    assert "[tensor cores]" in op.label and op.ip[K.QM_B_PACKED] == 1
+    b = wl.graph.initializers["B"]
+    bt = _weight(plan, op.tensors[3], np.uint8)
+    assert plan.tensors[op.tensors[3]].kind == T_WEIGHT and bt.shape == (24, 96)
+    assert np.array_equal(bt, np.ascontiguousarray(b.T).view(np.uint8))
+    assert np.array_equal(_weight(plan, op.tensors[4], np.int32), b.astype(np.int64).sum(axis=0))
+    assert plan.tensors[op.tensors[5]].kind == T_TEMP and plan.tensors[op.tensors[5]].shape == (40,)
+
+
+def test_qmatmul_tensor_core_plan_runtime_b_and_ineligible_k():
+    from emx_onnx_cgen_b200.plan import T_TEMP
+    m, k, n = 8, 64, 16
+    g = GraphSpec("mmi_rt", [TensorSpec("A", "u8", (m, k)), TensorSpec("B", "i8", (k, n))],
+                  [TensorSpec("Y", "i32", (m, n))], [NodeSpec("MatMulInteger", "mmi", ("A", "B"), ("Y",))],
+                  initializers={}, opset_imports=(("", 10),))
+    plan = B200PlanEmitter().emit_plan(lowering.lower(g))
+    op = plan.ops[0]
+    assert op.ip.get(K.QM_B_PACKED, 0) == 0 and len(op.tensors) == 6
+    assert all(plan.tensors[t].kind == T_TEMP for t in plan.ops[0].tensors[3:])
+    # K not a multiple of 16, or the tensor cores switched off: the CUDA-core kernel
+    for wl, kw in ((W.matmul_integer_u8(m=8, k=40, n=16), {}), (W.matmul_integer_u8(m=8, k=64, n=16),
+                                                                 {"use_tensor_cores": False})):
+        op = B200PlanEmitter(**kw).emit_plan(lowering.lower(wl.graph)).ops[0]
+        assert len(op.tensors) == 3 and "[tensor cores]" not in op.label
+
+
+def test_swish_plan_reserves_a_table():
+    wl = W.swish_mul_f16((8, 24))
+    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    (sw,) = [o for o in plan.ops if o.kernel == K.K_SWISH_F16]  # standalone: no MatMulNBits to fuse into
+    assert plan.tensors[sw.tensors[2]].nbytes == 2 * 65536
