@@ -7,7 +7,8 @@
 // all modulo 2^32, so the result equals the reference's int32 sum whenever
 // that sum is defined (no int32 overflow).  K <= 32768 keeps even the raw sum
 // of u8 * u8 products below 2^31, so no accumulator ever wraps.  The output
-// then goes through the CUDA-core kernel's requantisation (qm_requant).
+// then goes through the CUDA-core kernel's requantisation (qm_requant_int or
+// qm_requant_double, the form the plan selected, one per kernel instantiation).
 //
 // B^T (K-major rows [N][K], the layout the MMA reads) and B's column sums are
 // packed by the planner when B is an initializer; otherwise a preparation
@@ -130,6 +131,11 @@ __global__ void __launch_bounds__(256) qgemm_prep_kernel(const QGemmPrepParams p
   }
 }
 
+// MODE: QG_OUT_I32 (MatMulInteger), QG_OUT_REQ_INT / QG_OUT_REQ_DOUBLE (QLinearMatMul's two
+// requantisations), so each instantiation's epilogue carries one form only.
+enum { QG_OUT_I32, QG_OUT_REQ_INT, QG_OUT_REQ_DOUBLE };
+
+template <int MODE>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_tc_kernel(const __grid_constant__ QGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -269,17 +275,20 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_tc_kernel(const __grid_co
           acc[j] = (int32_t)(v[j] + row_corr - (uint32_t)qp.za * cs);
         }
         if (!row_ok) continue;
-        if (qp.quantized) {
+        if (MODE != QG_OUT_I32) {
           uint8_t* yr = reinterpret_cast<uint8_t*>(qp.y) + m * qp.n;
           if (vec) {  // n % 16 == 0: the 16 columns are all in range
             uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w[j >> 2] |= (uint32_t)qm_requant(acc[j], qp) << (8 * (j & 3));
+            for (int j = 0; j < 16; ++j)
+              w[j >> 2] |= (uint32_t)(MODE == QG_OUT_REQ_INT ? qm_requant_int(acc[j], qp) : qm_requant_double(acc[j], qp))
+                           << (8 * (j & 3));
             *reinterpret_cast<uint4*>(yr + nb) = make_uint4(w[0], w[1], w[2], w[3]);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (nb + j < qp.n) yr[nb + j] = qm_requant(acc[j], qp);
+              if (nb + j < qp.n)
+                yr[nb + j] = MODE == QG_OUT_REQ_INT ? qm_requant_int(acc[j], qp) : qm_requant_double(acc[j], qp);
           }
         } else {
           int32_t* yr = reinterpret_cast<int32_t*>(qp.y) + m * qp.n;
@@ -310,8 +319,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_tc_kernel(const __grid_co
 
 // ------------------------------------------------------------------ host side
 int prepare_qgemm_tc() {
-  cudaError_t e = cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QG_SMEM);
-  return e == cudaSuccess ? 0 : 4;
+  for (auto fn : {qgemm_tc_kernel<QG_OUT_I32>, qgemm_tc_kernel<QG_OUT_REQ_INT>, qgemm_tc_kernel<QG_OUT_REQ_DOUBLE>})
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QG_SMEM) != cudaSuccess) return 4;
+  return 0;
 }
 
 // t[3] = B^T scratch [N][K], t[4] = column sums [N] int32, t[5] = row sums [M] int32.
@@ -365,7 +375,10 @@ int launch_qgemm_tc(const PlanOp& op, void* const* ptrs, const LaunchCtx& ctx, c
   p.idesc = make_idesc(2u, (uint32_t)q.a_signed, (uint32_t)q.b_signed, QG_BM, QG_BN);
   const int64_t work = (int64_t)p.m_tiles * p.n_tiles;
   const int grid = (int)(work < ctx.num_sms ? work : ctx.num_sms);
-  e = launch_pdl(qgemm_tc_kernel, dim3(grid), dim3(QG_THREADS), QG_SMEM, ctx.stream, p);
+  void (*fn)(QGemmParams) = !q.quantized ? qgemm_tc_kernel<QG_OUT_I32>
+                            : q.use_int ? qgemm_tc_kernel<QG_OUT_REQ_INT>
+                                        : qgemm_tc_kernel<QG_OUT_REQ_DOUBLE>;
+  e = launch_pdl(fn, dim3(grid), dim3(QG_THREADS), QG_SMEM, ctx.stream, p);
   ++*launches;
   return e == cudaSuccess ? 0 : 4;
 }
