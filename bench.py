@@ -1,29 +1,35 @@
-"""Benchmark: inferences/s of one workload graph through the B200 launch plan.
+"""Benchmark: inferences/s of the five workload graphs through the B200 launch plan.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME | --workloads a,b,...]
 
-One step = one inference = one invocation of the workload graph at its full
-batch (default workload: the int8 ResNet-style stack, X uint8 [32,64,56,56],
-4 x QLinearConv 3x3 64->64 + 2 x QLinearAdd).  Under torchrun every rank runs
-its own independent inferences on its own GPU with a full weight replica
-(weak scaling, no collective on the data path); the reported time is the max
-over ranks.
+One step = one inference = one invocation of a workload graph at its full
+batch.  The printed JSON line is the headline workload (the int8 ResNet-style
+stack, X uint8 [32,64,56,56], 4 x QLinearConv 3x3 64->64 + 2 x QLinearAdd);
+its ``per_workload`` key holds the same measurement for every other workload
+(fp32 MLP, int4 Llama MLP, fp16 causal attention in both modes, fp32 LSTM).
+
+Under torchrun every rank runs its own independent inferences on its own GPU
+with a full weight replica (weak scaling, no collective on the data path);
+the reported time is the max over ranks.  With N > 1 each workload also gets a
+``strong`` entry: ONE inference split along its batch dimension over the N
+GPUs (each rank runs the same graph at batch/N), and a ``copy_ceiling``: the
+same host<->device copies as the e2e step, all ranks at once, no kernels.
 
 * ``value``  -- inputs/outputs resident in HBM, device time per step from CUDA
-  events on the launching stream, L2 flushed (256 MiB write) before every
-  timed step, max over ranks.
+  events on the launching stream, L2 flushed (256 MiB write) between timed
+  steps outside the event windows, max over ranks.
 * ``e2e``    -- the same step through the C-ABI with pinned HOST buffers:
   host->device input copy, the plan, device->host output copy, all inside the
-  timed region.  ``--host-io overlap`` (what ``auto``, the default, picks when
-  a step moves at least 1 MiB): K steps issued back to back
-  with the library's overlapped-runs mode (step k+1's upload and step k-1's
+  timed region.  When a step moves at least 1 MiB, K steps are issued back to
+  back in the library's overlapped-runs mode (step k+1's upload and step k-1's
   download overlap step k's kernels), timed from an event before the first
-  step to an event after the last step's download (emx_b200_join), / K;
-  ``--host-io slices``: each step on its own, its batch cut into slices whose
-  copies overlap its kernels, timed step by step.
+  step to an event after the last download (emx_b200_join), / K; the L2 is
+  flushed once before that window, not inside it.  Smaller steps run one at a
+  time, timed step by step.
 * ``roofline`` -- the dominant kernel's algorithmic work per launch / its mean
-  CUDA-event duration (per-op events inside the library), against the
-  measured peaks.
+  CUDA-event duration (per-op events inside the library, chain members that
+  launch nothing excluded), against the measured peaks.
 * ``cpu_baseline`` -- the reference's own generated C (``oracle/_ref``, gcc
   -O2) on the host cores (one row-slice per core), rank 0 at N=1 only, on a
   bounded sample; ``single_thread`` inside it: the same C on one core.
@@ -48,65 +54,73 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20
+HEADLINE = "qconv_stack_int8"
+ALL_WORKLOADS = ("qconv_stack_int8", "llama_mlp_int4", "mlp_fp32", "attention_fp16", "lstm_fp32")
 
 
 # ----------------------------------------------------------------------------- workloads
-def workload_spec(name: str):
-    """(workload, per-launch algorithmic model of the dominant kernel)."""
+def workload_spec(name: str, shard: int = 1):
+    """(workload, per-launch algorithmic model of the dominant kernel, plan emitter options).
+
+    ``shard`` > 1 builds the same graph at 1/shard of its batch dimension (the
+    slice one rank runs when one inference is split over ``shard`` GPUs)."""
     from emx_onnx_cgen_b200 import workloads as W
     if name == "qconv_stack_int8":
-        wl = W.qconv_stack_int8()
+        wl = W.qconv_stack_int8(batch=32 // shard)
         p = wl.params
         n, c, h, w = p["batch"], p["channels"], p["height"], p["width"]
         ops_per_conv = 2 * n * h * w * c * c * 9
         act = n * c * h * w
-        # per conv launch: activation in + out, residual read for the 2 fused adds, weights
+        # activation in + out per conv, residual read for the 2 fused adds, weights
         bytes_all = 4 * (2 * act + c * c * 9) + 2 * act
-        dom = {"kernel": "qconv_tc", "launches": 4, "ops_total": 4 * ops_per_conv,
-               "bytes_total": bytes_all, "engine": "int8", "unit_ops": "TOP/s", "dtype": "u8/s8 -> s32",
+        dom = {"kernel": "qconv_tc", "ops_total": 4 * ops_per_conv, "bytes_total": bytes_all,
+               "engine": "int8", "unit_ops": "TOP/s", "dtype": "u8/s8 -> s32",
                "ref_tag": "ref_qconv_b1", "ref_rows": 1, "full_rows": n}
-        return wl, dom
+        return wl, dom, {}
     if name == "llama_mlp_int4":
-        wl = W.llama_mlp_int4()
+        wl = W.llama_mlp_int4(m=2048 // shard)
         p = wl.params
         m, h, f, bs = p["m"], p["hidden"], p["inter"], p["block"]
         flops = 3 * 2 * m * h * f  # gate, up, down
         w_bytes = 3 * h * f // 2 + 3 * f * (h // bs) * 2  # int4 weights + fp16 scales
         # A read (by the fused gate/up launch), P written and read back, Y written
         act_bytes = 2 * (m * h + 2 * m * f + m * h)
-        dom = {"kernel": "nbits_gemm", "launches": 2, "ops_total": flops, "bytes_total": w_bytes + act_bytes,
+        dom = {"kernel": "nbits_gemm", "ops_total": flops, "bytes_total": w_bytes + act_bytes,
                "engine": "f16", "unit_ops": "TFLOP/s", "dtype": "f16 x int4 -> f32 acc -> f16",
                "ref_tag": "ref_nbits_m1", "ref_rows": 1, "full_rows": m}
-        return wl, dom
+        return wl, dom, {}
     if name == "mlp_fp32":
-        wl = W.mlp_fp32()
+        wl = W.mlp_fp32(m=64 // shard)
         p = wl.params
         m, k, h = p["m"], p["k"], p["hidden"]
         flops = 2 * m * k * h * 2
         byts = 4 * (2 * k * h + m * k + m * k + k + h)
-        dom = {"kernel": "gemm_f32", "launches": 2, "ops_total": flops, "bytes_total": byts, "engine": "fp32",
+        dom = {"kernel": "gemm_f32", "ops_total": flops, "bytes_total": byts, "engine": "fp32",
                "unit_ops": "TFLOP/s", "dtype": "f32 (reference accumulation order)", "ref_tag": "ref_mlp_m64",
                "ref_rows": 64, "full_rows": m}
-        return wl, dom
-    if name == "attention_fp16":
-        wl = W.attention_fp16()
+        return wl, dom, {}
+    if name in ("attention_fp16", "attention_fp16_tc"):
+        wl = W.attention_fp16(batch=8 // shard)
         p = wl.params
         b, h, t, d = p["batch"], p["heads"], p["seq"], p["head_dim"]
         flops = 2 * (2 * b * h * t * t * d) // 2  # causal: QK^T and PV over the unmasked half
         byts = 4 * b * h * t * d * 2
-        dom = {"kernel": "attention_f16", "launches": 1, "ops_total": flops, "bytes_total": byts, "engine": "f16",
-               "unit_ops": "TFLOP/s", "dtype": "f16 (reference statement rounding)", "ref_tag": "ref_attn_b1h1",
-               "ref_rows": 1, "full_rows": b * h}
-        return wl, dom
+        tc = name.endswith("_tc")
+        dom = {"kernel": "attention_tc" if tc else "attention_f16", "ops_total": flops, "bytes_total": byts,
+               "engine": "f16", "unit_ops": "TFLOP/s",
+               "dtype": ("f16 in, tcgen05 f16 MMAs, f32 accumulation and online softmax" if tc
+                         else "f16 (reference statement rounding)"),
+               "ref_tag": "ref_attn_b1h1", "ref_rows": 1, "full_rows": b * h}
+        return wl, dom, ({"attention_mode": "tensor"} if tc else {})
     if name == "lstm_fp32":
-        wl = W.lstm_fp32()
+        wl = W.lstm_fp32(batch=256 // shard)
         p = wl.params
         t, b, i, h = p["seq"], p["batch"], p["input_size"], p["hidden"]
         flops = 2 * t * b * 4 * h * (i + h)
         byts = 4 * (t * b * i + t * b * h + 4 * h * (i + h) + 2 * b * h)
-        dom = {"kernel": "lstm_f32", "launches": 1, "ops_total": flops, "bytes_total": byts, "engine": "fp32",
+        dom = {"kernel": "lstm_f32", "ops_total": flops, "bytes_total": byts, "engine": "fp32",
                "unit_ops": "TFLOP/s", "dtype": "f32", "ref_tag": "ref_lstm_b1", "ref_rows": 1, "full_rows": b}
-        return wl, dom
+        return wl, dom, {}
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -119,6 +133,18 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def _best_ms(torch, fn, reps: int = 10) -> float:
+    best = 1e30
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best
+
+
 def measure_fp32_peak(torch) -> float:
     """fp32 CUDA-core throughput of cuBLAS SGEMM (TF32 off), best of 10, TFLOP/s."""
     n = 8192
@@ -128,14 +154,7 @@ def measure_fp32_peak(torch) -> float:
     b = torch.randn(n, n, device="cuda")
     for _ in range(2):
         a @ b
-    best = 1e30
-    for _ in range(10):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        a @ b
-        e1.record()
-        torch.cuda.synchronize()
-        best = min(best, e0.elapsed_time(e1))
+    best = _best_ms(torch, lambda: a @ b)
     torch.backends.cuda.matmul.allow_tf32 = prev
     del a, b
     return 2 * n ** 3 / (best * 1e-3) / 1e12
@@ -148,14 +167,7 @@ def measure_int8_peak(torch) -> float:
     b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda").t()
     for _ in range(3):
         torch._int_mm(a, b)
-    best = 1e30
-    for _ in range(10):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        torch._int_mm(a, b)
-        e1.record()
-        torch.cuda.synchronize()
-        best = min(best, e0.elapsed_time(e1))
+    best = _best_ms(torch, lambda: torch._int_mm(a, b))
     del a, b
     return 2 * n ** 3 / (best * 1e-3) / 1e12
 
@@ -217,11 +229,11 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
 
     Returns (list of per-step seconds, rows per step, threads).  One step runs
     ``threads`` independent row-slices in parallel, one per thread; ctypes
-    releases the GIL for the duration of each call."""
+    releases the GIL for the duration of each call.  At least one step runs,
+    however long it takes."""
     from oracle.refc import RefCModel
     from emx_onnx_cgen_b200 import workloads as W
-    import json as _json
-    idx = _json.loads((ROOT / "oracle" / "_ref" / "index.json").read_text())[dom["ref_tag"]]
+    idx = json.loads((ROOT / "oracle" / "_ref" / "index.json").read_text())[dom["ref_tag"]]
     model = RefCModel(dom["ref_tag"])
     wl = W.BUILDERS[idx["builder"]](**idx["kwargs"])
     cores = len(os.sched_getaffinity(0))
@@ -254,8 +266,7 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
     return times, threads * dom["ref_rows"], threads
 
 
-# ----------------------------------------------------------------------------- arms
-def single_thread_baseline(dom: dict, seconds: float = 6.0) -> dict:
+def single_thread_baseline(dom: dict, seconds: float = 5.0) -> dict:
     """The generated C single-threaded on a bounded sample (at least one row-slice)."""
     times, rows, _ = cpu_reference_sample(dom, seconds, threads=1)
     sec = sum(times) / len(times)
@@ -263,100 +274,153 @@ def single_thread_baseline(dom: dict, seconds: float = 6.0) -> dict:
             "sample": f"{len(times)} steps x {rows} of {dom['full_rows']} batch rows, one thread"}
 
 
+def cpu_baseline(dom: dict, seconds: float) -> dict:
+    times, rows, threads = cpu_reference_sample(dom, seconds=seconds)
+    sec = sum(times) / len(times)
+    out = {"value": rows / dom["full_rows"] / sec, "unit": "inferences/s", "cores": threads,
+           "kind": "reference",
+           "sample": f"{len(times)} steps x {rows} of {dom['full_rows']} batch rows, reference generated C "
+                     f"(gcc -std=c99 -O2), one row-slice per thread"}
+    if min(times) * threads <= 4 * seconds:
+        out["single_thread"] = single_thread_baseline(dom, seconds=seconds / 2)
+    else:
+        # one slice alone would outlast the sample budget: report the per-thread rate of
+        # the parallel run (each thread ran one whole slice on its own core)
+        out["single_thread"] = {"value": out["value"] / threads, "unit": "inferences/s", "cores": 1,
+                                "sample": "per-thread rate of the parallel run above (one slice per core)"}
+    return out
+
+
+# ----------------------------------------------------------------------------- arms
 def reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    wl, dom = workload_spec(args.workload)
-    # one step = one row-slice per host thread; the run stops after K steps or
-    # ~150 s of CPU time, whichever comes first (the line reports the steps run)
-    times, rows, threads = cpu_reference_sample(dom, 150.0, steps=args.steps, warmup=min(args.warmup, 1))
-    args.steps = len(times)
-    sec = sum(times) / len(times)
-    value = rows / dom["full_rows"] / sec
-    line = {
-        "impl": "reference", "metric": "inferences/s", "value": value, "unit": "inferences/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"],
-        "data": "synthetic", "config": {"workload": args.workload, **_config(wl)},
-        "cpu_baseline": {"value": value, "unit": "inferences/s", "cores": threads, "kind": "reference",
-                         "sample": f"{rows} of {dom['full_rows']} batch rows per step, reference generated C "
-                                   f"(gcc -std=c99 -O2), one row-slice per thread",
-                         "single_thread": single_thread_baseline(dom)},
-        "e2e": {"value": value, "unit": "inferences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    names = _workload_list(args)
+    lines = {}
+    for name in names:
+        if name.endswith("_tc"):
+            continue  # the reference has one attention; its line is attention_fp16's
+        wl, dom, _ = workload_spec(name)
+        # one step = one row-slice per host thread; the run stops after K steps or the
+        # sample budget, whichever comes first (the line reports the steps run)
+        budget = 60.0 if name == HEADLINE else 20.0
+        times, rows, threads = cpu_reference_sample(dom, budget, steps=args.steps,
+                                                    warmup=min(args.warmup, 1) if name == HEADLINE else 0)
+        sec = sum(times) / len(times)
+        value = rows / dom["full_rows"] / sec
+        lines[name] = {
+            "impl": "reference", "metric": "inferences/s", "value": value, "unit": "inferences/s",
+            "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup, "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"],
+            "data": "synthetic", "config": {"workload": name, **_config(wl)},
+            "cpu_baseline": {"value": value, "unit": "inferences/s", "cores": threads, "kind": "reference",
+                             "sample": f"{rows} of {dom['full_rows']} batch rows per step, reference generated "
+                                       f"C (gcc -std=c99 -O2), one row-slice per thread"},
+            "e2e": {"value": value, "unit": "inferences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+    head = names[0] if names[0] in lines else next(iter(lines))
+    line = dict(lines[head])
+    others = {k: v for k, v in lines.items() if k != head}
+    if others:
+        line["per_workload"] = others
     print(json.dumps(line), flush=True)
 
 
 def _config(wl) -> dict:
     cfg = {k: (list(v) if isinstance(v, tuple) else v) for k, v in wl.params.items()}
     cfg["parallelism"] = "replicas (batch of independent inferences per GPU)"
-    cfg["l2"] = "flushed (256 MiB write) before every timed step"
+    cfg["l2"] = "flushed (256 MiB write) between timed device steps, outside the event windows"
     return cfg
 
 
-def ours_arm(args) -> None:
-    import torch
-    import torch.distributed as dist
-    from emx_onnx_cgen_b200 import lowering
-    from emx_onnx_cgen_b200.plan import B200PlanEmitter
+class Ctx:
+    """Per-process GPU context shared by the workload measurements."""
+
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist, self.args = torch, dist, args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+        # a real (non-legacy) stream: its handle is what the library launches on and
+        # what the timing events are recorded on
+        self.stream = torch.cuda.Stream()
+        torch.cuda.set_stream(self.stream)
+        self.sptr = self.stream.cuda_stream
+        assert self.sptr != 0
+        self.flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+        self.peaks = measured_peaks()
+        self.engine_peaks = {}
+
+    def barrier(self):
+        self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        from emx_onnx_cgen_b200.distributed import max_over_ranks
+        return max_over_ranks(v, device="cuda")
+
+    def engine_peak(self, engine: str):
+        """Measured engine peak (rank 0 measures; every rank gets the value)."""
+        if engine in self.engine_peaks:
+            return self.engine_peaks[engine]
+        torch = self.torch
+        if engine == "int8":
+            v = measure_int8_peak(torch)
+            src = "int8 dense, cuBLASLt torch._int_mm 8192^3 best of 10, measured in this run"
+        elif engine == "fp32":
+            v = measure_fp32_peak(torch)
+            src = "fp32 CUDA cores, cuBLAS SGEMM (TF32 off) 8192^3 best of 10, measured in this run"
+        else:
+            v = self.peaks["bf16_tflops"]
+            src = f"dense bf16 (= fp16 rate) burst, MEASURED_PEAKS.json ({self.peaks['source']})"
+        # every rank measured its own GPU; the roof is the best of them
+        if self.world > 1:
+            v = self.max_over_ranks(v)
+        self.engine_peaks[engine] = (v, src)
+        return v, src
+
+
+def run_workload(ctx: Ctx, name: str, shard: int = 1) -> dict:
+    """Measure one workload on this rank (max over ranks applied); returns its line."""
+    torch, args = ctx.torch, ctx.args
+    from emx_onnx_cgen_b200 import lowering, kernel_ids as K
+    from emx_onnx_cgen_b200.plan import B200PlanEmitter, NP
     from emx_onnx_cgen_b200.runtime import Session
+    from emx_onnx_cgen_b200.distributed import check_same_plan
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    wl, dom, emit_opts = workload_spec(name, shard)
+    plan = B200PlanEmitter(**emit_opts).emit_plan(lowering.lower(wl.graph))
+    if not check_same_plan(plan.plan_bytes, plan.weight_bytes, device="cuda"):
+        raise SystemExit("ranks emitted different plans")
+    sess = Session(plan, device=ctx.local)
+    stream, sptr, flush = ctx.stream, ctx.sptr, ctx.flush
 
-    wl, dom = workload_spec(args.workload)
-    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
-    sess = Session(plan, device=local)
-    if args.io_chunks is not None:
-        sess.set_host_io_chunks(args.io_chunks)
-    # a real (non-legacy) stream: its handle is what the library launches on and
-    # what the timing events are recorded on
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    sptr = stream.cuda_stream
-    assert sptr != 0
-
-    x_np = wl.make_inputs(rank)
+    x_np = wl.make_inputs(ctx.rank)
     host_in = [torch.from_numpy(np.ascontiguousarray(x_np[n])).pin_memory() for n in plan.input_names]
+    del x_np
     dev_in = [t.to("cuda") for t in host_in]
-    from emx_onnx_cgen_b200.plan import NP
     dev_out = [torch.empty(s, dtype=getattr(torch, np.dtype(NP[d]).name), device="cuda")
                for s, d in zip(plan.output_shapes, plan.output_dtypes)]
     host_out = [torch.empty_like(t, device="cpu").pin_memory() for t in dev_out]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     in_d, out_d = [t.data_ptr() for t in dev_in], [t.data_ptr() for t in dev_out]
     in_h, out_h = [t.data_ptr() for t in host_in], [t.data_ptr() for t in host_out]
 
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-
-    def timed_overlap(ins, outs, steps):
-        # K steps back to back; the stream waits for the last download before e1
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            flush.fill_(1)
-            sess.run_ptrs(ins, outs, stream=sptr)
-        sess.join(sptr)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        sess.sync()
-        return e0.elapsed_time(e1) / steps
-
-    def timed(ins, outs, steps):
+    def timed(ins, outs, steps, flush_between=True):
         ev = []
         for _ in range(steps):
-            flush.fill_(1)
+            if flush_between:
+                flush.fill_(1)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             sess.run_ptrs(ins, outs, stream=sptr)
@@ -366,15 +430,20 @@ def ours_arm(args) -> None:
         sess.sync()
         return sum(a.elapsed_time(b) for a, b in ev) / steps
 
-    from emx_onnx_cgen_b200.distributed import check_same_plan, max_over_ranks as _max_over_ranks
+    def timed_overlap(ins, outs, steps):
+        # K steps back to back; the stream waits for the last download before e1
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            sess.run_ptrs(ins, outs, stream=sptr)
+        sess.join(sptr)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sess.sync()
+        return e0.elapsed_time(e1) / steps
 
-    def max_over_ranks(v: float) -> float:
-        return _max_over_ranks(v, device="cuda")
-
-    if not check_same_plan(plan.plan_bytes, plan.weight_bytes, device="cuda"):
-        raise SystemExit("ranks emitted different plans")
-
-    with ClockSampler(local) as clk:
+    with ClockSampler(ctx.local) as clk:
         # warm-up: at least W steps and at least ~1 s of back-to-back work so the
         # SM clock has ramped before the timed region
         t0 = time.perf_counter()
@@ -384,104 +453,168 @@ def ours_arm(args) -> None:
             sess.run_ptrs(in_d, out_d, stream=sptr)
             sess.run_ptrs(in_h, out_h, stream=sptr)
             done += 1
-            if done % 16 == 0:
+            if done % 4 == 0:
                 sess.sync()
         sess.sync()
         launches_before = sess.launch_count()
-        barrier()
+        ctx.barrier()
         ms = timed(in_d, out_d, args.steps)
         launches = sess.launch_count() - launches_before
-    barrier()
-    host_io = args.host_io
-    if host_io == "auto":  # overlapping runs pays when copies are worth hiding (the library's 1 MiB slicing threshold)
-        host_io = "overlap" if h2d + d2h >= (1 << 20) else "slices"
-    if host_io == "overlap":
+    ctx.barrier()
+    overlap = h2d + d2h >= (1 << 20)
+    if overlap:
         sess.set_host_io_overlap(True)
         for _ in range(max(4, args.warmup)):  # both staging sets' graphs
-            flush.fill_(3)
             sess.run_ptrs(in_h, out_h, stream=sptr)
         sess.join(sptr)
         torch.cuda.synchronize()
         sess.sync()
-        barrier()
+        ctx.barrier()
         ms_e2e = timed_overlap(in_h, out_h, args.steps)
         sess.set_host_io_overlap(False)
     else:
-        ms_e2e = timed(in_h, out_h, args.steps)
-    barrier()
-    ms = max_over_ranks(ms)
-    ms_e2e = max_over_ranks(ms_e2e)
+        ms_e2e = timed(in_h, out_h, args.steps, flush_between=False)
+    ctx.barrier()
+    ms_copy = copy_ceiling_ms(ctx, host_in, dev_in, host_out, dev_out, args.steps) if ctx.world > 1 else None
+    ms = ctx.max_over_ranks(ms)
+    ms_e2e = ctx.max_over_ranks(ms_e2e)
+    if ms_copy is not None:
+        ms_copy = ctx.max_over_ranks(ms_copy)
 
     # per-kernel durations from the library's per-op events (outside the timed region)
     sess.set_profiling(True)
-    for _ in range(max(3, args.steps)):
+    for _ in range(max(3, min(args.steps, 20))):
         flush.fill_(2)
         sess.run_ptrs(in_d, out_d, stream=sptr)
         sess.sync()
     op_ms, runs = sess.op_times()
     sess.set_profiling(False)
-    from emx_onnx_cgen_b200 import kernel_ids as K
-    dom_ops = [(t / runs, op) for t, op in zip(op_ms, plan.ops) if K.NAMES[op.kernel] == dom["kernel"]]
-    dom_total_ms = sum(t for t, _ in dom_ops)
-    # chained convolutions run as one launch timed on the chain's first op (members launch nothing)
-    dom_ms = [t for t, op in dom_ops if op.ip.get(K.QC_CHAIN, 0) >= 0 or op.kernel != K.K_QCONV_TC]
-    launch_ms = dom_total_ms / len(dom_ms)
-    peaks = measured_peaks()
-    if dom["engine"] == "int8":
-        eng_peak = measure_int8_peak(torch) if rank == 0 else None
-        eng_src = "int8 dense, cuBLASLt torch._int_mm 8192^3 best of 10, measured in this run"
-    elif dom["engine"] == "fp32":
-        eng_peak = measure_fp32_peak(torch) if rank == 0 else None
-        eng_src = "fp32 CUDA cores, cuBLAS SGEMM (TF32 off) 8192^3 best of 10, measured in this run"
-    else:
-        eng_peak = peaks["bf16_tflops"]
-        eng_src = f"dense bf16 (= fp16 rate) burst, MEASURED_PEAKS.json ({peaks['source']})"
+    # chained convolutions run as one launch timed on the chain's first op; chain
+    # members (QC_CHAIN < 0) launch nothing and their empty event windows are skipped
+    dom_ms = [t / runs for t, op in zip(op_ms, plan.ops)
+              if K.NAMES[op.kernel] == dom["kernel"]
+              and not (op.kernel == K.K_QCONV_TC and op.ip.get(K.QC_CHAIN, 0) < 0)]
+    dom_total_ms = sum(dom_ms)
+    peaks = ctx.peaks
+    eng_peak, eng_src = ctx.engine_peak(dom["engine"])
     achieved_ops = dom["ops_total"] / (dom_total_ms * 1e-3) / 1e12
     achieved_bw = dom["bytes_total"] / (dom_total_ms * 1e-3) / 1e9
-    t_compute = dom["ops_total"] / (eng_peak * 1e12) if eng_peak else 0
+    t_compute = dom["ops_total"] / (eng_peak * 1e12)
     t_mem = dom["bytes_total"] / (peaks["hbm_gbs"] * 1e9)
+    # attainable = min(engine peak, AI x HBM peak); frac = achieved work rate / attainable
+    attainable_ops = min(eng_peak, dom["ops_total"] / dom["bytes_total"] * peaks["hbm_gbs"] * 1e9 / 1e12)
     if t_compute >= t_mem:
-        roof = {"bound": "tensor", "achieved": achieved_ops, "peak": eng_peak, "unit": dom["unit_ops"],
-                "frac": achieved_ops / eng_peak, "peak_source": eng_src}
+        roof = {"bound": "tensor" if dom["engine"] in ("int8", "f16") else "fp32",
+                "achieved": achieved_ops, "peak": eng_peak, "unit": dom["unit_ops"],
+                "frac": achieved_ops / attainable_ops, "peak_source": eng_src + " (of measured)"}
     else:
         roof = {"bound": "hbm", "achieved": achieved_bw, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved_bw / peaks["hbm_gbs"], "peak_source": f"MEASURED_PEAKS.json ({peaks['source']})"}
-    roof.update({"traffic": _ncu_traffic(dom["kernel"], args.workload), "kernel": dom["kernel"],
-                 "launches_per_step": len(dom_ms), "launch_ms": launch_ms,
-                 "ops_per_launch": dom["ops_total"] / len(dom_ms),
-                 "bytes_per_launch": dom["bytes_total"] / len(dom_ms),
+                "frac": achieved_bw / peaks["hbm_gbs"],
+                "peak_source": f"MEASURED_PEAKS.json ({peaks['source']}) (of measured)"}
+    roof.update({"traffic": _ncu_traffic(dom["kernel"], name), "kernel": dom["kernel"],
+                 "launches_per_step": len(dom_ms), "launch_ms": dom_total_ms / max(1, len(dom_ms)),
+                 "ops_per_launch": dom["ops_total"] / max(1, len(dom_ms)),
+                 "bytes_per_launch": dom["bytes_total"] / max(1, len(dom_ms)),
                  "hbm_frac_at_same_time": achieved_bw / peaks["hbm_gbs"],
-                 "tensor_frac_at_same_time": achieved_ops / eng_peak if eng_peak else None})
+                 "engine_frac_at_same_time": achieved_ops / eng_peak})
 
+    per = ctx.world if shard == 1 else 1  # weak: N inferences per step; strong: one split over N
     line = {
-        "metric": "inferences/s", "value": world * 1000.0 / ms, "unit": "inferences/s", "n_gpus": world,
+        "metric": "inferences/s", "value": per * 1000.0 / ms, "unit": "inferences/s", "n_gpus": ctx.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": dom["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, **_config(wl),
-                   "host_io": ("overlapped runs (two staging sets)" if host_io == "overlap"
-                               else f"one run at a time ({args.io_chunks or 4} batch slices when >= 1 MiB moves)")},
-        "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "inferences/s", "h2d_bytes_per_step": h2d,
+        "scaling": "weak" if shard == 1 else "strong", "vs_baseline": None, "dtype": dom["dtype"],
+        "data": "synthetic", "config": {"workload": name, **_config(wl),
+                                        "host_io": ("overlapped runs (two staging sets)" if overlap
+                                                    else "one run at a time")},
+        "e2e": {"value": per * 1000.0 / ms_e2e, "unit": "inferences/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary(),
         "per_op_ms": {f"{i}:{K.NAMES[op.kernel]}": t / runs for i, (t, op) in enumerate(zip(op_ms, plan.ops))},
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            times, rows, threads = cpu_reference_sample(dom, seconds=12.0)
-            sec = sum(times) / len(times)
-            line["cpu_baseline"] = {
-                "value": rows / dom["full_rows"] / sec, "unit": "inferences/s", "cores": threads,
-                "kind": "reference",
-                "sample": f"{len(times)} steps x {rows} of {dom['full_rows']} batch rows, reference generated C "
-                          f"(gcc -std=c99 -O2), one row-slice per thread",
-                "single_thread": single_thread_baseline(dom)}
-        except Exception as exc:  # the GPU number stands without it
-            line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    if shard > 1:
+        line["config"]["parallelism"] = f"one inference split along its batch dimension over {shard} GPUs"
+    if ms_copy is not None:
+        line["copy_ceiling"] = {
+            "value": per * 1000.0 / ms_copy, "unit": "inferences/s", "ms_per_step": ms_copy,
+            "what": "the step's H2D and D2H copies alone (same pinned buffers, two copy streams, all ranks at "
+                    "once, max over ranks)",
+            "e2e_frac": ms_copy / ms_e2e}
     sess.close()
-    if world > 1:
-        dist.destroy_process_group()
+    del dev_in, dev_out, host_in, host_out
+    torch.cuda.empty_cache()
+    line["_dom"] = dom
+    return line
+
+
+def copy_ceiling_ms(ctx: Ctx, host_in, dev_in, host_out, dev_out, steps: int) -> float:
+    """Per-step time of the e2e step's copies alone: uploads on one stream and
+    downloads on another, K steps back to back, every rank at the same time."""
+    torch = ctx.torch
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def copies(k):
+        for _ in range(k):
+            with torch.cuda.stream(up):
+                for h, d in zip(host_in, dev_in):
+                    d.copy_(h, non_blocking=True)
+            with torch.cuda.stream(down):
+                for h, d in zip(host_out, dev_out):
+                    h.copy_(d, non_blocking=True)
+
+    copies(2)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ctx.stream)
+    up.wait_stream(ctx.stream)
+    down.wait_stream(ctx.stream)
+    copies(steps)
+    ctx.stream.wait_stream(up)
+    ctx.stream.wait_stream(down)
+    e1.record(ctx.stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _workload_list(args) -> list[str]:
+    if args.workloads:
+        return [w for w in args.workloads.split(",") if w]
+    if args.workload:
+        return [args.workload]
+    return list(ALL_WORKLOADS)
+
+
+def ours_arm(args) -> None:
+    ctx = Ctx(args)
+    names = _workload_list(args)
+    lines = {}
+    for name in names:
+        lines[name] = run_workload(ctx, name)
+        if ctx.world > 1:
+            strong = run_workload(ctx, name, shard=ctx.world)
+            strong.pop("_dom")
+            lines[name]["strong"] = {k: strong[k] for k in ("value", "unit", "ms_per_step", "scaling", "e2e",
+                                                           "roofline", "gpu_launches", "config")}
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        for name, line in lines.items():
+            if name.endswith("_tc") and name[:-3] in lines and "cpu_baseline" in lines[name[:-3]]:
+                line["cpu_baseline"] = lines[name[:-3]]["cpu_baseline"]
+                continue
+            try:
+                line["cpu_baseline"] = cpu_baseline(line["_dom"], seconds=10.0 if name == HEADLINE else 6.0)
+            except Exception as exc:  # the GPU number stands without it
+                line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+    for line in lines.values():
+        line.pop("_dom", None)
+    if ctx.rank == 0:
+        head = names[0]
+        out = dict(lines[head])
+        others = {k: v for k, v in lines.items() if k != head}
+        if others:
+            out["per_workload"] = others
+        print(json.dumps(out), flush=True)
+    if ctx.world > 1:
+        ctx.dist.destroy_process_group()
 
 
 def _ncu_traffic(kernel: str, workload: str):
@@ -501,16 +634,12 @@ def _ncu_traffic(kernel: str, workload: str):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="qconv_stack_int8")
+    ap.add_argument("--workload", default=None, help="measure one workload only")
+    ap.add_argument("--workloads", default=None, help="comma-separated list; the first is the headline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--host-io", choices=["auto", "overlap", "slices"], default="auto",
-                    help="e2e host copies: overlap consecutive steps, or one step at a time (its batch sliced); "
-                         "auto: overlap when a step moves >= 1 MiB")
-    ap.add_argument("--io-chunks", type=int, default=None,
-                    help="batch slices for the e2e run's pipelined host copies (library default 4; 1 = off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -130,6 +130,13 @@ struct LaunchCtx {
   const OpState* states = nullptr;
   size_t n_ops = 0;
   size_t index = 0;
+  int fault = 0;  // test hooks in effect (FAULT_* bits, emx_b200_set_fault)
+};
+
+// Failure-detection test hooks (emx_b200_set_fault): each makes a bounded
+// device wait run out; none faults, traps or hangs the GPU.
+enum FaultHook : int {
+  FAULT_DROP_CHAIN_PROGRESS = 1,  // chained convolutions never publish their progress words
 };
 
 // Last integer slot of every op: 1 when the op's leading (batch) extent

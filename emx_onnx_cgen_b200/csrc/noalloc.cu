@@ -29,10 +29,15 @@
 //
 // The kernels are the plan path's own (layout kernel + qconv_tc); only the
 // buffers differ, so results are bit-identical to emx_b200_run on a plan of
-// the same QLinearConv.  The call only enqueues work: it returns launch
-// errors; a device-side wait that gives up (the kernels' bounded waits) is
-// recorded in a word inside the scratch, which the next call clears, and is
-// not reported by this entry point.
+// the same QLinearConv.  The call only enqueues work: it returns argument and
+// launch errors only.  Every device-side error -- a bounded wait that gives
+// up, or a kernel finding an inconsistent configuration -- is recorded in a
+// word inside the scratch, which the next call clears; none of them is
+// reported by this entry point, and the output of such a call is undefined.
+//
+// Cost to every user: the static array (8 MiB + 256 B) is reserved on each
+// device whose context loads this library's module, whether or not this
+// entry point is ever called (plan-only users included).
 #include <mutex>
 
 #include "emx_b200.h"
@@ -138,14 +143,19 @@ extern "C" int emx_b200_qlinear_conv3x3_noalloc(const uint8_t* x, const int8_t* 
   float* epi = reinterpret_cast<float*>(scratch + act_bytes + img_bytes);
   int* d_err = reinterpret_cast<int*>(scratch + kNoAllocScratchBytes);
 
+  // The weight image and epilogue table first: the conv kernel reads them
+  // before its programmatic-dependency wait (they are load-time constants on
+  // the plan path), so they must be complete before the layout kernel starts.
+  // The memsets below are not kernels and end any programmatic overlap, so the
+  // stream fully orders this kernel before the layout and conv kernels.
+  noalloc_conv_prep_kernel<<<64, 256, 0, stream>>>(w, w_scale, bias, img, epi, oc, c, x_scale, y_scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return report(EMX_ERR_CUDA, "noalloc conv: weight image: %s", cudaGetErrorString(e));
   // the border and tail rows of the planar copy must read as zero; the
   // device error word starts clear on every call
   e = cudaMemsetAsync(act, 0, (size_t)rows * c, stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, sizeof(int), stream);
   if (e != cudaSuccess) return report(EMX_ERR_CUDA, "noalloc conv: clearing scratch: %s", cudaGetErrorString(e));
-  noalloc_conv_prep_kernel<<<64, 256, 0, stream>>>(w, w_scale, bias, img, epi, oc, c, x_scale, y_scale);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return report(EMX_ERR_CUDA, "noalloc conv: weight image: %s", cudaGetErrorString(e));
 
   // the plan path's two ops, pointed at the scratch
   void* ptrs[5] = {const_cast<uint8_t*>(x), act, img, epi, y};

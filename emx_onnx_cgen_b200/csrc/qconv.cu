@@ -106,6 +106,9 @@ struct QConvChainParams {
   int rlo, rhi;  // tile t's residual rows were written by tiles t-rlo .. t+rhi
   unsigned long long* state;  // [0] run epoch, [1] CTAs finished, [2 + t] progress of tile t; null for L = 1
   int* err;
+  // failure-detection test hook (emx_b200_set_fault): the publisher never
+  // advances the progress words, so the next layer's bounded waits run out
+  int drop_progress;
 };
 
 // bytes of a clamped integer-valued float (see float_to_byte): gather the low
@@ -187,6 +190,7 @@ __device__ __forceinline__ void qc_publish(const QConvChainParams& cp, const uin
   const uint32_t total = (uint32_t)(per_layer * (L - 1));
   uint32_t published = 0;
   uint64_t t_last = globaltimer_ns();
+  const uint64_t budget = wait_budget_ns(err);
   uint32_t spins = 0;
   while (published < total) {
     uint32_t done = total;
@@ -196,7 +200,7 @@ __device__ __forceinline__ void qc_publish(const QConvChainParams& cp, const uin
       for (uint32_t k = published; k < done; ++k) {
         const int l = (int)(k / (uint32_t)per_layer);
         const int tile = t_first + (int)(k % (uint32_t)per_layer) * t_step;
-        st_relaxed_u64(progress + tile, epoch * 64ull + (unsigned)(l + 1));
+        if (!cp.drop_progress) st_relaxed_u64(progress + tile, epoch * 64ull + (unsigned)(l + 1));
       }
       published = done;
       t_last = globaltimer_ns();
@@ -204,7 +208,7 @@ __device__ __forceinline__ void qc_publish(const QConvChainParams& cp, const uin
     }
     if ((++spins & 15u) == 0) {
       if (error_raised(err)) break;
-      if (globaltimer_ns() - t_last > EMX_WAIT_BUDGET_NS) {
+      if (globaltimer_ns() - t_last > budget) {
         record_error(err, DEV_TIMEOUT_EPILOGUE);
         break;
       }
@@ -899,6 +903,16 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
   cudaError_t e = cudaFuncSetAttribute(kQcVariants[st->variant].fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)QC_SMEM_MAX);
   if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  // A chain's CTAs wait on each other's progress words, so its grid (at most
+  // one CTA per SM) must be resident all at once: refuse at load time, rather
+  // than time out at run time, where this device cannot hold one CTA per SM.
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kQcVariants[st->variant].fn,
+                                                    qc_threads(kQcVariants[st->variant].oc), QC_SMEM_MAX);
+  if (e != cudaSuccess) return fail(msg, n, 4, "occupancy query: %s", cudaGetErrorString(e));
+  if (per_sm < 1)
+    return fail(msg, n, 5, "QLinearConv tensor-core path: no CTA of %d threads and %zu B shared memory fits an SM",
+                qc_threads(kQcVariants[st->variant].oc), QC_SMEM_MAX);
   st->fast_div = 0;
   if (op.ip[QC_HAS_ADD]) {
     QConvTcParams p{};
@@ -1003,6 +1017,7 @@ static bool build_chain(const PlanOp& op, void* const* ptrs, const LaunchCtx& ct
   cp.rhi = 0;
   cp.state = (unsigned long long*)ptrs[op.t[6]];
   cp.err = ctx.d_error;
+  cp.drop_progress = (ctx.fault & FAULT_DROP_CHAIN_PROGRESS) ? 1 : 0;
   return true;
 }
 

@@ -108,6 +108,7 @@ struct emx_plan {
   };
   bool use_graphs = true;
   std::vector<GraphEntry> graphs;
+  int fault = 0;  // failure-detection test hooks (emx_b200_set_fault)
   uint64_t graph_clock = 0;
   // host-mapped release flag for the profiling hold kernel
   int* h_hold = nullptr;
@@ -274,6 +275,7 @@ void destroy(emx_plan* p) {
 // events measure kernels rather than host launch gaps.
 int launch_ops(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches) {
   emx::LaunchCtx ctx{stream, p->d_error, run_batch, p->num_sms};
+  ctx.fault = p->fault;
   ctx.ops = p->ops.data();
   ctx.states = p->states.data();
   ctx.n_ops = p->ops.size();
@@ -781,6 +783,30 @@ int64_t emx_b200_launch_count(const emx_plan_t* p) { return p ? p->launches_tota
 int emx_b200_set_graphs(emx_plan_t* p, int enable) {
   if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
   p->use_graphs = enable != 0;
+  return EMX_OK;
+}
+
+int emx_b200_set_wait_budget(emx_plan_t* p, uint64_t ns) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  // the word 8 bytes after the error word (tc100.cuh wait_budget_ns); ordered
+  // after every run already enqueued on the plan's streams
+  CUDA_TRY(cudaDeviceSynchronize(), "device synchronize");
+  const unsigned long long v = ns;
+  CUDA_TRY(cudaMemcpy(reinterpret_cast<char*>(p->d_error) + 8, &v, sizeof(v), cudaMemcpyHostToDevice),
+           "wait budget");
+  return EMX_OK;
+}
+
+int emx_b200_set_fault(emx_plan_t* p, int hooks) {
+  if (!p) return set_error(EMX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (hooks & ~emx::FAULT_DROP_CHAIN_PROGRESS) return set_error(EMX_ERR_INVALID_ARGUMENT, "unknown hook bits %d", hooks);
+  if (hooks == p->fault) return EMX_OK;
+  CUDA_TRY(cudaSetDevice(p->device), "cudaSetDevice");
+  CUDA_TRY(cudaDeviceSynchronize(), "device synchronize");
+  for (auto& g : p->graphs) cudaGraphExecDestroy(g.exec);  // captured with the previous hooks
+  p->graphs.clear();
+  p->fault = hooks;
   return EMX_OK;
 }
 

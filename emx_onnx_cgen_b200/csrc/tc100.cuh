@@ -20,7 +20,9 @@ enum DeviceError : int {
   DEV_BAD_CONFIG = 5,
 };
 
-// Bounded waits: give up after this many nanoseconds of %globaltimer.
+// Bounded waits: give up after this many nanoseconds of %globaltimer.  The
+// default; a plan can set its own (emx_b200_set_wait_budget), stored in the
+// 64-bit word 8 bytes after its device error word.
 #ifndef EMX_WAIT_BUDGET_NS
 #define EMX_WAIT_BUDGET_NS 2000000000ull
 #endif
@@ -43,6 +45,14 @@ __device__ __forceinline__ void record_error(int* err, int code) {
 
 __device__ __forceinline__ bool error_raised(const int* err) {
   return err && *reinterpret_cast<const volatile int*>(err) != 0;
+}
+
+// Wait budget of the plan owning `err` (read when a wait starts spinning, not
+// on the fast path): the word 8 bytes after the error word, 0 = the default.
+__device__ __forceinline__ uint64_t wait_budget_ns(const int* err) {
+  if (!err) return EMX_WAIT_BUDGET_NS;
+  const uint64_t v = *reinterpret_cast<const volatile unsigned long long*>(err + 2);
+  return v ? v : EMX_WAIT_BUDGET_NS;
 }
 
 // ----------------------------------------------------------------- mbarrier
@@ -85,12 +95,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t budget = wait_budget_ns(err);
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (error_raised(err)) return false;
-      if (globaltimer_ns() - t0 > EMX_WAIT_BUDGET_NS) {
+      if (globaltimer_ns() - t0 > budget) {
         record_error(err, code);
         return false;
       }
@@ -146,11 +157,12 @@ __device__ __forceinline__ bool wait_flags_at_least(const unsigned long long* fl
     for (int j = 0; j < 8; ++j) {
       if (v[j] >= target) continue;
       const uint64_t t0 = globaltimer_ns();
+      const uint64_t budget = wait_budget_ns(err);
       uint32_t spins = 0;
       while (ld_acquire_u64(flags + base + j) < target) {
         if ((++spins & 15u) == 0) {
           if (error_raised(err)) return false;
-          if (globaltimer_ns() - t0 > EMX_WAIT_BUDGET_NS) {
+          if (globaltimer_ns() - t0 > budget) {
             record_error(err, code);
             return false;
           }

@@ -1,7 +1,7 @@
 """ctypes binding of libemx_b200.so (include/emx_b200.h) and a per-device Session.
 
 This is the "thin ctypes C-ABI" the Python driver uses; it is also the model
-for a binding in any other host language (see INTEGRATION.md).  The library
+for a binding in any other host language.  The library
 must have been built (``python -m emx_onnx_cgen_b200.build``); there is no
 fallback: a missing library raises ``RuntimeError`` at first use.
 """
@@ -25,7 +25,10 @@ STATUS_NAMES = {0: "EMX_OK", 1: "EMX_ERR_INVALID_ARGUMENT", 2: "EMX_ERR_PLAN_FOR
 EXPORTED = ("emx_b200_version", "emx_b200_last_error", "emx_b200_plan_load", "emx_b200_plan_load_mem",
             "emx_b200_run", "emx_b200_sync", "emx_b200_plan_free", "emx_b200_plan_info",
             "emx_b200_launch_count", "emx_b200_set_profiling", "emx_b200_op_times", "emx_b200_set_graphs",
-            "emx_b200_set_host_io_chunks", "emx_b200_set_host_io_overlap", "emx_b200_join")
+            "emx_b200_set_host_io_chunks", "emx_b200_set_host_io_overlap", "emx_b200_join",
+            "emx_b200_set_wait_budget", "emx_b200_set_fault")
+
+FAULT_DROP_CHAIN_PROGRESS = 1
 
 
 class EmxError(RuntimeError):
@@ -74,6 +77,10 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.emx_b200_set_host_io_overlap.restype = i32
         lib.emx_b200_join.argtypes = [vp, vp]
         lib.emx_b200_join.restype = i32
+        lib.emx_b200_set_wait_budget.argtypes = [vp, ctypes.c_uint64]
+        lib.emx_b200_set_wait_budget.restype = i32
+        lib.emx_b200_set_fault.argtypes = [vp, i32]
+        lib.emx_b200_set_fault.restype = i32
         lib.emx_b200_op_times.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
                                           ctypes.POINTER(i64)]
         for name in ("emx_b200_plan_load", "emx_b200_plan_load_mem", "emx_b200_run", "emx_b200_sync",
@@ -157,6 +164,14 @@ class Session:
     def set_host_io_chunks(self, chunks: int) -> None:
         """Batch slices for pipelined page-locked host I/O (1 = off)."""
         _check(self.lib.emx_b200_set_host_io_chunks(self.handle, int(chunks)))
+
+    def set_wait_budget(self, ns: int) -> None:
+        """Budget of every bounded device-side wait, in ns (0 = the 2 s default)."""
+        _check(self.lib.emx_b200_set_wait_budget(self.handle, int(ns)))
+
+    def set_fault(self, hooks: int) -> None:
+        """Failure-detection test hooks (FAULT_* bits; 0 = none)."""
+        _check(self.lib.emx_b200_set_fault(self.handle, int(hooks)))
 
     def set_profiling(self, enable: bool) -> None:
         _check(self.lib.emx_b200_set_profiling(self.handle, 1 if enable else 0))

@@ -151,6 +151,24 @@ int emx_b200_set_host_io_overlap(emx_plan_t *plan, int enable);
  * the plan's overlapped runs issued so far is complete. */
 int emx_b200_join(emx_plan_t *plan, void *stream);
 
+/* Budget of every bounded device-side wait of this plan's kernels, in
+ * nanoseconds of the GPU's global timer (0: the default, 2 s).  A wait that
+ * runs out records a code in the plan's device error word, the kernels
+ * return, and emx_b200_sync reports EMX_ERR_DEVICE_TIMEOUT; the context
+ * stays usable.  Waits on the device for the plan's previous runs first.
+ * No counterpart in the reference (its generated C has no device waits). */
+int emx_b200_set_wait_budget(emx_plan_t *plan, uint64_t ns);
+
+/* Failure-detection test hooks (bit set; 0 = none, the default).
+ * EMX_FAULT_DROP_CHAIN_PROGRESS: chained convolutions never publish their
+ * per-tile progress words, so the next layer's bounded waits run out and the
+ * run ends with EMX_ERR_DEVICE_TIMEOUT -- a flag that nothing sets; nothing
+ * faults, traps or hangs.  Changing the hooks drops the plan's captured
+ * graphs.  No counterpart in the reference (its failure paths are host-side:
+ * a NULL malloc, c_emitter.py:2785-2788). */
+#define EMX_FAULT_DROP_CHAIN_PROGRESS 1
+int emx_b200_set_fault(emx_plan_t *plan, int hooks);
+
 /* Allocation-free standalone QLinearConv, 3x3 kernel, stride 1, pads 1,
  * group 1, no dilation: uint8 NCHW x [n][c][h][w] with x_zero_point 0 or 128,
  * int8 OIHW weights [oc][c][3][3] with per-output-channel fp32 scales
@@ -168,8 +186,13 @@ int emx_b200_join(emx_plan_t *plan, void *stream);
  * more (EMX_ERR_INVALID_ARGUMENT, e.g. a 32 x 64 x 56 x 56 batch fits).
  * The first call on a device sets up the scratch address (with that device
  * current) and must come before any stream capture begins.  Calls that can
- * overlap in time share the scratch and race: serialise them.  Only launch
- * errors are returned; device-side wait timeouts are not reported here. */
+ * overlap in time share the scratch and race: serialise them.  Only argument
+ * and launch errors are returned; no device-side error (a bounded wait that
+ * gives up, an inconsistent configuration found by a kernel) is reported by
+ * this entry point, and the output of such a call is undefined.
+ * Loading the library reserves the 8 MiB + 256 B static array on every device
+ * whose context loads the library's module, whether or not this entry point
+ * is ever called. */
 int emx_b200_qlinear_conv3x3_noalloc(const uint8_t *x, const int8_t *w, const float *w_scale,
                                      const int32_t *bias, float x_scale, int x_zero_point,
                                      float y_scale, int y_zero_point, int n, int c, int h, int w_,

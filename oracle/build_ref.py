@@ -1,8 +1,9 @@
 """TEST INFRASTRUCTURE ONLY: recipe that builds ``oracle/_ref/`` -- the
 reference's own generated C for the CPU-baseline slices of each workload.
 
-For every target the reference compiler (read from its source tree,
-``EMX_REFERENCE_SRC``, default ``/root/reference/src``, via the onnx shim)
+For every target the reference compiler (read from its source tree, the
+directory ``EMX_REFERENCE_SRC`` names, else ``reference/src`` beside this
+repository, via the onnx shim)
 lowers the workload graph at a slice size and emits C, which is compiled with
 ``gcc -std=c99 -O2 -fPIC -shared``.  The slice keeps the full per-row problem
 and shrinks only the independent batch/row dimension, along which the

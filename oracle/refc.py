@@ -1,7 +1,8 @@
 """TEST INFRASTRUCTURE ONLY: the reference's own generated C as the parity oracle.
 
-This module drives the reference compiler (mounted read-only; location from
-``EMX_REFERENCE_SRC``, default ``/root/reference/src``) to lower a
+This module drives the reference compiler (its ``src`` directory, read-only:
+the directory the ``EMX_REFERENCE_SRC`` environment variable names, else a
+``reference/src`` checkout beside this repository's) to lower a
 ``GraphSpec`` and emit its C translation unit, exactly the way the
 reference's CLI does between ``Compiler._lower_model`` (``compiler.py:514``)
 and ``CEmitter.emit_model`` / ``collect_weight_data``
@@ -29,7 +30,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / "_ref"
-REFERENCE_SRC = Path(os.environ.get("EMX_REFERENCE_SRC", "/root/reference/src"))
+_SRC_ENV = os.environ.get("EMX_REFERENCE_SRC", "")
+REFERENCE_SRC = Path(_SRC_ENV) if _SRC_ENV else HERE.parent.parent / "reference" / "src"
 
 sys.path.insert(0, str(HERE.parent))
 from emx_onnx_cgen_b200.spec import GraphSpec, NP_DTYPE  # noqa: E402
@@ -38,6 +40,7 @@ CFLAGS = ["-std=c99", "-O2", "-fPIC", "-shared", "-w"]
 
 
 def reference_available() -> bool:
+    """True when the reference's ``src`` directory is present."""
     return (REFERENCE_SRC / "emx_onnx_cgen" / "compiler.py").is_file()
 
 

@@ -9,8 +9,8 @@ records the builder arguments.  The fixtures pin both the oracle restatement
 (``oracle/oracle.c``) and the CUDA kernels without needing the reference at
 test time.
 
-Run from the repository root (needs the reference source tree, default
-``/root/reference/src``, override with ``EMX_REFERENCE_SRC``)::
+Run from the repository root with the reference's ``src`` directory in
+``EMX_REFERENCE_SRC`` (default: ``reference/src`` beside this repository)::
 
     python tests/golden/make_golden.py [case ...]   # all cases, or only the named ones
 """
