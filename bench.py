@@ -237,7 +237,10 @@ def cpu_reference_sample(dom: dict, seconds: float, steps: int | None = None, wa
     model = RefCModel(dom["ref_tag"])
     wl = W.BUILDERS[idx["builder"]](**idx["kwargs"])
     cores = len(os.sched_getaffinity(0))
-    threads = max(1, min(threads or cores, dom["full_rows"] // dom["ref_rows"]))
+    # one slice per thread; a slice that is a whole inference (the MLP) runs once per thread
+    threads = max(1, threads or cores)
+    if dom["ref_rows"] < dom["full_rows"]:
+        threads = min(threads, dom["full_rows"] // dom["ref_rows"])
     per_thread = [wl.make_inputs(s) for s in range(threads)]
     outs = [None] * threads
 
