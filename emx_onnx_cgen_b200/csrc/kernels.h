@@ -29,6 +29,7 @@ enum KernelId : uint32_t {
   K_SOFTMAX_F32 = 16,
   K_QUANTIZE_LINEAR = 17,
   K_DEQUANTIZE_LINEAR = 18,
+  K_ATTENTION_TC = 19,  // opset-23 Attention, fast mode: tcgen05 kind::f16, fp32 online softmax (attention_tc.cu)
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -46,7 +47,9 @@ enum {
   QC_Y_LAYOUT /*0 planar, 1 NCHW*/, QC_Y_XOR, QC_Y_HP, QC_Y_WP, QC_Y_PT, QC_Y_PL, QC_Y_SIGNED,
   QC_HAS_ADD, QC_C_ZERO /*conv-side zero in the add*/, QC_R_ZERO, QC_R_XOR, QC_R_SIGNED, QC_R_HP, QC_R_WP,
   QC_R_PT, QC_R_PL, QC_ADD_ZERO /*add output zero*/, QC_ADD_SIGNED, QC_X_ROWS, QC_Y_ROWS, QC_R_ROWS,
-  QC_CHAIN /*first op of a chain: its length L (t[6] = chain state); later members: -1; else 0*/
+  QC_CHAIN /*first op of a chain: its length L (t[6] = chain state); later members: -1; else 0*/,
+  QC_RQ_INT /*1: |(float)acc * scale| < 2^21 for every accumulator the weights allow (planner-proved), so
+               rint + zero point + clamp run as one integer saturating pack, exactly*/
 };
 enum { QCF_C_SCALE, QCF_R_SCALE, QCF_ADD_SCALE };
 
@@ -74,7 +77,8 @@ enum {
 };
 enum { NBF_ALPHA };
 
-// ---- K_ATTENTION_F16: t[0]=Q, t[1]=K, t[2]=V, t[3]=Y (fp16), t[4]=scratch (4 words);
+// ---- K_ATTENTION_F16 and K_ATTENTION_TC (same slots; the latter needs head sizes of 128 and
+//      ignores t[4]): t[0]=Q, t[1]=K, t[2]=V, t[3]=Y (fp16), t[4]=scratch (4 words);
 //      element (b, h, t, d) of a tensor sits at b*SB + h*SH + t*ST + d (3-D or 4-D layouts)
 enum {
   AT_B, AT_HQ, AT_GROUP, AT_TQ, AT_TK, AT_PAST, AT_D, AT_DV, AT_CAUSAL,
@@ -206,5 +210,7 @@ int launch_softmax_f32(const PlanOp&, void* const*, const OpState*, const Launch
 int launch_quant(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_attention(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_attention(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_attention_tc(const PlanOp&, void* const*, OpState*, int, char*, size_t);
+int launch_attention_tc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 
 }  // namespace emx

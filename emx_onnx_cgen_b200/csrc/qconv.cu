@@ -77,6 +77,8 @@ struct QConvTcParams {
   int64_t r_off;
   // fused add by table: out byte = lut[(conv byte << 8) | residual byte], staged in shared memory
   const uint8_t* lut;
+  int rq_int;  // integer requantisation (QC_RQ_INT)
+  int rq_sub;  // bits(1.5 * 2^23) - output zero point
 };
 
 constexpr int QC_RSTAGES = 3;  // residual ring depth (tiles)
@@ -89,7 +91,7 @@ constexpr int QC_RSTAGES = 3;  // residual ring depth (tiles)
 // the 512 TMEM columns (OC <= 64), else 2.
 constexpr int QC_MMA_WARPS = 4;  // most issuers of any variant
 constexpr int QC_EPI_WARPS = 16;
-__host__ __device__ constexpr int qc_partials(int oc) { return 2 * QC_MMA_WARPS * oc <= 512 ? QC_MMA_WARPS : 256 / oc; }
+__host__ __device__ constexpr int qc_partials(int oc) { return oc <= 64 ? 2 : 256 / oc; }
 __host__ __device__ constexpr int qc_epi_warp0(int oc) { return (qc_partials(oc) + 2 + 3) & ~3; }
 __host__ __device__ constexpr int qc_threads(int oc) { return 32 * (qc_epi_warp0(oc) + QC_EPI_WARPS); }
 constexpr int QC_TILE_M = 128;
@@ -245,8 +247,12 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
   const int L = cp.n_layers;
   const bool chained = cp.state != nullptr;
   int* const err = cp.err;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Shared-memory regions are carved out by adding byte offsets to the
+  // extern __shared__ array (never through integer casts), so the compiler
+  // keeps them in the shared state space: LDS/STS with 32-bit addresses
+  // instead of generic loads and stores.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   // weights: one buffer, or two for a chain (layer l uses buffer l & 1, so
   // layer l+1's weights load while layer l's MMAs run)
   const int wbufs = L > 1 ? 2 : 1;
@@ -278,8 +284,7 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
   // per MMA k of a tile: byte offsets of its A (window) and B (weights) operands
   uint32_t* s_koff = s_stored + QC_EPI_WARPS;  // [2 * MMAs per tile]
   // residual ring after that (128-byte aligned)
-  uint8_t* s_r = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(s_koff + 2 * g.kh * g.kw * KSTEPS) + 127) & ~uintptr_t(127));
+  uint8_t* s_r = smem + ((uint32_t)(reinterpret_cast<uint8_t*>(s_koff + 2 * g.kh * g.kw * KSTEPS) - smem) + 127u & ~127u);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -537,7 +542,10 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
     const int quarter = warp & 3;
     const int col0 = (ew >> 2) * G;
     const int row = quarter * 32 + lane;
-    const int64_t hpwp = (int64_t)g.hp * g.wp;
+    // geometry shared by every layer, in registers
+    const uint32_t hpwp = (uint32_t)g.hp * (uint32_t)g.wp;
+    const uint64_t hpwp_mul = g.hpwp_mul, wp_mul = g.wp_mul;
+    const int gwp = g.wp, gbatch = g.batch, goh = g.oh, gow = g.ow;
     auto fetch_consts = [&](int l) {  // this warp's slice of layer l's scales and biases, parity l & 1
       if (lane < G) {
         cp_async4(s_scale + ((l & 1) * QC_EPI_WARPS + ew) * G + lane, cp.layer[l].scale + col0 + lane);
@@ -548,12 +556,32 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
     fetch_consts(0);  // plan constants: not written by the preceding kernel
     if (L > 1) fetch_consts(1);
     pdl_wait();  // residual reads and output writes follow the preceding kernel
-    const unsigned long long epoch = chained ? ld_acquire_u64(cp.state) : 0ull;
     int it = 0, rit = 0, luts = 0;
     uint32_t pub = 0;
     bool ok = true;
+    bool pend = false;  // a stored tile not yet published
     for (int l = 0; l < L && ok; ++l) {
+      // Layer constants, read once per layer: the layer table is indexed at run
+      // time, so each field read is a memory load that must stay out of the tile loop.
       const QConvTcParams& lp = cp.layer[l];
+      uint8_t* const ybase = lp.y;
+      const int y_layout = lp.y_layout;
+      const uint32_t yx4 = (uint32_t)lp.y_xor * 0x01010101u;
+      const int y_hp = lp.y_hp, y_wp = lp.y_wp, y_pt = lp.y_pt, y_pl = lp.y_pl;
+      const int64_t yplane = (int64_t)lp.oh * lp.ow;
+      const float ymz = lp.y_m_minus_zero, ylo = lp.y_lo, yhi = lp.y_hi;
+      const bool y_signed = lp.y_lo < 0.0f;
+      const int has_add = lp.has_add;
+      const bool use_lut = lp.lut != nullptr;
+      // integer requantisation (rint + zero point + clamp as one saturating pack)
+      // where the planner proved it exact; the float fused add needs float values.
+      // Signed outputs saturate y + 128 to [0, 255] and flip the top bit back.
+      const bool int_rq = lp.rq_int && (!has_add || use_lut);
+      const int rq_sub = lp.rq_sub - (y_signed ? 128 : 0);
+      const uint32_t sx4 = y_signed ? 0x80808080u : 0u;
+      const int64_t r_off = lp.r_off;
+      const uint32_t rx4 = (uint32_t)lp.r_xor * 0x01010101u;
+      const bool rb_on = has_add && lp.r_bulk;
       // this warp's scales and biases of layer l (its own slice: no cross-warp
       // barrier), fetched asynchronously one layer ahead
       float* sc = s_scale + ((l & 1) * QC_EPI_WARPS + ew) * G;
@@ -565,13 +593,11 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
       else
         cp_async_wait_group<0>();
       __syncwarp();
-      const uint32_t yx4 = (uint32_t)lp.y_xor * 0x01010101u;
-      if (lp.lut) {
+      if (use_lut) {
         ok = __all_sync(0xffffffffu, mbar_wait(lbar, (uint32_t)luts & 1u, err, DEV_TIMEOUT_EPILOGUE));
         ++luts;
         if (!ok) break;
       }
-      const bool rb_on = lp.has_add && lp.r_bulk;
       const bool publish = chained && l + 1 < L;
       for (int tile = t_first; tile < n_tiles; tile += t_step, ++it) {
         __syncwarp();
@@ -621,60 +647,61 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
         // pixel of pitched row q: divisions by Hp*Wp and Wp as multiply-shift
         // with host-computed ceil(2^40 / d) (exact for q * d < 2^40, checked on the host)
         const uint32_t q = (uint32_t)tile * QC_TILE_M + (uint32_t)row;
-        const int n = (int)(((uint64_t)q * g.hpwp_mul) >> 40);
-        const int rem = (int)(q - (uint32_t)n * (uint32_t)hpwp);
-        const int oh = (int)(((uint64_t)(uint32_t)rem * g.wp_mul) >> 40);
-        const int ow = rem - oh * g.wp;
-        if (n < g.batch && oh < g.oh && ow < g.ow) {
-          float r[G];
-#pragma unroll
-          for (int c4 = 0; c4 < G / 4; ++c4) {
-            const float4 s4 = *reinterpret_cast<const float4*>(&sc[4 * c4]);
-            const int4 b4 = *reinterpret_cast<const int4*>(&bi[4 * c4]);
-            r[4 * c4 + 0] = requant_fast((int32_t)v[4 * c4 + 0] + b4.x, s4.x, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
-            r[4 * c4 + 1] = requant_fast((int32_t)v[4 * c4 + 1] + b4.y, s4.y, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
-            r[4 * c4 + 2] = requant_fast((int32_t)v[4 * c4 + 2] + b4.z, s4.z, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
-            r[4 * c4 + 3] = requant_fast((int32_t)v[4 * c4 + 3] + b4.w, s4.w, lp.y_m_minus_zero, lp.y_lo, lp.y_hi);
-          }
-          uint32_t out[G / 4];
-          if (lp.has_add) {
-            uint32_t rb[G / 4];
-            if (lp.r_bulk) {
-              const uint8_t* rrow = s_r + ((size_t)rs * QC_TILE_M + row) * OC;
-              const int64_t rpix = (int64_t)q + lp.r_off;
-              if constexpr (G == 8) {
-                const uint2 t = *reinterpret_cast<const uint2*>(rrow + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
-                rb[0] = t.x;
-                rb[1] = t.y;
-              } else {
-#pragma unroll
-                for (int c = 0; c < G / 16; ++c) {
-                  const uint4 t = *reinterpret_cast<const uint4*>(rrow + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
-                  rb[4 * c + 0] = t.x;
-                  rb[4 * c + 1] = t.y;
-                  rb[4 * c + 2] = t.z;
-                  rb[4 * c + 3] = t.w;
-                }
-              }
+        const int n = (int)(((uint64_t)q * hpwp_mul) >> 40);
+        const uint32_t rem = q - (uint32_t)n * hpwp;
+        const int oh = (int)(((uint64_t)rem * wp_mul) >> 40);
+        const int ow = (int)rem - oh * gwp;
+        const bool valid = n < gbatch && oh < goh && ow < gow;
+        // the tile's residual bytes of this warp's G channels (a fused add)
+        auto load_rb = [&](uint32_t(&rb)[G / 4]) {
+          if (rb_on) {
+            const uint8_t* rrow = s_r + ((size_t)rs * QC_TILE_M + row) * OC;
+            const int64_t rpix = (int64_t)q + r_off;
+            if constexpr (G == 8) {
+              const uint2 t = *reinterpret_cast<const uint2*>(rrow + 16 * swz_chunk(rpix, col0 / 16, OC) + (col0 % 16));
+              rb[0] = t.x;
+              rb[1] = t.y;
             } else {
-              qc_load_resid<OC, G>(lp, rb, col0, n, oh, ow);
+#pragma unroll
+              for (int c = 0; c < G / 16; ++c) {
+                const uint4 t = *reinterpret_cast<const uint4*>(rrow + 16 * swz_chunk(rpix, col0 / 16 + c, OC));
+                rb[4 * c + 0] = t.x;
+                rb[4 * c + 1] = t.y;
+                rb[4 * c + 2] = t.z;
+                rb[4 * c + 3] = t.w;
+              }
             }
-            if (lp.lut) {
-              // out byte = table[(conv byte << 8) | residual byte]: the conv
-              // bytes packed four to a word, the 16-bit indices of two
-              // channels built by one byte permute from the two words
-              const uint32_t rx4 = (uint32_t)lp.r_xor * 0x01010101u;
+          } else {
+            qc_load_resid<OC, G>(lp, rb, col0, n, oh, ow);
+          }
+        };
+        uint32_t out[G / 4];
+        if (valid) {
+          if (int_rq) {
 #pragma unroll
-              for (int c4 = 0; c4 < G / 4; ++c4) {
-                const uint32_t cw = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]);
-                const uint32_t rw = rb[c4] ^ rx4;
-                const uint32_t t01 = __byte_perm(rw, cw, 0x5140);  // [r0, c0, r1, c1]
-                const uint32_t t23 = __byte_perm(rw, cw, 0x7362);  // [r2, c2, r3, c3]
-                const uint32_t b0 = s_lut[t01 & 0xFFFFu], b1 = s_lut[t01 >> 16];
-                const uint32_t b2 = s_lut[t23 & 0xFFFFu], b3 = s_lut[t23 >> 16];
-                out[c4] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410) ^ yx4;
-              }
-            } else {
+            for (int c4 = 0; c4 < G / 4; ++c4) {
+              const float4 s4 = *reinterpret_cast<const float4*>(&sc[4 * c4]);
+              const int4 b4 = *reinterpret_cast<const int4*>(&bi[4 * c4]);
+              const int y0 = requant_int((int32_t)v[4 * c4 + 0] + b4.x, s4.x, rq_sub);
+              const int y1 = requant_int((int32_t)v[4 * c4 + 1] + b4.y, s4.y, rq_sub);
+              const int y2 = requant_int((int32_t)v[4 * c4 + 2] + b4.z, s4.z, rq_sub);
+              const int y3 = requant_int((int32_t)v[4 * c4 + 3] + b4.w, s4.w, rq_sub);
+              out[c4] = pack_sat_u8x4(y0, y1, y2, y3) ^ sx4;
+            }
+          } else {
+            float r[G];
+#pragma unroll
+            for (int c4 = 0; c4 < G / 4; ++c4) {
+              const float4 s4 = *reinterpret_cast<const float4*>(&sc[4 * c4]);
+              const int4 b4 = *reinterpret_cast<const int4*>(&bi[4 * c4]);
+              r[4 * c4 + 0] = requant_fast((int32_t)v[4 * c4 + 0] + b4.x, s4.x, ymz, ylo, yhi);
+              r[4 * c4 + 1] = requant_fast((int32_t)v[4 * c4 + 1] + b4.y, s4.y, ymz, ylo, yhi);
+              r[4 * c4 + 2] = requant_fast((int32_t)v[4 * c4 + 2] + b4.z, s4.z, ymz, ylo, yhi);
+              r[4 * c4 + 3] = requant_fast((int32_t)v[4 * c4 + 3] + b4.w, s4.w, ymz, ylo, yhi);
+            }
+            if (has_add && !use_lut) {  // the fused add in float, one channel at a time
+              uint32_t rb[G / 4];
+              load_rb(rb);
               if (lp.fast_div) {
 #pragma unroll
                 for (int c = 0; c < G; ++c) {
@@ -690,28 +717,72 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
                                           lp.add_inv_scale, lp.add_zero, lp.add_lo, lp.add_hi);
                 }
               }
-#pragma unroll
-              for (int c4 = 0; c4 < G / 4; ++c4)
-                out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
             }
-          } else {
 #pragma unroll
             for (int c4 = 0; c4 < G / 4; ++c4)
-              out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]) ^ yx4;
+              out[c4] = pack4(r[4 * c4 + 0], r[4 * c4 + 1], r[4 * c4 + 2], r[4 * c4 + 3]);
           }
-          qc_store<OC, G>(lp, out, col0, n, oh, ow);
+          if (has_add && use_lut) {
+            // out byte = table[(conv byte << 8) | residual byte]: the conv
+            // bytes packed four to a word, the 16-bit indices of two
+            // channels built by one byte permute from the two words
+            uint32_t rb[G / 4];
+            load_rb(rb);
+#pragma unroll
+            for (int c4 = 0; c4 < G / 4; ++c4) {
+              const uint32_t cw = out[c4];
+              const uint32_t rw = rb[c4] ^ rx4;
+              const uint32_t t01 = __byte_perm(rw, cw, 0x5140);  // [r0, c0, r1, c1]
+              const uint32_t t23 = __byte_perm(rw, cw, 0x7362);  // [r2, c2, r3, c3]
+              const uint32_t b0 = s_lut[t01 & 0xFFFFu], b1 = s_lut[t01 >> 16];
+              const uint32_t b2 = s_lut[t23 & 0xFFFFu], b3 = s_lut[t23 >> 16];
+              out[c4] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+            }
+          }
+#pragma unroll
+          for (int c4 = 0; c4 < G / 4; ++c4) out[c4] ^= yx4;
+        }
+        // Publish the previous tile now: its stores were issued a tile ago, so
+        // the proxy fence (which waits for this thread's earlier global writes)
+        // finds them drained instead of stalling right behind them.
+        if (pend) {
+          fence_proxy_async_global();
+          __syncwarp();
+          ++pub;
+          if (lane == 0) st_release_cta_u32(&s_stored[ew], (uint32_t)pub);
+          pend = false;
+        }
+        if (valid) {
+          if (y_layout == 0) {  // swizzled NHWC: G bytes of the pixel's OC-byte row
+            const int64_t ypix = ((int64_t)n * y_hp + oh + y_pt) * y_wp + ow + y_pl;
+            uint8_t* yrow = ybase + (uint64_t)ypix * OC;
+            if constexpr (G == 8) {
+              st_global_v2(yrow + 16 * swz_chunk(ypix, col0 / 16, OC) + (col0 % 16), out[0], out[1]);
+            } else {
+#pragma unroll
+              for (int c = 0; c < G / 16; ++c)
+                st_global_v4(yrow + 16 * swz_chunk(ypix, col0 / 16 + c, OC), out[4 * c + 0], out[4 * c + 1],
+                             out[4 * c + 2], out[4 * c + 3]);
+            }
+          } else {  // NCHW: one byte per channel plane
+            uint8_t* yb = ybase + ((int64_t)n * OC + col0) * yplane + (int64_t)oh * gow + ow;
+#pragma unroll
+            for (int c = 0; c < G; ++c) st_global_u8(yb + (int64_t)c * yplane, out[c >> 2] >> (8 * (c & 3)));
+          }
         }
         if (rb_on) {  // this warp is done with the tile's residual rows
           __syncwarp();
           if (lane == 0) mbar_arrive(&rempty[rs]);
           ++rit;
         }
-        if (publish) {  // this warp's rows of the tile are stored: tell the publisher
-          fence_proxy_async_global();
-          __syncwarp();
-          ++pub;
-          if (lane == 0) st_release_cta_u32(&s_stored[ew], (uint32_t)pub);
-        }
+        pend = publish;  // this warp's rows of the tile are stored: published with the next tile
+      }
+      if (pend) {  // the layer's last tile
+        fence_proxy_async_global();
+        __syncwarp();
+        ++pub;
+        if (lane == 0) st_release_cta_u32(&s_stored[ew], (uint32_t)pub);
+        pend = false;
       }
       if (!ok) break;
       __syncwarp();
@@ -825,6 +896,8 @@ static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, c
   p.y_lo = ys ? -128.0f : 0.0f;
   p.y_hi = ys ? 127.0f : 255.0f;
   p.y_m_minus_zero = kMagic - (float)op.ip[QC_Y_ZERO];
+  p.rq_int = (int)op.ip[QC_RQ_INT];
+  p.rq_sub = kMagicBits - (int)op.ip[QC_Y_ZERO];
   p.y_layout = (int)op.ip[QC_Y_LAYOUT];
   p.y_xor = (int)op.ip[QC_Y_XOR];
   p.y_hp = (int)op.ip[QC_Y_HP];

@@ -77,6 +77,40 @@ __device__ __forceinline__ float requant_fast(int32_t acc, float scale, float m_
   return fminf(r, hi);
 }
 
+// Integer form of requant_fast for |(float)acc * scale| < 2^21 (planner-proved,
+// QC_RQ_INT): adding 1.5 * 2^23 rounds v half-to-even to an integer k exactly
+// (the sum stays in [2^23, 2^24), where the float spacing is 1, and 1.5 * 2^23
+// is even), and the bit pattern of that sum is kMagicBits + k; subtracting
+// rq_sub = kMagicBits - zero leaves k + zero, the reference's rint(v) + zy, as
+// an int32 that pack_sat_u8x4 clamps to the output range.
+__device__ __forceinline__ int requant_int(int32_t acc, float scale, int rq_sub) {
+  const float v = __fmul_rn(__int2float_rn(acc), scale);
+  return __float_as_int(__fadd_rn(v, kMagic)) - rq_sub;
+}
+
+// Four int32 values saturated to [0, 255] and packed little-endian (y0 in the
+// low byte): two cvt.pack.sat, each converting two values with saturation.
+__device__ __forceinline__ uint32_t pack_sat_u8x4(int y0, int y1, int y2, int y3) {
+  uint32_t hi, w;
+  asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(y3), "r"(y2), "r"(0));
+  asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(y1), "r"(y0), "r"(hi));
+  return w;
+}
+
+// Stores with the state space stated: the output pointers come from a table
+// indexed at run time, where the compiler cannot see that they are global.
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(__cvta_generic_to_global(p)), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void st_global_v2(void* p, uint32_t a, uint32_t b) {
+  asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(__cvta_generic_to_global(p)), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void st_global_u8(void* p, uint32_t v) {
+  asm volatile("st.global.u8 [%0], %1;" ::"l"(__cvta_generic_to_global(p)), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ float div_refined(float s, float ys, float inv_ys) {
   const float q0 = __fmul_rn(s, inv_ys);
   const float e = __fmaf_rn(-q0, ys, s);

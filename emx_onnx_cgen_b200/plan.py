@@ -229,6 +229,23 @@ def unpack_nbits_zero_points(zp, n: int, n_blocks: int) -> np.ndarray:
     return np.stack([z & 15, z >> 4], axis=-1).reshape(n, -1)[:, :n_blocks]
 
 
+def qconv_int_requant_ok(w: np.ndarray, bias: np.ndarray, scale: np.ndarray, a_signed: int) -> int:
+    """1 when every accumulator the weights allow keeps |(float)acc * scale| < 2^21.
+
+    acc = bias + sum (x - zx) * w with |x - zx| <= 128 (int8 operands) or 255
+    (raw uint8 with zero point 0).  Below 2^21 (well inside 2^22) the kernel's
+    rint by adding 1.5 * 2^23 is exact and the result plus the zero point fits
+    an int32, so rounding, zero point and the clamp to the output range run as
+    one integer saturating pack with the reference's result
+    (qlinear_conv_op.c.j2:34-38)."""
+    if not np.all(np.isfinite(scale)):
+        return 0
+    oc = w.shape[0]
+    xmax = 128 if a_signed else 255
+    acc = xmax * np.abs(w.astype(np.int64)).reshape(oc, -1).sum(1) + np.abs(bias.astype(np.int64))
+    return int(float((acc.astype(np.float64) * np.abs(scale.astype(np.float64))).max()) < 2.0 ** 21)
+
+
 def nbits_weight_image(parts, k: int, block: int, fused: bool):
     """Weight image of the tcgen05 MatMulNBits kernel.
 
@@ -330,14 +347,22 @@ class B200PlanEmitter:
     """Emit target producing a B200 launch plan from a LoweredModel."""
 
     def __init__(self, *, use_tensor_cores: bool = True, nbits_rounded_dequant: bool = False,
-                 chain_convs: bool = True):
+                 chain_convs: bool = True, attention_mode: str = "exact"):
         """``nbits_rounded_dequant``: MatMulNBits multiplies fp16-rounded
         dequantised weights (one MMA per K slice, about 2x the throughput)
         instead of the exact hi + lo split; outputs then differ from the
         reference by up to ~2^-12 of sum_k |a_k * deq_k| rather than by
         summation order only.  ``chain_convs``: consecutive tensor-core
         convolutions of one geometry run as one persistent launch (outputs
-        are identical either way)."""
+        are identical either way).  ``attention_mode``: "exact" repeats the
+        reference's fp16 statement rounding bit for bit on CUDA cores;
+        "tensor" runs fp16 Attention with 128-wide heads on the tensor cores
+        (fp32 accumulation and online softmax: closer to the exact value than
+        the reference, not bit-identical to it); other head sizes keep the
+        exact kernel."""
+        if attention_mode not in ("exact", "tensor"):
+            raise ValueError(f"attention_mode {attention_mode!r}: 'exact' or 'tensor'")
+        self.attention_mode = attention_mode
         self.use_tensor_cores = use_tensor_cores
         self.nbits_rounded_dequant = nbits_rounded_dequant
         self.chain_convs = chain_convs
@@ -709,7 +734,8 @@ class B200PlanEmitter:
         oh, ow = op.out_spatial
         ip = {K.QC_N: n, K.QC_CIN: cin, K.QC_OC: oc, K.QC_KH: kh, K.QC_KW: kw, K.QC_HP: xin.hp, K.QC_WP: xin.wp,
               K.QC_OH: oh, K.QC_OW: ow, K.QC_A_SIGNED: cfg["a_signed"], K.QC_Y_ZERO: zy,
-              K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QC_X_ROWS: xin.rows}
+              K.QC_Y_SIGNED: int(_suffix(op.dtype) == "i8"), K.QC_X_ROWS: xin.rows,
+              K.QC_RQ_INT: qconv_int_requant_ok(w, bias, scale, cfg["a_signed"])}
         fp = {}
         t_r = t_lut = -1
         out_name = op.output
@@ -1107,8 +1133,14 @@ class B200PlanEmitter:
               K.AT_D: d, K.AT_DV: dv, K.AT_CAUSAL: int(bool(op.is_causal))}
         for slot, val in zip(range(K.AT_Q_SB, K.AT_O_ST + 1), ss):
             ip[slot] = val
-        self._b.op(K.K_ATTENTION_F16, [q, k, v, y, t_st], ip, {K.ATF_SCALE: scale16},
-                   label=f"{op.output} (reference fp16 arithmetic)", batched=batched)
+        tensor = (self.attention_mode == "tensor" and self.use_tensor_cores and d == 128 and dv == 128
+                  and all(st % 8 == 0 for st in ss))
+        if tensor:
+            self._b.op(K.K_ATTENTION_TC, [q, k, v, y, t_st], ip, {K.ATF_SCALE: scale16},
+                       label=f"{op.output} (tensor cores, fp32 online softmax)", batched=batched)
+        else:
+            self._b.op(K.K_ATTENTION_F16, [q, k, v, y, t_st], ip, {K.ATF_SCALE: scale16},
+                       label=f"{op.output} (reference fp16 arithmetic)", batched=batched)
 
     # ------------------------------------------------------------------ LSTM
     def _emit_LstmOp(self, i, op):
