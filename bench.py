@@ -55,7 +55,7 @@ sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20
 HEADLINE = "qconv_stack_int8"
-ALL_WORKLOADS = ("qconv_stack_int8", "llama_mlp_int4", "mlp_fp32", "attention_fp16", "lstm_fp32")
+ALL_WORKLOADS = ("qconv_stack_int8", "llama_mlp_int4", "mlp_fp32", "attention_fp16", "attention_fp16_tc", "lstm_fp32")
 
 
 # ----------------------------------------------------------------------------- workloads

@@ -66,7 +66,8 @@ def parse_input_dims(items) -> dict[str, int]:
 
 def _emitter(args) -> B200PlanEmitter:
     return B200PlanEmitter(use_tensor_cores=not args.no_tensor_cores,
-                           nbits_rounded_dequant=args.nbits_rounded_dequant)
+                           nbits_rounded_dequant=args.nbits_rounded_dequant,
+                           attention_mode=getattr(args, "attention_mode", "exact"))
 
 
 def compile_model(model_path, dim_values=None, weights_bin=None, threshold=DEFAULT_LARGE_WEIGHT_THRESHOLD,
@@ -198,6 +199,9 @@ def _common(p):
     p.add_argument("--nbits-rounded-dequant", action="store_true",
                    help="MatMulNBits: one fp16 MMA per K slice on rounded dequantised weights (faster, "
                         "not bit-compatible with the reference's fp32 dequantisation)")
+    p.add_argument("--attention-mode", choices=["exact", "tensor"], default="exact",
+                   help="Attention: the reference's fp16 rounding bit for bit (exact), or tensor cores with "
+                        "fp32 accumulation for 128-wide heads (tensor)")
 
 
 def build_parser() -> argparse.ArgumentParser:
