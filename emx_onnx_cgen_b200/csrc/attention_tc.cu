@@ -14,8 +14,9 @@
 // tests hold it to that (max ULP against a float64 evaluation no larger than
 // the reference's own).
 //
-// Work split: one CTA per (128 query rows, head, batch), heaviest causal
-// query tiles first.  Warp 0: TMA producer (the Q tile once, then K and V
+// Work split: one CTA per (128 query rows, head, batch); heads in groups of 8
+// run all their query tiles together (K/V stay in L2), heaviest causal query
+// tiles first within a group.  Warp 0: TMA producer (the Q tile once, then K and V
 // tiles of 128 keys, double-buffered).  Warp 1: issues S_j = Q K_j^T into one
 // of two TMEM score buffers.  Warp 2: issues O += P_j V_j into the TMEM output
 // accumulator.  Warps 4-7: one thread per query row -- scores from TMEM,
@@ -49,6 +50,7 @@ constexpr int ATC_THREADS = 256;  // 8 warps
 constexpr uint32_t ATC_SLAB = 128u * 128u;     // one 64-wide slab of a 128-row tile: 16 KB
 constexpr uint32_t ATC_TILE = 2u * ATC_SLAB;   // a 128 x 128 fp16 tile: 32 KB
 constexpr float ATC_RESCALE = 8.0f;            // lazy-rescale threshold, log2 units
+constexpr int ATC_GROUP = 8;                   // heads whose query tiles run together
 
 struct AttnTcParams {
   CUtensorMap map_q, map_k, map_v;  // 4-D (d, t, h, b), box (64, 128, 1, 1), 128-byte swizzle
@@ -147,9 +149,15 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* const err = p.err;
+  // CTA order: heads in groups of ATC_GROUP, every query tile of a group before
+  // the next group (a head's K and V, 1 MB at 2048 x 128, stay in L2 while its
+  // query tiles run), heaviest causal tiles first within a group
   const int bh_count = p.HQ * p.B;
-  const int qt = p.n_qtiles - 1 - (int)(blockIdx.x / (unsigned)bh_count);  // heaviest query tiles first
-  const int bh = (int)(blockIdx.x % (unsigned)bh_count);
+  const int grp = (int)(blockIdx.x / (unsigned)(ATC_GROUP * p.n_qtiles));
+  const int gsize = min(ATC_GROUP, bh_count - grp * ATC_GROUP);
+  const int within = (int)blockIdx.x - grp * ATC_GROUP * p.n_qtiles;
+  const int qt = p.n_qtiles - 1 - within / gsize;
+  const int bh = grp * ATC_GROUP + within % gsize;
   const int h = bh % p.HQ, b = bh / p.HQ;
   const int kvh = h / p.group;
   const int q0 = qt * ATC_M;

@@ -91,8 +91,14 @@ enum { ATF_SCALE };
 //      t[5]=scratch h [2][B][H], t[6]=scratch c [B][H], t[7]=Y|-1, t[8]=Y_h|-1, t[9]=Y_c|-1
 //      gate columns are in tiles of 4 * LS_TILE_UNITS: position g * LS_TILE_UNITS + u of tile T is
 //      gate g of unit T * LS_TILE_UNITS + u (units padded to a multiple of LS_TILE_UNITS with zero rows)
-enum { LS_T, LS_B, LS_I, LS_H };
+enum { LS_T, LS_B, LS_I, LS_H, LS_GX_PLACEHOLDER /*1: t[4] is a placeholder (persistent path planned)*/ };
 enum { LS_TILE_UNITS = 16 };
+// Persistent LSTM kernel (lstm.cu): chunk of K staged per cp.async stage, stages,
+// batch rows per thread (max), threads per CTA (max), shared memory per CTA,
+// and the SM count the planner assumes when it leaves out the x-partials scratch.
+// (The shared-memory limit is dynamic memory: 225 KB, below the 227 KB a CTA may
+// hold in total, which also covers the kernel's static words.)
+enum { LP_KC = 8, LP_STAGES = 6, LP_RB_MAX = 4, LP_MAX_THREADS = 512, LP_SMEM_LIMIT = 230400, LP_PLAN_SMS = 148 };
 
 // ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y;
 //      tensor-core plans add t[3]=B^T [N][K] u8, t[4]=B's column sums [N] i32, t[5]=A's row sums [M] i32

@@ -153,11 +153,306 @@ __global__ void lstm_init_kernel(float* __restrict__ h0, float* __restrict__ c0,
   }
 }
 
+// ---- persistent path: one launch for all T steps.
+//
+// CTA k owns hidden units [k*U, (k+1)*U): the W and R rows of their four gates
+// (U * 4 * (I + H) floats) stay in shared memory for the whole sequence.
+// Compute warp w serves unit w / WU and batch rows ((w % WU) * 32 * RB) + lane
+// + 32 r (r < RB), so each thread holds RB x 4 exact-order chains (its rows'
+// i, o, f, c gates of one unit) and the cell states of those (row, unit) pairs
+// in registers.  One producer warp streams the activations through a ring of
+// LP_STAGES chunks (LP_KC columns of every batch row) with 2-D TMA loads
+// (32-byte swizzle), in the order the compute warps consume them: x_0; then
+// per step t, x_{t+1} (its x terms are computed first, kept aside) and, once
+// the grid counter says every CTA has written h_{t-1}, h_{t-1}.  The compute warps never synchronise CTA-wide
+// inside a step: a chunk's full barrier carries its bytes, and each warp
+// releases the chunk on its empty barrier once its lanes have read it.  Per
+// step a compute warp adds the h terms, applies the bias and the cell update,
+// stores h_t, and the compute warps' named barrier lets one thread arrive on
+// the grid counter; the x terms of step t+1 follow at once, so that work
+// overlaps the other CTAs finishing step t.  A step-0 h term adds h = 0 times
+// R, i.e. +-0, which leaves every partial sum unchanged (a partial sum started
+// at +0.0f is never -0), so step 0 has no h terms.  Every wait is bounded.
+struct LstmPParams {
+  CUtensorMap map_x;   // x as [T*B][I] f32, box (LP_KC, BPAD), 32-byte swizzle
+  CUtensorMap map_h;   // h buffer as [2*B][H] f32, same box
+  const float* wp;     // [4Hp][I], gate rows interleaved (kernels.h)
+  const float* rp;     // [4Hp][H]
+  const float* bsum;   // [4Hp]
+  float* hbuf;         // [2][B][H]
+  unsigned int* bar;   // grid counter: one arrival per CTA per step
+  float* y;            // [T][1][B][H] or null
+  float* y_h;          // [1][B][H] or null
+  float* y_c;
+  int T, B, I, H, U, WU, BPAD;
+  int* err;
+};
+
+struct LpConfig {
+  int rb, wu, u, grid, threads, bpad;
+  size_t smem;
+  bool ok;
+};
+
+// Shape of the persistent launch for batch B, input I, hidden H on `sms` SMs
+// (threads: the compute warps plus the producer warp).
+static LpConfig lp_config(int B, int I, int H, int sms) {
+  LpConfig c{};
+  c.rb = B > 64 ? 4 : (B > 32 ? 2 : 1);
+  c.wu = (B + 32 * c.rb - 1) / (32 * c.rb);
+  c.bpad = c.wu * 32 * c.rb;
+  c.u = sms > 0 ? (H + sms - 1) / sms : H;
+  c.grid = (H + c.u - 1) / c.u;
+  c.threads = c.u * c.wu * 32 + 32;
+  c.smem = 1024 + (size_t)c.u * 4 * (I + H) * sizeof(float) + (size_t)LP_STAGES * c.bpad * LP_KC * sizeof(float) +
+           (size_t)(2 * LP_STAGES + 1) * 8;
+  c.ok = I % LP_KC == 0 && H % LP_KC == 0 && c.bpad <= 256 && c.threads <= LP_MAX_THREADS &&
+         c.smem <= (size_t)LP_SMEM_LIMIT && c.grid <= sms;
+  return c;
+}
+
+// gate row of (unit u, gate g) in the interleaved weight layout
+__device__ __forceinline__ int lp_row(int u, int g) {
+  return (u / LS_TILE_UNITS) * (4 * LS_TILE_UNITS) + g * LS_TILE_UNITS + (u % LS_TILE_UNITS);
+}
+
+template <int RB>
+__global__ void __launch_bounds__(LP_MAX_THREADS, 1) lstm_persistent_kernel(const __grid_constant__ LstmPParams p) {
+  extern __shared__ __align__(1024) uint8_t lp_raw[];
+  constexpr int KC = LP_KC, S = LP_STAGES;
+  static_assert(KC == 8, "the ring's 32-byte swizzle assumes 8-float rows");
+  const int KW = p.I + p.H;  // weight row: x part then h part
+  uint8_t* base = lp_raw + ((1024u - (smem_u32(lp_raw) & 1023u)) & 1023u);
+  float* ring = reinterpret_cast<float*>(base);                              // [S][BPAD][KC], 1024-aligned
+  float* ws = ring + (size_t)S * p.BPAD * KC;                                // [U][4][KW]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ws + (size_t)p.U * 4 * KW);   // [S]
+  uint64_t* empty = full + S;                                                // [S]
+  uint64_t* step_done = empty + S;  // every compute warp has stored its h_t (one phase per step)
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int n_compute = p.U * p.WU;  // compute warps; the producer is warp n_compute
+  const int B = p.B, I = p.I, H = p.H;
+  int* const err = p.err;
+  const uint32_t stage_bytes = (uint32_t)(p.BPAD * KC * sizeof(float));
+  const int nx = I / KC, nh = H / KC;  // chunks of an x part / an h part
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)n_compute);
+    }
+    mbar_init(step_done, (uint32_t)n_compute);
+    fence_barrier_init();
+  }
+  pdl_wait();  // x and the zeroed counter come from preceding kernels
+  pdl_launch_dependents();
+  // this CTA's weight rows (plan constants) into shared memory
+  {
+    const int q_per_row = KW / 4;
+    const int total = p.U * 4 * q_per_row;
+    for (int e = tid; e < total; e += blockDim.x) {
+      const int row = e / q_per_row, q = e - row * q_per_row;
+      const int uu = blockIdx.x * p.U + row / 4, g = row % 4;
+      const bool ok = uu < H;
+      const int k = 4 * q;
+      const float* src = !ok ? p.wp : (k < I ? p.wp + (size_t)lp_row(uu, g) * I + k
+                                               : p.rp + (size_t)lp_row(uu, g) * H + (k - I));
+      xc_cp16(ws + (size_t)row * KW + k, src, ok);
+    }
+    xc_commit();
+    xc_wait<0>();
+  }
+  __syncthreads();
+
+  if (warp == n_compute) {
+    // ---------------- producer: chunks in consumption order
+    if (lane == 0) {
+      int cc = 0;  // chunks issued
+      bool ok = true;
+      auto issue = [&](const CUtensorMap* map, int x0, int y0) -> bool {
+        const int s = cc % S;
+        if (cc >= S && !mbar_wait(&empty[s], (uint32_t)((cc / S) - 1) & 1u, err, DEV_TIMEOUT_PRODUCER)) return false;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        tma_load_2d(ring + (size_t)s * p.BPAD * KC, map, &full[s], x0, y0);
+        ++cc;
+        return true;
+      };
+      // stream order = consumption order: x_0, then per step t: x_{t+1}, h_{t-1}
+      for (int c = 0; c < nx && ok; ++c) ok = issue(&p.map_x, c * KC, 0);
+      const unsigned int grid = gridDim.x;
+      for (int t = 0; t < p.T && ok; ++t) {
+        if (t + 1 < p.T)
+          for (int c = 0; c < nx && ok; ++c) ok = issue(&p.map_x, c * KC, (t + 1) * B);
+        if (!ok || t == 0) continue;
+        // h_{t-1} needs every CTA's step t-1
+        const unsigned int target = (unsigned int)t * grid;
+        const uint64_t t0 = globaltimer_ns();
+        const uint64_t budget = wait_budget_ns(err);
+        uint32_t spins = 0;
+        while (true) {
+          unsigned int v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
+          if (v >= target) break;
+          if ((++spins & 15u) == 0) {
+            if (error_raised(err)) { ok = false; break; }
+            if (globaltimer_ns() - t0 > budget) {
+              record_error(err, DEV_TIMEOUT_GRID);
+              ok = false;
+              break;
+            }
+          }
+          __nanosleep(64);
+        }
+        if (!ok) break;
+        fence_proxy_async_global();  // the TMA reads h written by generic stores of other CTAs
+        for (int c = 0; c < nh && ok; ++c) ok = issue(&p.map_h, c * KC, ((t - 1) & 1) * B);
+      }
+      // let every copy issued land before the CTA can exit
+      for (int k = cc - S < 0 ? 0 : cc - S; k < cc; ++k) (void)mbar_wait(&full[k % S], (uint32_t)(k / S) & 1u, nullptr, 0);
+    }
+    return;
+  }
+
+  // ---------------- compute warps
+  const int ul = warp / p.WU, wb = warp % p.WU;
+  const int u = blockIdx.x * p.U + ul;
+  const bool unit_ok = u < H;
+  float bs[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) bs[g] = unit_ok ? p.bsum[lp_row(u, g)] : 0.0f;
+  const float* wrow = ws + (size_t)ul * 4 * KW;
+  const int row0 = wb * 32 * RB + lane;
+  float acc[RB][4];
+  float cst[RB];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) cst[r] = 0.0f;
+  int cc = 0;  // chunks consumed
+  bool ok = true;
+  // acc[r][g] += a[row][k] * W[g][wofs + k] over n chunks, k in order
+  auto run_part = [&](int n, int wofs) {
+    for (int ch = 0; ch < n; ++ch, ++cc) {
+      const int s = cc % S;
+      ok = mbar_wait(&full[s], (uint32_t)(cc / S) & 1u, err, DEV_TIMEOUT_MMA);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        return;
+      }
+      const float* a = ring + (size_t)s * p.BPAD * KC;
+      const float* w = wrow + wofs + ch * KC;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float4 w4[4], a4[RB];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) w4[g] = *reinterpret_cast<const float4*>(w + g * KW + 4 * half);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {  // 32-byte swizzle: 16-byte half h of row q sits at h ^ ((q >> 2) & 1)
+          const int q = row0 + 32 * r;
+          a4[r] = *reinterpret_cast<const float4*>(a + q * KC + 4 * (half ^ ((q >> 2) & 1)));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const float av = j == 0 ? a4[r].x : j == 1 ? a4[r].y : j == 2 ? a4[r].z : a4[r].w;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const float wv = j == 0 ? w4[g].x : j == 1 ? w4[g].y : j == 2 ? w4[g].z : w4[g].w;
+              acc[r][g] = __fadd_rn(acc[r][g], __fmul_rn(av, wv));
+            }
+          }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  };
+
+  const size_t bh = (size_t)B * H;
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) acc[r][g] = 0.0f;
+  run_part(nx, 0);  // x terms of step 0
+  for (int t = 0; t < p.T && ok; ++t) {
+    // x terms of step t are in acc; the h terms of h_{t-1} follow (none at step 0)
+    float acc_x[RB][4];
+    if (t + 1 < p.T) {
+      // the chunk stream has x_{t+1} before h_{t-1}: the next step's x terms first, kept aside
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          acc_x[r][g] = acc[r][g];
+          acc[r][g] = 0.0f;
+        }
+      run_part(nx, 0);
+      if (!ok) break;
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const float nxt = acc[r][g];
+          acc[r][g] = acc_x[r][g];
+          acc_x[r][g] = nxt;
+        }
+    }
+    if (t > 0) {
+      run_part(nh, I);
+      if (!ok) break;
+    }
+    // bias and cell update; h_t to global memory
+    float* hn = p.hbuf + (size_t)(t & 1) * bh;
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const int b = row0 + 32 * r;
+      if (!unit_ok || b >= B) continue;
+      const float gi = __fadd_rn(acc[r][0], bs[0]);
+      const float go = __fadd_rn(acc[r][1], bs[1]);
+      const float gf = __fadd_rn(acc[r][2], bs[2]);
+      const float gc = __fadd_rn(acc[r][3], bs[3]);
+      const float ig = sigmoid_ref(gi);
+      const float fg = sigmoid_ref(gf);
+      const float cg = tanhf(gc);
+      const float c_new = __fadd_rn(__fmul_rn(fg, cst[r]), __fmul_rn(ig, cg));
+      const float og = sigmoid_ref(go);
+      const float h_new = __fmul_rn(og, tanhf(c_new));
+      cst[r] = c_new;
+      const size_t o = (size_t)b * H + u;
+      hn[o] = h_new;
+      if (p.y) p.y[(size_t)t * bh + o] = h_new;
+      if (t == p.T - 1) {
+        if (p.y_h) p.y_h[o] = h_new;
+        if (p.y_c) p.y_c[o] = c_new;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(step_done);  // this warp's h_t stores are issued
+    if (tid == 0) {  // once every compute warp's are: one arrival on the grid counter
+      if (!mbar_wait(step_done, (uint32_t)t & 1u, err, DEV_TIMEOUT_EPILOGUE)) break;
+      __threadfence();
+      atomicAdd(p.bar, 1u);
+    }
+    if (t + 1 < p.T) {
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) acc[r][g] = acc_x[r][g];
+    }
+  }
+}
+
+__global__ void lstm_counter_reset_kernel(unsigned int* bar) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) *bar = 0u;
+}
+
 int prepare_lstm_f32(const PlanOp&, void* const*, OpState*, int, char* msg, size_t n) {
   cudaError_t e = cudaFuncSetAttribute(lstm_gx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)GxChain::SMEM_BYTES);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(lstm_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)StChain::SMEM_BYTES);
+  for (auto k : {lstm_persistent_kernel<1>, lstm_persistent_kernel<2>, lstm_persistent_kernel<4>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM_LIMIT);
   if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   return 0;
 }
@@ -181,6 +476,45 @@ int launch_lstm_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   const int hp = (H + LS_TILE_UNITS - 1) / LS_TILE_UNITS * LS_TILE_UNITS;
   const int N = 4 * hp;
   const int64_t bh = (int64_t)B * H;
+  // persistent path: one CTA per SM resident at once (checked by occupancy), weights in shared memory
+  const LpConfig lc = lp_config(B, I, H, ctx.num_sms);
+  if (lc.ok) {
+    auto kern = lc.rb == 1 ? lstm_persistent_kernel<1> : (lc.rb == 2 ? lstm_persistent_kernel<2> : lstm_persistent_kernel<4>);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, lc.threads, lc.smem) != cudaSuccess || per_sm < 1)
+      return 5;
+    unsigned int* bar = reinterpret_cast<unsigned int*>(c);  // the c scratch: the persistent path keeps c in registers
+    LstmPParams pp{};
+    char msg[128];
+    if (make_tmap_2d(&pp.map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, (uint64_t)I, (uint64_t)T * B, (uint64_t)I * 4,
+                     LP_KC, (uint32_t)lc.bpad, CU_TENSOR_MAP_SWIZZLE_32B, msg, sizeof(msg)) ||
+        make_tmap_2d(&pp.map_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, hbuf, (uint64_t)H, (uint64_t)2 * B, (uint64_t)H * 4,
+                     LP_KC, (uint32_t)lc.bpad, CU_TENSOR_MAP_SWIZZLE_32B, msg, sizeof(msg)))
+      return 5;
+    cudaError_t e = launch_pdl(lstm_counter_reset_kernel, dim3(1), dim3(32), 0, ctx.stream, bar);
+    ++*launches;
+    if (e != cudaSuccess) return 4;
+    pp.wp = wp;
+    pp.rp = rp;
+    pp.bsum = bsum;
+    pp.hbuf = hbuf;
+    pp.bar = bar;
+    pp.y = y;
+    pp.y_h = y_h;
+    pp.y_c = y_c;
+    pp.T = T;
+    pp.B = B;
+    pp.I = I;
+    pp.H = H;
+    pp.U = lc.u;
+    pp.WU = lc.wu;
+    pp.BPAD = lc.bpad;
+    pp.err = ctx.d_error;
+    e = launch_pdl(kern, dim3(lc.grid), dim3(lc.threads), lc.smem, ctx.stream, pp);
+    ++*launches;
+    return e == cudaSuccess ? 0 : 4;
+  }
+  if (op.ip[LS_GX_PLACEHOLDER]) return 5;  // planned for the persistent path, which this device cannot run
   cudaError_t e = launch_pdl(lstm_init_kernel, dim3((unsigned)((bh + 255) / 256 < 1184 ? (bh + 255) / 256 : 1184)),
                              dim3(256), 0, ctx.stream, hbuf, c, bh);
   ++*launches;

@@ -229,6 +229,23 @@ def unpack_nbits_zero_points(zp, n: int, n_blocks: int) -> np.ndarray:
     return np.stack([z & 15, z >> 4], axis=-1).reshape(n, -1)[:, :n_blocks]
 
 
+def lstm_persistent_fits(b: int, isz: int, h: int, sms: int) -> bool:
+    """The persistent LSTM kernel's launch-shape rule (lstm.cu lp_config): one
+    CTA per SM holds ceil(H / sms) units' W and R rows and a LP_STAGES-deep
+    ring of LP_KC activation columns for every batch row (at most 256 rows,
+    one TMA box), with one compute warp per 32 x RB rows of a unit plus a
+    producer warp."""
+    rb = 4 if b > 64 else (2 if b > 32 else 1)
+    wu = -(-b // (32 * rb))
+    bpad = wu * 32 * rb
+    u = -(-h // sms)
+    grid = -(-h // u)
+    threads = u * wu * 32 + 32
+    smem = 1024 + u * 4 * (isz + h) * 4 + K.LP_STAGES * bpad * K.LP_KC * 4 + (2 * K.LP_STAGES + 1) * 8
+    return (isz % K.LP_KC == 0 and h % K.LP_KC == 0 and bpad <= 256 and threads <= K.LP_MAX_THREADS
+            and smem <= K.LP_SMEM_LIMIT and grid <= sms)
+
+
 def qconv_int_requant_ok(w: np.ndarray, bias: np.ndarray, scale: np.ndarray, a_signed: int) -> int:
     """1 when every accumulator the weights allow keeps |(float)acc * scale| < 2^21.
 
@@ -1189,15 +1206,20 @@ class B200PlanEmitter:
         t_r = self._b.weight(rp, "f32", op.input_r + ":interleaved")
         t_bs = self._b.weight(bsum, "f32", (op.input_b or "lstm") + ":bias-sum")
         x = self._src(op.input_x)
-        t_gx = self._b.arena_tensor(T_TEMP, "f32", (t * b, 4 * hp), name=f"{op.input_x}:lstm-x-partials")
+        # the persistent kernel computes each step's x terms itself; only the
+        # per-step path needs every step's x partial sums in the arena
+        persistent = lstm_persistent_fits(b, isz, h, K.LP_PLAN_SMS)
+        gx_shape = (1, 4) if persistent else (t * b, 4 * hp)
+        t_gx = self._b.arena_tensor(T_TEMP, "f32", gx_shape, name=f"{op.input_x}:lstm-x-partials")
         t_h = self._b.arena_tensor(T_TEMP, "f32", (2, b, h), name="lstm:h")
         t_c = self._b.arena_tensor(T_TEMP, "f32", (b, h), name="lstm:c")
         outs = []
         for name, shp in ((op.output_y, (t, 1, b, h)), (op.output_y_h, (1, b, h)), (op.output_y_c, (1, b, h))):
             outs.append(self._dest(name, "f32", shp) if name else -1)
         self._b.op(K.K_LSTM_F32, [x, t_w, t_r, t_bs, t_gx, t_h, t_c, *outs],
-                   {K.LS_T: t, K.LS_B: b, K.LS_I: isz, K.LS_H: h},
-                   label=f"LSTM T={t} B={b} I={isz} H={h} (reference order)")
+                   {K.LS_T: t, K.LS_B: b, K.LS_I: isz, K.LS_H: h, K.LS_GX_PLACEHOLDER: int(persistent)},
+                   label=f"LSTM T={t} B={b} I={isz} H={h} (reference order, "
+                         f"{'one persistent launch' if persistent else 'one launch per step'})")
 
     # ------------------------------------------------------------------ MatMulNBits
     def _nbits_reject(self, op) -> str | None:

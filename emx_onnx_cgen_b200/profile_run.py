@@ -26,6 +26,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch/rows (0: default)")
     ap.add_argument("--kw", default="", help='builder arguments as JSON, e.g. \'{"shape": [16384, 4096]}\'')
+    ap.add_argument("--emit", default="", help='plan emitter options as JSON, e.g. \'{"attention_mode": "tensor"}\'')
     args = ap.parse_args()
     kw = {k: tuple(v) if isinstance(v, list) else v for k, v in json.loads(args.kw).items()} if args.kw else {}
     if args.batch:
@@ -33,7 +34,7 @@ def main() -> None:
                "lstm_fp32": "batch"}[args.workload]
         kw[key] = args.batch
     wl = W.BUILDERS[args.workload](**kw)
-    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    plan = B200PlanEmitter(**(json.loads(args.emit) if args.emit else {})).emit_plan(lowering.lower(wl.graph))
     sess = Session(plan, device=0)
     x = wl.make_inputs(0)
     ins = [torch.from_numpy(np.ascontiguousarray(x[n])).cuda() for n in plan.input_names]

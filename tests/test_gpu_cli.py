@@ -22,10 +22,10 @@ CASES = {
     "mlp_fp32": dict(m=8, k=128, hidden=256),
     "llama_mlp_int4": dict(m=16, hidden=256, inter=512),
 }
-# the fused int4 MLP rounds its fp16 intermediate in a different place than
-# the C (a one-ULP flip of the intermediate can move an output by more than
-# 100 ULP near a cancellation); its own parity tests bound that per element
-MAX_ULP = {"llama_mlp_int4": 1000}
+# every case runs at the reference verify's default --max-ulp 100 (measured
+# max ULP: 0 for all three at these sizes; the int4 MLP's full-size worst case
+# is bounded per element in test_gpu_nbits.py)
+MAX_ULP = {}
 
 
 def _files(tmp_path, name, seed=3):
@@ -46,6 +46,8 @@ def test_verify_against_oracle(name, tmp_path, capsys):
     rc = cli.main(["verify", str(model), "--inputs", str(tmp_path / "in.npz"), "--expected",
                    str(tmp_path / "exp.npz"), *tol])
     out = capsys.readouterr().out
+    with capsys.disabled():
+        print(f"\n{name}: verify {out.strip()} (tolerance --max-ulp {tol[1]})")
     assert rc == 0 and out.startswith("OK (max ULP"), out
     # perturb one element of the first output far beyond any tolerance
     name0 = wl.graph.outputs[0].name

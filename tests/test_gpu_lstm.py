@@ -10,9 +10,8 @@ steps of the full-size model the difference stays at the fp32 epsilon level
 (max |Y - Y_ref| 1.3e-7, and as close to a float64 evaluation as the
 reference itself), so it shows up as a large ULP count only on outputs near
 zero.  Outputs must agree within LSTM_MAX_ULP fp32 ULP under the reference's
-metric (shared/ulp.py:26-50) with the absolute skip widened to
-LSTM_ATOL_EPS fp32 eps (the reference verify's --atol-eps; its --max-ulp
-default is 100).
+metric (shared/ulp.py:26-50) with the absolute skip at LSTM_ATOL_EPS fp32
+eps: the reference verify's defaults (--max-ulp 100, --atol-eps 1).
 """
 import numpy as np
 import pytest
@@ -26,15 +25,29 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 LSTM_MAX_ULP = 100
-LSTM_ATOL_EPS = 4.0
+LSTM_ATOL_EPS = 1.0
 
 
-def _check(out, ref, what):
+# Full size (512 steps): the expf / tanhf last-bit differences carried through
+# the recurrence reach |Y - Y_ref| = 1.49e-7 (1.25 fp32 eps, measured on a B200
+# over 512 steps); at the reference's 1-eps skip that is 8750 ULP on an output
+# within 1e-6 of zero.  The stated bound there: |diff| <= LSTM_FULL_ABS_EPS eps,
+# and <= LSTM_MAX_ULP ULP with the skip at LSTM_FULL_ABS_EPS eps.
+LSTM_FULL_ABS_EPS = 2.0
+
+
+def _check(out, ref, what, atol_eps=LSTM_ATOL_EPS, abs_eps=None):
     worst = 0
+    eps = float(np.finfo(np.float32).eps)
     for k in ref:
-        d = ulp_diff_f32(out[k], ref[k], atol_eps=LSTM_ATOL_EPS)
-        worst = max(worst, int(d.max(initial=0)))
-        assert int(d.max(initial=0)) <= LSTM_MAX_ULP, f"{what}:{k}: max ULP {int(d.max())}"
+        d1 = int(ulp_diff_f32(out[k], ref[k], atol_eps=1.0).max(initial=0))
+        m = int(ulp_diff_f32(out[k], ref[k], atol_eps=atol_eps).max(initial=0))
+        diff = float(np.max(np.abs(out[k].astype(np.float64) - ref[k].astype(np.float64)), initial=0))
+        print(f"{what}:{k}: max ULP {d1} (skip 1 eps), {m} (skip {atol_eps} eps), max |diff| {diff:.3g}")
+        worst = max(worst, m)
+        assert m <= LSTM_MAX_ULP, f"{what}:{k}: max ULP {m}"
+        if abs_eps is not None:
+            assert diff <= abs_eps * eps, f"{what}:{k}: |diff| {diff:.3g} above {abs_eps} eps"
     return worst
 
 
@@ -83,4 +96,4 @@ def test_full_size_batch_rows():
         small.graph.initializers[k] = wl.graph.initializers[k]
     ref = oracle.run_graph(small.graph, {"X": np.ascontiguousarray(x["X"][:, rows, :])})
     sub = {"Y": out["Y"][:, :, rows, :], "Y_h": out["Y_h"][:, rows, :], "Y_c": out["Y_c"][:, rows, :]}
-    _check(sub, ref, "full-size sample rows")
+    _check(sub, ref, "full-size sample rows", atol_eps=LSTM_FULL_ABS_EPS, abs_eps=LSTM_FULL_ABS_EPS)
