@@ -30,6 +30,11 @@ enum KernelId : uint32_t {
   K_QUANTIZE_LINEAR = 17,
   K_DEQUANTIZE_LINEAR = 18,
   K_ATTENTION_TC = 19,  // opset-23 Attention, fast mode: tcgen05 kind::f16, fp32 online softmax (attention_tc.cu)
+  K_COPY = 20,             // byte copy (a Reshape whose output is a graph output)
+  K_TRANSPOSE = 21,        // N-d transpose, 1/2/4-byte elements
+  K_MAXPOOL = 22,          // 2-D MaxPool, 8-bit
+  K_QLINEAR_AVGPOOL = 23,  // com.microsoft QLinearAveragePool, 2-D NCHW, 8-bit
+  K_QLINEAR_SOFTMAX = 24,  // com.microsoft QLinearSoftmax, 8-bit
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -99,6 +104,26 @@ enum { LS_TILE_UNITS = 16 };
 // (The shared-memory limit is dynamic memory: 225 KB, below the 227 KB a CTA may
 // hold in total, which also covers the kernel's static words.)
 enum { LP_KC = 8, LP_STAGES = 6, LP_RB_MAX = 4, LP_MAX_THREADS = 512, LP_SMEM_LIMIT = 230400, LP_PLAN_SMS = 148 };
+
+// ---- K_COPY: t[0]=src, t[1]=dst; CP_BATCH > 0: CP_BYTES covers that many batch entries
+enum { CP_BYTES, CP_BATCH };
+
+// ---- K_TRANSPOSE: t[0]=x, t[1]=y; y[o0..o5] = x[sum o_i * TR_S_i] over the output dims
+//      (rank padded to 6 with leading 1s; TR_S_i = x's stride of the input axis perm[i]);
+//      TR_BATCH_AXIS: padded output axis that follows the run's batch (batched plans)
+enum { TR_ELEM, TR_D0, TR_D1, TR_D2, TR_D3, TR_D4, TR_D5, TR_S0, TR_S1, TR_S2, TR_S3, TR_S4, TR_S5, TR_BATCH_AXIS };
+
+// ---- K_MAXPOOL / K_QLINEAR_AVGPOOL: t[0]=x NCHW, t[1]=y NCHW
+enum {
+  PL_N, PL_C, PL_H, PL_W, PL_OH, PL_OW, PL_KH, PL_KW, PL_SH, PL_SW, PL_DH, PL_DW, PL_PT, PL_PL, PL_X_SIGNED,
+  PL_Y_SIGNED, PL_COUNT_PAD, PL_X_ZERO, PL_Y_ZERO
+};
+enum { PLF_SCALE /*QLinearAveragePool: (float)x_scale / (float)y_scale*/ };
+
+// ---- K_QLINEAR_SOFTMAX: t[0]=x, t[1]=y, t[2]=expf table f32 [256][256] (raw byte of the element,
+//      raw byte of the row maximum); rows (outer, inner) of axis_size elements at stride inner
+enum { QS_OUTER, QS_AXIS, QS_INNER, QS_X_SIGNED, QS_Y_SIGNED, QS_X_ZERO, QS_Y_ZERO };
+enum { QSF_X_SCALE, QSF_Y_INV /*floorf(1 / (float)y_scale)*/ };
 
 // ---- K_QLINEAR_MATMUL / K_MATMUL_INTEGER: t[0]=A [M][K] 8-bit, t[1]=B [K][N] 8-bit, t[2]=Y;
 //      tensor-core plans add t[3]=B^T [N][K] u8, t[4]=B's column sums [N] i32, t[5]=A's row sums [M] i32
@@ -216,6 +241,11 @@ int launch_softmax_f32(const PlanOp&, void* const*, const OpState*, const Launch
 int launch_quant(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_attention(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_attention(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_copy(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_transpose(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_maxpool(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_qlinear_avgpool(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int launch_qlinear_softmax(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_attention_tc(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_attention_tc(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 

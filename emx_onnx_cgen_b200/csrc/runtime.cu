@@ -53,6 +53,11 @@ const KernelEntry kKernels[] = {
     {emx::K_LSTM_F32, emx::prepare_lstm_f32, emx::launch_lstm_f32, "lstm_f32"},
     {emx::K_ATTENTION_F16, emx::prepare_attention, emx::launch_attention, "attention_f16"},
     {emx::K_ATTENTION_TC, emx::prepare_attention_tc, emx::launch_attention_tc, "attention_tc"},
+    {emx::K_COPY, nullptr, emx::launch_copy, "copy"},
+    {emx::K_TRANSPOSE, nullptr, emx::launch_transpose, "transpose"},
+    {emx::K_MAXPOOL, nullptr, emx::launch_maxpool, "maxpool"},
+    {emx::K_QLINEAR_AVGPOOL, nullptr, emx::launch_qlinear_avgpool, "qlinear_avgpool"},
+    {emx::K_QLINEAR_SOFTMAX, nullptr, emx::launch_qlinear_softmax, "qlinear_softmax"},
     {emx::K_QLINEAR_MATMUL, emx::prepare_qmatmul, emx::launch_qmatmul, "qlinear_matmul"},
     {emx::K_MATMUL_INTEGER, emx::prepare_qmatmul, emx::launch_qmatmul, "matmul_integer"},
     {emx::K_CONV_F32, nullptr, emx::launch_conv_f32, "conv_f32"},

@@ -12,7 +12,9 @@ the same class names and the same fields for the ops this backend runs:
   GemmOp          ir/ops/nn.py:1624     UnaryOp       ir/ops/elementwise.py:538
   BinaryOp        ir/ops/elementwise.py:23
   MatMulNBitsOp   ir/ops/nn.py:1035     AttentionOp   ir/ops/nn.py:2478
-  LstmOp          ir/ops/nn.py:8449
+  LstmOp          ir/ops/nn.py:8449     ReshapeOp     ir/ops/misc.py:1995
+  TransposeOp     ir/ops/misc.py:1927   MaxPoolOp     ir/ops/nn.py:9614
+  QLinearAveragePoolOp ir/ops/nn.py:5454 QLinearSoftmaxOp ir/ops/nn.py:5997
 
 Attribute defaults follow the reference's lowerings (lowering/qlinear_conv.py:40,
 qlinear_add.py:31, gemm.py:9, matmul_nbits.py:120, attention.py:363 (scale
@@ -337,6 +339,128 @@ class DequantizeLinearOp:
     block_size: int | None
 
 
+@dataclass(frozen=True)
+class ReshapeOp:
+    input0: str
+    output: str
+
+
+@dataclass(frozen=True)
+class TransposeOp:
+    input0: str
+    output: str
+    perm: tuple[int, ...]
+
+
+@dataclass(frozen=True)
+class MaxPoolOp:
+    input0: str
+    output: str
+    indices: str | None
+    batch: int
+    channels: int
+    spatial_rank: int
+    in_spatial: tuple[int, ...]
+    out_spatial: tuple[int, ...]
+    kernel_shape: tuple[int, ...]
+    strides: tuple[int, ...]
+    pads: tuple[int, ...]
+    dilations: tuple[int, ...]
+    ceil_mode: bool
+    storage_order: int
+    dtype: ScalarType
+    indices_dtype: ScalarType | None
+
+
+@dataclass(frozen=True)
+class QLinearAveragePoolOp:
+    input0: str
+    input_scale: str
+    input_zero_point: str
+    output_scale: str
+    output_zero_point: str
+    output: str
+    batch: int
+    channels: int
+    in_h: int
+    in_w: int
+    out_h: int
+    out_w: int
+    kernel_h: int
+    kernel_w: int
+    dilation_h: int
+    dilation_w: int
+    stride_h: int
+    stride_w: int
+    pad_top: int
+    pad_left: int
+    pad_bottom: int
+    pad_right: int
+    count_include_pad: bool
+    input_dtype: ScalarType
+    dtype: ScalarType
+    input_scale_dtype: ScalarType
+    output_scale_dtype: ScalarType
+    input_scale_shape: tuple[int, ...]
+    output_scale_shape: tuple[int, ...]
+    input_zero_shape: tuple[int, ...]
+    output_zero_shape: tuple[int, ...]
+    spatial_rank: int = 2
+    channels_last: bool = False
+
+
+@dataclass(frozen=True)
+class QLinearSoftmaxOp:
+    input0: str
+    input_scale: str
+    input_zero_point: str
+    output_scale: str
+    output_zero_point: str
+    output: str
+    input_shape: tuple[int, ...]
+    output_shape: tuple[int, ...]
+    axis: int
+    outer: int
+    axis_size: int
+    inner: int
+    dtype: ScalarType
+    input_dtype: ScalarType
+    input_scale_dtype: ScalarType
+    output_scale_dtype: ScalarType
+
+
+def _auto_pads(a, in_spatial, ks, strides, dil) -> tuple[int, ...]:
+    """(begin..., end...) pads of a pooling node: explicit, or from auto_pad
+    (VALID: none; SAME_UPPER / SAME_LOWER: out = ceil(in / stride), the odd
+    pad at the end / the start), as lowering/maxpool.py:78-103 resolves them."""
+    rank = len(in_spatial)
+    mode = a.get("auto_pad", "NOTSET")
+    mode = mode.decode() if isinstance(mode, bytes) else str(mode)
+    if mode in ("", "NOTSET"):
+        return tuple(int(v) for v in a.get("pads", [0] * (2 * rank)))
+    if mode == "VALID":
+        return (0,) * (2 * rank)
+    if mode not in ("SAME_UPPER", "SAME_LOWER"):
+        raise UnsupportedOpError(f"auto_pad {mode} is not supported")
+    begin, end = [], []
+    for size, k, s, d in zip(in_spatial, ks, strides, dil):
+        need = max(0, (-(-size // s) - 1) * s + d * (k - 1) + 1 - size)
+        first = need // 2 if mode == "SAME_UPPER" else (need + 1) // 2
+        begin.append(first)
+        end.append(need - first)
+    return (*begin, *end)
+
+
+def _pool_out(size: int, k: int, s: int, d: int, p0: int, p1: int, ceil_mode: bool) -> int:
+    """Output extent of a pooling window (ONNX; with ceil_mode the last window
+    must start inside the input or its leading pad)."""
+    span = size + p0 + p1 - ((k - 1) * d + 1)
+    out = (-(-span // s) if ceil_mode else span // s) + 1
+    if ceil_mode and (out - 1) * s >= size + p0:
+        out -= 1
+    return out
+
+
 # ------------------------------------------------------------------ lowering
 def _st(suffix: str) -> ScalarType:
     return ScalarType(suffix)
@@ -355,8 +479,14 @@ def lower(spec: GraphSpec) -> LoweredModel:
         dtypes[name] = _st(t.dtype)
         consts.append(ConstTensor(name, tuple(arr.shape), arr, _st(t.dtype)))
     ops = []
-    for node in spec.nodes:
-        ops.append(_lower_node(node, shapes, dtypes))
+    _INITS.clear()
+    _INITS.update(spec.initializers)
+    _INITS["__opset__"] = np.int64(dict(spec.opset_imports).get("", 17))
+    try:
+        for node in spec.nodes:
+            ops.append(_lower_node(node, shapes, dtypes))
+    finally:
+        _INITS.clear()
     return LoweredModel(
         name=spec.name,
         input_names=tuple(t.name for t in spec.inputs),
@@ -369,6 +499,15 @@ def lower(spec: GraphSpec) -> LoweredModel:
         ops=tuple(ops),
         op_context=OpContext(shapes, dtypes),
     )
+
+
+_INITS: dict[str, np.ndarray] = {}  # the graph's initializers while lower() runs (Reshape reads its shape)
+
+
+def _initializer(name: str) -> np.ndarray:
+    if name not in _INITS:
+        raise UnsupportedOpError(f"'{name}' must be an initializer")
+    return _INITS[name]
 
 
 def _lower_node(node, shapes, dtypes):
@@ -536,4 +675,75 @@ def _lower_node(node, shapes, dtypes):
             direction=str(a.get("direction", "forward")), layout=int(a.get("layout", 0)),
             input_forget=int(a.get("input_forget", 0)), clip=a.get("clip"), activation_kinds=(2, 1, 1),
             dtype=dtypes[ins[0]])
+    if op == "Reshape":
+        shape_name = ins[1]
+        target = list(int(v) for v in np.asarray(_initializer(shape_name)).reshape(-1))
+        src = shapes[ins[0]]
+        out = [src[i] if v == 0 and not int(a.get("allowzero", 0)) else v for i, v in enumerate(target)]
+        if -1 in out:
+            known = int(np.prod([v for v in out if v != -1]))
+            out[out.index(-1)] = int(np.prod(src)) // max(known, 1)
+        y = node.outputs[0]
+        shapes[y] = tuple(out)
+        dtypes[y] = dtypes[ins[0]]
+        return ReshapeOp(input0=ins[0], output=y)
+    if op == "Transpose":
+        src = shapes[ins[0]]
+        perm = tuple(int(v) for v in a.get("perm", list(range(len(src)))[::-1]))
+        y = node.outputs[0]
+        shapes[y] = tuple(src[p_] for p_ in perm)
+        dtypes[y] = dtypes[ins[0]]
+        return TransposeOp(input0=ins[0], output=y, perm=perm)
+    if op in ("MaxPool", "QLinearAveragePool"):
+        x = ins[0]
+        n, c, *sp = shapes[x]
+        rank = len(sp)
+        ks = tuple(int(v) for v in a["kernel_shape"])
+        strides = tuple(int(v) for v in a.get("strides", [1] * rank))
+        dil = tuple(int(v) for v in a.get("dilations", [1] * rank))
+        pads = _auto_pads(a, tuple(sp), ks, strides, dil)
+        ceil_mode = bool(int(a.get("ceil_mode", 0)))
+        out_sp = tuple(_pool_out(sp[i], ks[i], strides[i], dil[i], pads[i], pads[i + rank], ceil_mode)
+                       for i in range(rank))
+        y = node.outputs[0]
+        shapes[y] = (n, c, *out_sp)
+        if op == "MaxPool":
+            dtypes[y] = dtypes[x]
+            return MaxPoolOp(input0=x, output=y, indices=node.outputs[1] if len(node.outputs) > 1 else None,
+                             batch=n, channels=c, spatial_rank=rank, in_spatial=tuple(sp), out_spatial=out_sp,
+                             kernel_shape=ks, strides=strides, pads=pads, dilations=dil, ceil_mode=ceil_mode,
+                             storage_order=int(a.get("storage_order", 0)), dtype=dtypes[x], indices_dtype=None)
+        if rank != 2:
+            raise UnsupportedOpError("QLinearAveragePool: only 2-D pooling has a B200 kernel")
+        dtypes[y] = dtypes[ins[4]]
+        return QLinearAveragePoolOp(
+            input0=x, input_scale=ins[1], input_zero_point=ins[2], output_scale=ins[3], output_zero_point=ins[4],
+            output=y, batch=n, channels=c, in_h=sp[0], in_w=sp[1], out_h=out_sp[0], out_w=out_sp[1],
+            kernel_h=ks[0], kernel_w=ks[1], dilation_h=dil[0], dilation_w=dil[1], stride_h=strides[0],
+            stride_w=strides[1], pad_top=pads[0], pad_left=pads[1], pad_bottom=pads[2], pad_right=pads[3],
+            count_include_pad=bool(int(a.get("count_include_pad", 0))), input_dtype=dtypes[x], dtype=dtypes[y],
+            input_scale_dtype=dtypes[ins[1]], output_scale_dtype=dtypes[ins[3]],
+            input_scale_shape=shapes[ins[1]], output_scale_shape=shapes[ins[3]],
+            input_zero_shape=shapes[ins[2]], output_zero_shape=shapes[ins[4]],
+            channels_last=bool(int(a.get("channels_last", 0))))
+    if op == "QLinearSoftmax":
+        src = shapes[ins[0]]
+        opset = int(a["opset"]) if "opset" in a else int(_INITS["__opset__"])
+        legacy = opset < 13
+        axis = int(a["axis"]) if "axis" in a else (1 if legacy else -1)
+        if axis < 0:
+            axis += len(src)
+        outer = int(np.prod(src[:axis], dtype=np.int64))
+        if legacy:
+            axis_size, inner = int(np.prod(src[axis:], dtype=np.int64)), 1
+        else:
+            axis_size, inner = src[axis], int(np.prod(src[axis + 1:], dtype=np.int64))
+        y = node.outputs[0]
+        shapes[y] = src
+        dtypes[y] = dtypes[ins[4]]
+        return QLinearSoftmaxOp(
+            input0=ins[0], input_scale=ins[1], input_zero_point=ins[2], output_scale=ins[3],
+            output_zero_point=ins[4], output=y, input_shape=src, output_shape=src, axis=axis, outer=outer,
+            axis_size=axis_size, inner=inner, dtype=dtypes[y], input_dtype=dtypes[ins[0]],
+            input_scale_dtype=dtypes[ins[1]], output_scale_dtype=dtypes[ins[3]])
     raise UnsupportedOpError(f"{op} has no B200 kernel")

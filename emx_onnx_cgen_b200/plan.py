@@ -181,6 +181,28 @@ def qadd_table(c_signed: bool, c_zero: int, c_scale, r_signed: bool, r_zero: int
     return (r & 0xFF).astype(np.uint8).reshape(-1)
 
 
+def qsoftmax_exp_table(x_signed: bool, x_zero: int, x_scale) -> np.ndarray:
+    """[256][256] f32: expf(v(b) - v(bm)) for raw bytes b, bm, where v(q) =
+    (float)(q - zx) * xs.  Evaluated once with the C library's expf -- the
+    function the reference's generated C calls (templates/qlinear_softmax_op.c.j2)
+    -- so the kernel's exp values are the reference's bit for bit; a device
+    exp is correctly rounded and differs from glibc's expf in about 1e-4 of
+    arguments."""
+    import ctypes
+    import ctypes.util
+    libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+    expf = libm.expf
+    expf.restype, expf.argtypes = ctypes.c_float, [ctypes.c_float]
+    q = np.arange(256, dtype=np.int32)
+    if x_signed:
+        q = q.astype(np.uint8).view(np.int8).astype(np.int32)
+    v = (q - np.int32(x_zero)).astype(np.float32) * np.float32(x_scale)
+    args = (v[:, None] - v[None, :]).astype(np.float32)
+    uniq, inv = np.unique(args.view(np.uint32), return_inverse=True)
+    vals = np.array([expf(float(a)) for a in uniq.view(np.float32)], dtype=np.float32)
+    return vals[inv].reshape(256, 256)
+
+
 def swizzle_positions(rows: int, row_bytes: int) -> np.ndarray:
     """[rows, row_bytes // 16]: position of 16-byte chunk j of row r in the
     tensor-core K-major swizzle of a row_bytes-wide row (same rule as
@@ -618,7 +640,8 @@ class B200PlanEmitter:
             "MatMulNBitsOp": ("input0",), "AttentionOp": ("input_q", "input_k", "input_v"),
             "LstmOp": ("input_x",), "QLinearMatMulOp": ("input0", "input1"), "MatMulIntegerOp": ("input0", "input1"),
             "ConvOp": ("input0", "weights", "bias"), "SoftmaxOp": ("input0",), "QuantizeLinearOp": ("input0",),
-            "DequantizeLinearOp": ("input0",),
+            "DequantizeLinearOp": ("input0",), "ReshapeOp": ("input0",), "TransposeOp": ("input0",),
+            "MaxPoolOp": ("input0",), "QLinearAveragePoolOp": ("input0",), "QLinearSoftmaxOp": ("input0",),
         }.get(_name(op), ())
         return [getattr(op, f) for f in fields if getattr(op, f, None)]
 
@@ -850,10 +873,20 @@ class B200PlanEmitter:
             i = j + 1
 
     # ------------------------------------------------------------------ QLinearAdd (standalone)
+    def _broadcast_operand(self, name: str, shape, out_shape) -> int:
+        """Tensor id of operand ``name`` at the output's shape: the tensor itself,
+        or an initializer broadcast once by the planner (a bias row added to
+        every batch entry)."""
+        if tuple(shape) == tuple(out_shape):
+            return self._src(name)
+        if name not in self._consts:
+            raise UnsupportedOpError("QLinearAdd: only initializer operands may broadcast")
+        full = np.ascontiguousarray(np.broadcast_to(self._consts[name].reshape(shape), tuple(out_shape)))
+        return self._b.weight(full, self._dtype(name), f"{name}:broadcast")
+
     def _emit_QLinearAddOp(self, i, op):
-        if tuple(op.input0_shape) != tuple(op.input1_shape):
-            raise UnsupportedOpError("QLinearAdd: broadcasting operands have no B200 kernel")
-        a, b_ = self._src(op.input0), self._src(op.input1)
+        a = self._broadcast_operand(op.input0, op.input0_shape, op.output_shape)
+        b_ = self._broadcast_operand(op.input1, op.input1_shape, op.output_shape)
         y = self._dest(op.output, _suffix(op.dtype), op.output_shape)
         count = int(np.prod(op.output_shape))
         batched = self._batch > 0 and len(op.output_shape) > 0 and op.output_shape[0] == self._batch
@@ -1071,6 +1104,111 @@ class B200PlanEmitter:
         self._b.op(K.K_SOFTMAX_F32, [x, y], {K.SM_OUTER: outer, K.SM_AXIS: shape[ax], K.SM_INNER: inner,
                                              K.SM_OUTER_PER_BATCH: outer // self._batch if batched else 0},
                    label=f"{op.output} (Softmax fp32)", batched=batched)
+
+    # ------------------------------------------------------------------ layout and pooling
+    def _emit_ReshapeOp(self, i, op):
+        """The same bytes under another shape: an alias of the source tensor,
+        a byte copy only when the result is a graph output."""
+        src = self._src(op.input0)
+        if op.output not in self._graph_outputs:
+            self._nchw[op.output] = src
+            return
+        shape = tuple(self._shape(op.output))
+        nbytes = int(np.prod(shape)) * np.dtype(NP[self._dtype(op.output)]).itemsize
+        y = self._dest(op.output, self._dtype(op.output), shape)
+        batched = (self._batch > 0 and len(shape) > 0 and shape[0] == self._batch
+                   and self._is_batched(op.input0))
+        self._b.op(K.K_COPY, [src, y], {K.CP_BYTES: nbytes, K.CP_BATCH: self._batch if batched else 0},
+                   label=f"{op.output} (Reshape)", batched=batched)
+
+    def _emit_TransposeOp(self, i, op):
+        dt = self._dtype(op.input0)
+        elem = np.dtype(NP[dt]).itemsize
+        if elem not in (1, 2, 4):
+            raise UnsupportedOpError(f"Transpose of {dt} has no B200 kernel")
+        shape = tuple(self._shape(op.input0))
+        rank = len(shape)
+        if rank > 6:
+            raise UnsupportedOpError("Transpose: rank above 6 has no B200 kernel")
+        perm = tuple(int(p_) for p_ in op.perm)
+        strides = [int(np.prod(shape[j + 1:])) for j in range(rank)]
+        out_shape = tuple(shape[p_] for p_ in perm)
+        pad = 6 - rank
+        ip = {K.TR_ELEM: elem, K.TR_BATCH_AXIS: -1}
+        for j in range(6):
+            ip[K.TR_D0 + j] = out_shape[j - pad] if j >= pad else 1
+            ip[K.TR_S0 + j] = strides[perm[j - pad]] if j >= pad else 0
+        batched = (self._batch > 0 and rank > 0 and perm[0] == 0 and shape[0] == self._batch
+                   and self._is_batched(op.input0))
+        if batched:
+            ip[K.TR_BATCH_AXIS] = pad
+        x = self._src(op.input0)
+        y = self._dest(op.output, dt, out_shape)
+        self._b.op(K.K_TRANSPOSE, [x, y], ip, label=f"{op.output} (Transpose {perm})", batched=batched)
+
+    def _pool_ip(self, op, kh, kw, sh, sw, dh, dw, pt, pl, oh, ow, xdt, ydt) -> dict:
+        n, c, h, w = self._shape(op.input0)
+        return {K.PL_N: n, K.PL_C: c, K.PL_H: h, K.PL_W: w, K.PL_OH: oh, K.PL_OW: ow, K.PL_KH: kh, K.PL_KW: kw,
+                K.PL_SH: sh, K.PL_SW: sw, K.PL_DH: dh, K.PL_DW: dw, K.PL_PT: pt, K.PL_PL: pl,
+                K.PL_X_SIGNED: int(xdt == "i8"), K.PL_Y_SIGNED: int(ydt == "i8")}
+
+    def _emit_MaxPoolOp(self, i, op):
+        dt = self._dtype(op.input0)
+        if dt not in ("u8", "i8"):
+            raise UnsupportedOpError(f"MaxPool on {dt} has no B200 kernel (8-bit only)")
+        if op.spatial_rank != 2 or op.indices:
+            raise UnsupportedOpError("MaxPool: 2-D pooling without the indices output only")
+        ip = self._pool_ip(op, *op.kernel_shape, *op.strides, *op.dilations, op.pads[0], op.pads[1],
+                           *op.out_spatial, dt, dt)
+        x = self._src(op.input0)
+        y = self._dest(op.output, dt, (op.batch, op.channels, *op.out_spatial))
+        self._b.op(K.K_MAXPOOL, [x, y], ip, label=f"{op.output} (MaxPool)",
+                   batched=op.batch == self._batch and self._is_batched(op.input0))
+
+    def _emit_QLinearAveragePoolOp(self, i, op):
+        xdt, ydt = self._dtype(op.input0), self._dtype(op.output)
+        if xdt not in ("u8", "i8") or ydt not in ("u8", "i8") or op.channels_last:
+            raise UnsupportedOpError("QLinearAveragePool: 8-bit NCHW only")
+        if _suffix(op.input_scale_dtype) != "f32" or _suffix(op.output_scale_dtype) != "f32":
+            raise UnsupportedOpError("QLinearAveragePool: fp32 scales only")
+        xs = np.float32(self._scalar(op.input_scale, "x_scale"))
+        ys = np.float32(self._scalar(op.output_scale, "y_scale"))
+        ip = self._pool_ip(op, op.kernel_h, op.kernel_w, op.stride_h, op.stride_w, op.dilation_h, op.dilation_w,
+                           op.pad_top, op.pad_left, op.out_h, op.out_w, xdt, ydt)
+        ip.update({K.PL_COUNT_PAD: int(op.count_include_pad),
+                   K.PL_X_ZERO: int(self._scalar(op.input_zero_point, "x_zero_point")),
+                   K.PL_Y_ZERO: int(self._scalar(op.output_zero_point, "y_zero_point"))})
+        x = self._src(op.input0)
+        y = self._dest(op.output, ydt, (op.batch, op.channels, op.out_h, op.out_w))
+        self._b.op(K.K_QLINEAR_AVGPOOL, [x, y], ip, {K.PLF_SCALE: float(np.float32(xs / ys))},
+                   label=f"{op.output} (QLinearAveragePool)",
+                   batched=op.batch == self._batch and self._is_batched(op.input0))
+
+    def _emit_QLinearSoftmaxOp(self, i, op):
+        xdt, ydt = self._dtype(op.input0), self._dtype(op.output)
+        if xdt not in ("u8", "i8") or ydt != xdt:
+            raise UnsupportedOpError("QLinearSoftmax: 8-bit only")
+        if _suffix(op.input_scale_dtype) != "f32" or _suffix(op.output_scale_dtype) != "f32":
+            raise UnsupportedOpError("QLinearSoftmax: fp32 scales only")
+        xs = np.float32(self._scalar(op.input_scale, "x_scale"))
+        ys = np.float32(self._scalar(op.output_scale, "y_scale"))
+        if not np.isfinite(xs):
+            raise UnsupportedOpError("QLinearSoftmax: x_scale must be finite")
+        zx = int(self._scalar(op.input_zero_point, "x_zero_point"))
+        table = self._b.weight(qsoftmax_exp_table(xdt == "i8", zx, xs), "f32", f"{op.output}:expf-table")
+        # ONNX Runtime's floored reciprocal of the output scale, in float
+        y_inv = np.floor(np.float32(1.0) / ys).astype(np.float32)
+        shape = tuple(op.input_shape)
+        batched = (self._batch > 0 and op.axis == 1 and op.outer == self._batch and op.inner == 1
+                   and self._is_batched(op.input0))
+        x = self._src(op.input0)
+        y = self._dest(op.output, ydt, shape)
+        self._b.op(K.K_QLINEAR_SOFTMAX, [x, y, table], {
+            K.QS_OUTER: op.outer, K.QS_AXIS: op.axis_size, K.QS_INNER: op.inner, K.QS_X_SIGNED: int(xdt == "i8"),
+            K.QS_Y_SIGNED: int(ydt == "i8"), K.QS_X_ZERO: zx,
+            K.QS_Y_ZERO: int(self._scalar(op.output_zero_point, "y_zero_point"))},
+            {K.QSF_X_SCALE: float(xs), K.QSF_Y_INV: float(y_inv)}, label=f"{op.output} (QLinearSoftmax)",
+            batched=batched)
 
     # ------------------------------------------------------------------ Quantize / Dequantize
     def _emit_quant(self, op, quantize: bool):

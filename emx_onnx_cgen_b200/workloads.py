@@ -414,6 +414,92 @@ def quant_dequant(shape: tuple[int, ...] = (16, 64), out_dtype: str = "u8", zero
                     dict(shape=tuple(shape), out_dtype=out_dtype, zero=zero, scale=scale))
 
 
+def _bytes(rng, shape, dtype: str) -> np.ndarray:
+    """8-bit tensor uniform over its whole range."""
+    lo, hi = (-128, 128) if dtype == "i8" else (0, 256)
+    return rng.integers(lo, hi, size=shape).astype(np.int8 if dtype == "i8" else np.uint8)
+
+
+def pool8(shape: tuple[int, ...] = (2, 8, 13, 11), kind: str = "max", kernel: tuple[int, int] = (3, 2),
+          strides: tuple[int, int] = (2, 1), pads: tuple[int, ...] = (1, 0, 1, 1), dilations: tuple[int, int] = (1, 1),
+          ceil_mode: int = 0, count_include_pad: int = 0, auto_pad: str | None = None, dtype: str = "i8",
+          y_dtype: str | None = None, x_scale: float = 0.05, x_zero: int = -3, y_scale: float = 0.04,
+          y_zero: int = 5) -> Workload:
+    """One 2-D pooling node on an 8-bit NCHW tensor: MaxPool (kind "max") or
+    com.microsoft QLinearAveragePool (kind "avg", per-tensor scales and zero
+    points)."""
+    from .lowering import _auto_pads, _pool_out
+    y_dtype = y_dtype or dtype
+    attrs = {"kernel_shape": list(kernel), "strides": list(strides)}
+    if auto_pad:
+        attrs["auto_pad"] = auto_pad
+    else:
+        attrs["pads"] = list(pads)
+    if tuple(dilations) != (1, 1):
+        attrs["dilations"] = list(dilations)
+    if ceil_mode:
+        attrs["ceil_mode"] = 1
+    pd = _auto_pads(attrs, shape[2:], kernel, strides, dilations)
+    out = (shape[0], shape[1], *(_pool_out(shape[2 + i], kernel[i], strides[i], dilations[i], pd[i], pd[i + 2],
+                                           bool(ceil_mode)) for i in range(2)))
+    npt = lambda d: np.int8 if d == "i8" else np.uint8
+    if kind == "max":
+        node = NodeSpec("MaxPool", "pool", ("X",), ("Y",), attrs)
+        inits, y_dtype = {}, dtype
+    else:
+        if count_include_pad:
+            attrs["count_include_pad"] = 1
+        inits = {"xs": _scalar(x_scale, np.float32), "xz": _scalar(x_zero, npt(dtype)),
+                 "ys": _scalar(y_scale, np.float32), "yz": _scalar(y_zero, npt(y_dtype))}
+        node = NodeSpec("QLinearAveragePool", "pool", ("X", "xs", "xz", "ys", "yz"), ("Y",), attrs, "com.microsoft")
+    g = GraphSpec(name=f"{kind}pool8", inputs=[TensorSpec("X", dtype, tuple(shape))],
+                  outputs=[TensorSpec("Y", y_dtype, out)], nodes=[node], initializers=inits,
+                  opset_imports=(("", 13), ("com.microsoft", 1)))
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"X": _bytes(np.random.default_rng(seed), shape, dtype)}
+
+    return Workload(f"{kind}pool8", g, make_inputs, {"X": 0, "Y": 0}, dict(shape=tuple(shape), kind=kind))
+
+
+def qlinear_softmax8(shape: tuple[int, ...] = (6, 37), axis: int = -1, dtype: str = "u8", x_scale: float = 0.08,
+                     x_zero: int = 128, y_scale: float = 1.0 / 256, y_zero: int = 0, opset: int = 13) -> Workload:
+    """com.microsoft QLinearSoftmax on an 8-bit tensor (opset < 13: the
+    flattened [outer, rest] semantics)."""
+    npt = np.int8 if dtype == "i8" else np.uint8
+    inits = {"xs": _scalar(x_scale, np.float32), "xz": _scalar(x_zero, npt), "ys": _scalar(y_scale, np.float32),
+             "yz": _scalar(y_zero, npt)}
+    g = GraphSpec(name="qlinear_softmax8", inputs=[TensorSpec("X", dtype, tuple(shape))],
+                  outputs=[TensorSpec("Y", dtype, tuple(shape))],
+                  nodes=[NodeSpec("QLinearSoftmax", "sm", ("X", "xs", "xz", "ys", "yz"), ("Y",),
+                                  {"axis": axis, "opset": opset}, "com.microsoft")],
+                  initializers=inits, opset_imports=(("", 13), ("com.microsoft", 1)))
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        return {"X": _bytes(np.random.default_rng(seed), shape, dtype)}
+
+    return Workload("qlinear_softmax8", g, make_inputs, {"X": 0, "Y": 0}, dict(shape=tuple(shape), axis=axis))
+
+
+def transpose(shape: tuple[int, ...] = (2, 3, 4, 5), perm: tuple[int, ...] = (0, 2, 3, 1),
+              dtype: str = "f32") -> Workload:
+    """Transpose of one tensor (Y = X.transpose(perm)), any element type."""
+    out = tuple(shape[p] for p in perm)
+    g = GraphSpec(name="transpose", inputs=[TensorSpec("X", dtype, tuple(shape))],
+                  outputs=[TensorSpec("Y", dtype, out)],
+                  nodes=[NodeSpec("Transpose", "t", ("X",), ("Y",), {"perm": list(perm)})],
+                  initializers={}, opset_imports=(("", 13),))
+
+    def make_inputs(seed: int = 0) -> dict[str, np.ndarray]:
+        rng = np.random.default_rng(seed)
+        if dtype in ("u8", "i8"):
+            return {"X": _bytes(rng, shape, dtype)}
+        return {"X": rng.standard_normal(shape).astype(np.float16 if dtype == "f16" else np.float32)}
+
+    return Workload("transpose", g, make_inputs, {"X": 0, "Y": 0} if perm[0] == 0 else {},
+                    dict(shape=tuple(shape), perm=tuple(perm)))
+
+
 BUILDERS = {
     "mlp_fp32": mlp_fp32,
     "qconv_stack_int8": qconv_stack_int8,
@@ -427,4 +513,7 @@ BUILDERS = {
     "conv_f32": conv_f32,
     "softmax_f32": softmax_f32,
     "quant_dequant": quant_dequant,
+    "pool8": pool8,
+    "qlinear_softmax8": qlinear_softmax8,
+    "transpose": transpose,
 }

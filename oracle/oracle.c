@@ -522,3 +522,99 @@ void orc_dequantize_linear(const uint8_t *x, int x_signed, const float *scale, c
                 y[idx] = (xv - z) * scale[a];
             }
 }
+
+/* ---------------------------------------------------------------------------
+ * MaxPool, 2-D NCHW, 8-bit, no indices (templates/maxpool_op.c.j2:30-66):
+ * start from the type's minimum, max over the in-bounds taps.
+ * ------------------------------------------------------------------------- */
+void orc_maxpool8(const uint8_t *x, uint8_t *y, int is_signed, long n, long c, long h, long w, long oh, long ow,
+                  long kh, long kw, long sh, long sw, long dh, long dw, long pt, long pl)
+{
+    for (long b = 0; b < n * c; ++b)
+        for (long oy = 0; oy < oh; ++oy)
+            for (long ox = 0; ox < ow; ++ox) {
+                int m = is_signed ? INT8_MIN : 0;
+                for (long ky = 0; ky < kh; ++ky) {
+                    const long iy = oy * sh + ky * dh - pt;
+                    if (iy < 0 || iy >= h) continue;
+                    for (long kx = 0; kx < kw; ++kx) {
+                        const long ix = ox * sw + kx * dw - pl;
+                        if (ix < 0 || ix >= w) continue;
+                        const uint8_t raw = x[(b * h + iy) * w + ix];
+                        const int v = is_signed ? (int)(int8_t)raw : (int)raw;
+                        m = v > m ? v : m;
+                    }
+                }
+                y[(b * oh + oy) * ow + ox] = (uint8_t)m;
+            }
+}
+
+/* ---------------------------------------------------------------------------
+ * QLinearAveragePool, 2-D NCHW, float compute (templates/qlinear_average_pool_op.c.j2:1-3,
+ * :165-189): int32 sum of (x - zx) over the in-bounds taps, denominator the tap
+ * count (or KH*KW with count_include_pad), mean = (float)acc / (float)denom,
+ * y = clamp((int32_t)roundf(mean * scale) + zy), scale = (float)xs / (float)ys.
+ * ------------------------------------------------------------------------- */
+void orc_qavgpool8(const uint8_t *x, uint8_t *y, int x_signed, int y_signed, long n, long c, long h, long w,
+                   long oh, long ow, long kh, long kw, long sh, long sw, long dh, long dw, long pt, long pl,
+                   int count_include_pad, float x_scale, int x_zero, float y_scale, int y_zero)
+{
+    const float scale = ((float)x_scale) / ((float)y_scale);
+    const int lo = y_signed ? INT8_MIN : 0, hi = y_signed ? INT8_MAX : UINT8_MAX;
+    for (long b = 0; b < n * c; ++b)
+        for (long oy = 0; oy < oh; ++oy)
+            for (long ox = 0; ox < ow; ++ox) {
+                int32_t acc = 0;
+                long count = 0;
+                for (long ky = 0; ky < kh; ++ky) {
+                    const long iy = oy * sh + ky * dh - pt;
+                    for (long kx = 0; kx < kw; ++kx) {
+                        const long ix = ox * sw + kx * dw - pl;
+                        if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+                            const uint8_t raw = x[(b * h + iy) * w + ix];
+                            acc += (x_signed ? (int32_t)(int8_t)raw : (int32_t)raw) - x_zero;
+                            ++count;
+                        } else if (count_include_pad) {
+                            ++count;
+                        }
+                    }
+                }
+                const long denom = count_include_pad ? kh * kw : count;
+                float mean = (denom > 0) ? (((float)acc) / (float)denom) : (float)0;
+                int32_t r = (int32_t)roundf(mean * scale) + y_zero;
+                r = r < lo ? lo : r;
+                r = r > hi ? hi : r;
+                y[(b * oh + oy) * ow + ox] = (uint8_t)r;
+            }
+}
+
+/* ---------------------------------------------------------------------------
+ * QLinearSoftmax, 8-bit (templates/qlinear_softmax_op.c.j2:1-54): v = (float)(x - zx)
+ * * xs, max with fmaxf, sum of expf(v - max) in axis order, y = clamp(nearbyintf(
+ * (expf(v - max) * inv) / sum) + zy) with inv = floorf(1 / ys).
+ * ------------------------------------------------------------------------- */
+void orc_qsoftmax8(const uint8_t *x, uint8_t *y, int x_signed, int y_signed, long outer, long axis, long inner,
+                   float x_scale, int x_zero, float y_scale, int y_zero)
+{
+    const float zy = (float)y_zero;
+    const float lo = y_signed ? (float)INT8_MIN : 0.0f, hi = y_signed ? (float)INT8_MAX : (float)UINT8_MAX;
+    const float inv = floorf((float)1 / y_scale);
+#define ORC_QS_V(i) (((float)((x_signed ? (int32_t)(int8_t)x[i] : (int32_t)x[i]) - x_zero)) * x_scale)
+    for (long o = 0; o < outer; ++o)
+        for (long in = 0; in < inner; ++in) {
+            const long base = o * axis * inner + in;
+            float mx = ORC_QS_V(base);
+            for (long a = 1; a < axis; ++a) mx = fmaxf(mx, ORC_QS_V(base + a * inner));
+            float sum = (float)0;
+            for (long a = 0; a < axis; ++a) sum += expf(ORC_QS_V(base + a * inner) - mx);
+            for (long a = 0; a < axis; ++a) {
+                const float e = expf(ORC_QS_V(base + a * inner) - mx);
+                const float scaled = (e * inv) / sum;
+                float r = nearbyintf(scaled) + zy;
+                r = fmaxf(r, lo);
+                r = fminf(r, hi);
+                y[base + a * inner] = y_signed ? (uint8_t)(int8_t)r : (uint8_t)r;
+            }
+        }
+#undef ORC_QS_V
+}

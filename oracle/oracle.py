@@ -65,14 +65,91 @@ def qlinear_conv2d(x, xs, xz, w, ws, wz, ys, yz, bias, strides=(1, 1), pads=(0, 
 
 
 def qlinear_add(a, a_s, a_z, b, b_s, b_z, y_s, y_z, y_dtype=np.uint8):
-    a = np.ascontiguousarray(a); b = np.ascontiguousarray(b)
-    assert a.shape == b.shape
+    """Multidirectional broadcast as the reference's loop nest indexes it
+    (templates/qlinear_add_op.c.j2): both operands at the output shape."""
+    shape = np.broadcast_shapes(a.shape, b.shape)
+    a = np.ascontiguousarray(np.broadcast_to(a, shape)); b = np.ascontiguousarray(np.broadcast_to(b, shape))
     y = np.zeros(a.shape, dtype=y_dtype)
     lib().orc_qlinear_add(_p(a), _i(a.dtype == np.int8), _f(float(np.float32(a_s))), _i(int(a_z)),
                           _p(b), _i(b.dtype == np.int8), _f(float(np.float32(b_s))), _i(int(b_z)),
                           _f(float(np.float32(y_s))), _i(int(y_z)), _p(y), _i(y.dtype == np.int8),
                           _sz(a.size))
     return y
+
+
+def _pool_geometry(x, a):
+    """(kernel, strides, dilations, pads, out) of a 2-D pooling node, ONNX rules."""
+    ks = [int(v) for v in a["kernel_shape"]]
+    st = [int(v) for v in a.get("strides", [1, 1])]
+    dl = [int(v) for v in a.get("dilations", [1, 1])]
+    mode = a.get("auto_pad", "NOTSET")
+    mode = mode.decode() if isinstance(mode, bytes) else str(mode)
+    if mode in ("SAME_UPPER", "SAME_LOWER"):
+        pd = [0, 0, 0, 0]
+        for i in range(2):
+            need = max(0, (-(-x.shape[2 + i] // st[i]) - 1) * st[i] + dl[i] * (ks[i] - 1) + 1 - x.shape[2 + i])
+            pd[i] = need // 2 if mode == "SAME_UPPER" else (need + 1) // 2
+            pd[i + 2] = need - pd[i]
+    elif mode == "VALID":
+        pd = [0, 0, 0, 0]
+    else:
+        pd = [int(v) for v in a.get("pads", [0, 0, 0, 0])]
+    ceil_mode = bool(int(a.get("ceil_mode", 0)))
+    out = []
+    for i in range(2):
+        span = x.shape[2 + i] + pd[i] + pd[i + 2] - ((ks[i] - 1) * dl[i] + 1)
+        o = (-(-span // st[i]) if ceil_mode else span // st[i]) + 1
+        if ceil_mode and (o - 1) * st[i] >= x.shape[2 + i] + pd[i]:
+            o -= 1
+        out.append(o)
+    return ks, st, dl, pd, out
+
+
+def maxpool8(x, a):
+    ks, st, dl, pd, (oh, ow) = _pool_geometry(x, a)
+    x = np.ascontiguousarray(x)
+    n, c, h, w = x.shape
+    y = np.zeros((n, c, oh, ow), dtype=x.dtype)
+    lib().orc_maxpool8(_p(x), _p(y), _i(x.dtype == np.int8), *(ctypes.c_long(v) for v in
+                       (n, c, h, w, oh, ow, ks[0], ks[1], st[0], st[1], dl[0], dl[1], pd[0], pd[1])))
+    return y
+
+
+def qlinear_avgpool8(x, xs, xz, ys, yz, a):
+    ks, st, dl, pd, (oh, ow) = _pool_geometry(x, a)
+    x = np.ascontiguousarray(x)
+    n, c, h, w = x.shape
+    y = np.zeros((n, c, oh, ow), dtype=np.asarray(yz).dtype)
+    lib().orc_qavgpool8(_p(x), _p(y), _i(x.dtype == np.int8), _i(y.dtype == np.int8),
+                        *(ctypes.c_long(v) for v in (n, c, h, w, oh, ow, ks[0], ks[1], st[0], st[1], dl[0], dl[1],
+                                                     pd[0], pd[1])),
+                        _i(int(a.get("count_include_pad", 0))), _f(float(np.float32(np.asarray(xs).reshape(-1)[0]))),
+                        _i(int(np.asarray(xz).reshape(-1)[0])), _f(float(np.float32(np.asarray(ys).reshape(-1)[0]))),
+                        _i(int(np.asarray(yz).reshape(-1)[0])))
+    return y
+
+
+def qlinear_softmax8(x, xs, xz, ys, yz, axis, legacy):
+    x = np.ascontiguousarray(x)
+    ax = axis % x.ndim
+    outer = int(np.prod(x.shape[:ax]))
+    if legacy:
+        n_axis, inner = int(np.prod(x.shape[ax:])), 1
+    else:
+        n_axis, inner = x.shape[ax], int(np.prod(x.shape[ax + 1:]))
+    y = np.zeros(x.shape, dtype=np.asarray(yz).dtype)
+    lib().orc_qsoftmax8(_p(x), _p(y), _i(x.dtype == np.int8), _i(y.dtype == np.int8), ctypes.c_long(outer),
+                        ctypes.c_long(n_axis), ctypes.c_long(inner),
+                        _f(float(np.float32(np.asarray(xs).reshape(-1)[0]))), _i(int(np.asarray(xz).reshape(-1)[0])),
+                        _f(float(np.float32(np.asarray(ys).reshape(-1)[0]))), _i(int(np.asarray(yz).reshape(-1)[0])))
+    return y
+
+
+def reshape(x, shape, allowzero=0):
+    """templates/reshape_op.c.j2: the same elements in row-major order."""
+    tgt = [int(v) for v in np.asarray(shape).reshape(-1)]
+    tgt = [x.shape[i] if v == 0 and not allowzero else v for i, v in enumerate(tgt)]
+    return np.ascontiguousarray(x).reshape(tgt)
 
 
 def gemm_f32(a, b, c=None, trans_a=0, trans_b=0, alpha=1.0, beta=1.0):
@@ -307,6 +384,19 @@ def run_graph(spec: GraphSpec, inputs: dict[str, np.ndarray]) -> dict[str, np.nd
             res = [dequantize_linear(ins[0], ins[1], ins[2] if len(ins) > 2 else None, a.get("axis"))]
         elif op == "Attention":
             res = [attention_f16(ins[0], ins[1], ins[2], a.get("scale"), bool(a.get("is_causal", 0)))]
+        elif op == "Reshape":
+            res = [reshape(ins[0], ins[1], int(a.get("allowzero", 0)))]
+        elif op == "Transpose":
+            res = [np.ascontiguousarray(np.transpose(ins[0], a.get("perm")))]
+        elif op == "MaxPool":
+            res = [maxpool8(ins[0], a)]
+        elif op == "QLinearAveragePool":
+            res = [qlinear_avgpool8(ins[0], ins[1], ins[2], ins[3], ins[4], a)]
+        elif op == "QLinearSoftmax":
+            opset = int(a["opset"]) if "opset" in a else dict(spec.opset_imports).get("", 17)
+            legacy = opset < 13
+            res = [qlinear_softmax8(ins[0], ins[1], ins[2], ins[3], ins[4],
+                                    int(a["axis"]) if "axis" in a else (1 if legacy else -1), legacy)]
         elif op == "LSTM":
             res = list(lstm_f32(ins[0], ins[1][0], ins[2][0], ins[3][0] if len(ins) > 3 else None))
         else:

@@ -1,6 +1,7 @@
 """Generate the golden input/output vectors in this directory.
 
-Each case builds a small instance of one workload graph, has the REFERENCE
+Each case builds a small instance of one workload graph (or reads one of the
+reference's own test models), has the REFERENCE
 compiler (imported from its source tree through the test-only onnx shim in
 ``oracle/onnx_shim.py``) lower it and emit C, compiles that C with
 ``gcc -std=c99 -O2`` and runs it on seeded inputs.  The graph's initializers,
@@ -71,7 +72,99 @@ CASES = [
     ("softmax_3x5x6_axis1", "softmax_f32", dict(shape=(3, 5, 6), axis=1), 1),
     ("qdq_u8_6x11", "quant_dequant", dict(shape=(6, 11)), 0),
     ("qdq_i8_4x9", "quant_dequant", dict(shape=(4, 9), out_dtype="i8", zero=-3, scale=0.05), 1),
+    ("maxpool_i8_2x8x13x11_k3x2_s2x1", "pool8", dict(), 0),
+    ("maxpool_u8_1x4x9x9_d2_ceil", "pool8",
+     dict(shape=(1, 4, 9, 9), kernel=(3, 3), strides=(2, 2), pads=(1, 1, 0, 0), dilations=(2, 2), ceil_mode=1,
+          dtype="u8"), 1),
+    ("maxpool_i8_same_upper", "pool8",
+     dict(shape=(2, 3, 10, 7), kernel=(4, 3), strides=(3, 2), auto_pad="SAME_UPPER"), 2),
+    ("qavgpool_i8_2x8x13x11_k3x2", "pool8", dict(kind="avg"), 0),
+    ("qavgpool_u8_pad_count", "pool8",
+     dict(shape=(2, 5, 12, 10), kind="avg", kernel=(3, 3), strides=(2, 2), pads=(1, 1, 1, 1),
+          count_include_pad=1, dtype="u8", x_zero=128, y_zero=120, x_scale=0.02, y_scale=0.015), 1),
+    ("qavgpool_i8_to_u8_ceil", "pool8",
+     dict(shape=(1, 6, 11, 9), kind="avg", kernel=(2, 2), strides=(2, 2), pads=(0, 0, 0, 0), ceil_mode=1,
+          y_dtype="u8", y_zero=128, y_scale=0.05), 2),
+    ("qsoftmax_u8_6x37", "qlinear_softmax8", dict(), 0),
+    ("qsoftmax_i8_4x5x12_axis1", "qlinear_softmax8",
+     dict(shape=(4, 5, 12), axis=1, dtype="i8", x_zero=-5, x_scale=0.11, y_zero=-128), 1),
+    ("qsoftmax_u8_3x4x6_opset11", "qlinear_softmax8",
+     dict(shape=(3, 4, 6), axis=1, opset=11, x_scale=0.03, x_zero=100), 2),
+    ("transpose_f32_2x3x4x5", "transpose", dict(), 0),
+    ("transpose_u8_perm_rev", "transpose", dict(shape=(3, 5, 7), perm=(2, 0, 1), dtype="u8"), 1),
 ]
+
+# whole models from the reference's own test tree: (case name, path inside the
+# reference project, input seed).  The graph is stored with the fixture (nodes
+# in cases.json, initializers in the .npz), so tests need neither the model
+# file nor the reference.
+MODEL_CASES = [
+    ("kws_qoperator", "tests/onnx/micro_kws_m_static_qoperator.onnx", 0),
+]
+MODEL_SAMPLES = 32  # seeded input sets per model, stacked on a leading sample axis
+
+
+def _json_attr(v):
+    if isinstance(v, (bool, int, float, str)):
+        return v
+    if isinstance(v, (list, tuple)) and all(isinstance(x, (bool, int, float, str)) for x in v):
+        return list(v)
+    raise TypeError(f"attribute value {v!r} has no JSON form")
+
+
+def graph_json(spec) -> dict:
+    return {
+        "name": spec.name,
+        "inputs": [[t.name, t.dtype, list(t.shape)] for t in spec.inputs],
+        "outputs": [[t.name, t.dtype, list(t.shape)] for t in spec.outputs],
+        "values": [[t.name, t.dtype, list(t.shape)] for t in spec.values],
+        "nodes": [[n.op_type, n.name, list(n.inputs), list(n.outputs),
+                   {k: _json_attr(v) for k, v in n.attrs.items()}, n.domain] for n in spec.nodes],
+        "opset_imports": [list(o) for o in spec.opset_imports],
+    }
+
+
+def _smooth_field(rng, shape, lo: float, hi: float) -> np.ndarray:
+    """Gaussian-filtered noise over the last two axes (a spectrogram-like
+    field), its mean and spread drawn inside [lo, hi]."""
+    f = np.fft.fft2(rng.standard_normal(shape))
+    ky = np.fft.fftfreq(shape[-2])[:, None]
+    kx = np.fft.fftfreq(shape[-1])[None, :]
+    f *= np.exp(-(ky ** 2 + kx ** 2) * rng.uniform(20, 120))
+    x = np.real(np.fft.ifft2(f))
+    x = x / (x.std() + 1e-12)
+    mid, half = (lo + hi) / 2, (hi - lo) / 2
+    return mid + rng.uniform(-0.2, 0.2) * half + x * half * rng.uniform(0.25, 0.5)
+
+
+def model_inputs(spec, seed: int) -> dict:
+    """Seeded inputs over the range the model's first quantizer covers: every
+    fourth set uniform over that whole range and a little past both ends (so
+    saturation is hit), the others smooth fields laid out as the image the
+    input is reshaped to (noise alone drives the keyword model to one class)."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for t in spec.inputs:
+        lo, hi, image = -1.0, 1.0, tuple(t.shape)
+        names = {t.name}
+        for n in spec.nodes:
+            if n.op_type == "Reshape" and n.inputs[0] in names:
+                names.add(n.outputs[0])
+                tgt = [int(v) for v in np.asarray(spec.initializers[n.inputs[1]]).reshape(-1)]
+                if len(tgt) == 4 and -1 not in tgt[1:]:
+                    image = tuple(tgt[1:])
+            if n.op_type == "QuantizeLinear" and n.inputs[0] in names:
+                s = float(np.asarray(spec.initializers[n.inputs[1]]).reshape(-1)[0])
+                zp = np.asarray(spec.initializers[n.inputs[2]]).reshape(-1)[0]
+                qlo, qhi = (-128, 127) if zp.dtype == np.int8 else (0, 255)
+                lo, hi = (qlo - 2 - int(zp)) * s, (qhi + 2 - int(zp)) * s
+                break
+        if seed % 4 == 3 or len(image) < 2:
+            x = rng.uniform(lo, hi, size=t.shape)
+        else:
+            x = _smooth_field(rng, image, lo, hi).reshape(t.shape)
+        out[t.name] = x.astype(np.float32)
+    return out
 
 
 def main() -> None:
@@ -102,6 +195,26 @@ def main() -> None:
                                     "kwargs": {k: list(v) if isinstance(v, tuple) else v
                                                for k, v in kwargs.items()},
                                     "seed": seed}
+            print(name, {k: v.shape for k, v in outputs.items()})
+        from emx_onnx_cgen_b200.onnx_reader import infer_types, read_onnx
+        for name, rel, seed in MODEL_CASES:
+            if only and name not in only:
+                continue
+            spec = infer_types(read_onnx(refc.REFERENCE_SRC.parent / rel))
+            tag = "g_" + name
+            refc.build(spec, tag, Path(tmp))
+            model = refc.RefCModel(tag, Path(tmp))
+            runs = []
+            for i in range(MODEL_SAMPLES):
+                inputs = model_inputs(spec, seed + i)
+                runs.append((inputs, model.run(inputs)))
+            arrays = {f"init:{k}": v for k, v in spec.initializers.items()}
+            arrays.update({f"in:{k}": np.stack([r[0][k] for r in runs]) for k in runs[0][0]})
+            arrays.update({f"out:{k}": np.stack([r[1][k] for r in runs]) for k in runs[0][1]})
+            outputs = runs[0][1]
+            np.savez_compressed(HERE / f"{name}.npz", **arrays)
+            index["cases"][name] = {"model": rel, "seed": seed, "samples": MODEL_SAMPLES,
+                                    "graph": graph_json(spec)}
             print(name, {k: v.shape for k, v in outputs.items()})
     (HERE / "cases.json").write_text(json.dumps(index, indent=1) + "\n")
 

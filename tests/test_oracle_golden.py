@@ -11,13 +11,17 @@ from oracle import oracle
 @pytest.mark.parametrize("name", sorted(cases()))
 def test_port_matches_reference_c(name):
     wl, inputs, ref = load(name)
-    got = oracle.run_graph(wl.graph, inputs)
-    for k, v in ref.items():
-        assert got[k].dtype == v.dtype and got[k].shape == v.shape
-        assert np.array_equal(got[k].view(np.uint8), v.view(np.uint8)), k
+    runs = [(inputs, ref)]
+    if hasattr(wl, "samples"):  # a whole model, several seeded input sets
+        runs = [(wl.sample(inputs, i), wl.sample(ref, i)) for i in range(wl.samples)]
+    for x, r in runs:
+        got = oracle.run_graph(wl.graph, x)
+        for k, v in r.items():
+            assert got[k].dtype == v.dtype and got[k].shape == v.shape
+            assert np.array_equal(got[k].view(np.uint8), v.view(np.uint8)), k
 
 
-@pytest.mark.parametrize("name", sorted(cases()))
+@pytest.mark.parametrize("name", sorted(n for n, m in cases().items() if "builder" in m))
 def test_builders_reproduce_fixture_weights(name):
     from emx_onnx_cgen_b200 import workloads as W
     meta = cases()[name]

@@ -20,6 +20,13 @@ SMALL = {
     "swish_mul": lambda: W.swish_mul_f16((8, 24)),
     "lstm": lambda: W.lstm_fp32(seq=3, batch=2, input_size=8, hidden=16),
     "attention": lambda: W.attention_fp16(batch=1, heads=2, seq=16, head_dim=8),
+    "maxpool": lambda: W.pool8(),
+    "maxpool_same": lambda: W.pool8(shape=(2, 3, 10, 7), kernel=(4, 3), strides=(3, 2), auto_pad="SAME_LOWER"),
+    "qavgpool": lambda: W.pool8(kind="avg", count_include_pad=1, ceil_mode=1),
+    "qsoftmax": lambda: W.qlinear_softmax8(),
+    "qsoftmax_opset11": lambda: W.qlinear_softmax8(shape=(3, 4, 6), axis=1, opset=11),
+    "transpose": lambda: W.transpose(),
+    "kws_qoperator_model": lambda: __import__("golden_util").load("kws_qoperator")[0],
 }
 
 
@@ -190,3 +197,37 @@ def test_swish_plan_reserves_a_table():
     plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
     (sw,) = [o for o in plan.ops if o.kernel == K.K_SWISH_F16]  # standalone: no MatMulNBits to fuse into
     assert plan.tensors[sw.tensors[2]].nbytes == 2 * 65536
+
+
+def test_kws_qoperator_model_plan():
+    """The reference's micro_kws_m_static_qoperator.onnx (stored with its golden
+    fixture): both Reshapes alias their source, every op has a kernel."""
+    from golden_util import load
+    fx = load("kws_qoperator")[0]
+    plan = B200PlanEmitter().emit_plan(lowering.lower(fx.graph))
+    kinds = [K.NAMES[o.kernel] for o in plan.ops]
+    assert kinds == ["quantize_linear", "qconv_generic", "maxpool", "qconv_generic", "qlinear_avgpool",
+                     "qconv_generic", "qlinear_avgpool", "dequantize_linear", "transpose", "quantize_linear",
+                     "qlinear_matmul", "qlinear_add", "qlinear_matmul", "qlinear_add", "qlinear_matmul",
+                     "qlinear_add", "qlinear_softmax", "dequantize_linear"]
+
+
+def test_reshape_to_graph_output_copies():
+    g = GraphSpec("r", [TensorSpec("X", "f32", (2, 3, 4))], [TensorSpec("Y", "f32", (2, 12))],
+                  [NodeSpec("Reshape", "r", ("X", "s"), ("Y",))], {"s": np.array([2, -1], np.int64)})
+    plan = B200PlanEmitter().emit_plan(lowering.lower(g))
+    assert [K.NAMES[o.kernel] for o in plan.ops] == ["copy"]
+    assert plan.ops[0].ip[K.CP_BYTES] == 96 and plan.ops[0].ip[K.CP_BATCH] == 2
+
+
+def test_qsoftmax_exp_table_is_libm_expf():
+    """The planner's exp table holds the C library's expf of v(b) - v(bm)."""
+    import ctypes
+    import ctypes.util
+    from emx_onnx_cgen_b200.plan import qsoftmax_exp_table
+    libm = ctypes.CDLL(ctypes.util.find_library("m"))
+    libm.expf.restype, libm.expf.argtypes = ctypes.c_float, [ctypes.c_float]
+    t = qsoftmax_exp_table(True, -5, np.float32(0.11))
+    v = lambda b: np.float32(np.float32(np.int8(np.uint8(b)).astype(np.int32) + 5) * np.float32(0.11))
+    for b, bm in [(0, 0), (3, 200), (127, 128), (128, 127), (255, 1)]:
+        assert t[b, bm] == np.float32(libm.expf(float(np.float32(v(b) - v(bm))))), (b, bm)
