@@ -75,6 +75,9 @@ struct QConvTcParams {
   // shared memory by one bulk copy per tile (r_bulk)
   int r_bulk;
   int64_t r_off;
+  // chain layer whose output the residual is (its progress is waited for), or
+  // -1: a tensor written before the launch
+  int r_src;
   // fused add by table: out byte = lut[(conv byte << 8) | residual byte], staged in shared memory
   const uint8_t* lut;
   int rq_int;  // integer requantisation (QC_RQ_INT)
@@ -87,13 +90,15 @@ constexpr int QC_RSTAGES = 3;  // residual ring depth (tiles)
 // accumulator each: one issuing thread completes a tcgen05.mma every ~150
 // cycles whatever its N, so with N = OC = 64 several issuers keep more of the
 // tensor core busy), warp P+1 residual producer, then 16 epilogue warps from
-// the next multiple of 4.  P = 4 while 2 tiles x P partials x OC columns fit
-// the 512 TMEM columns (OC <= 64), else 2.
+// the next multiple of 4, then the chain's progress publisher.  Each waiting
+// role has a warp of its own: two lanes of one warp spinning in different
+// loops delay each other by microseconds.
 constexpr int QC_MMA_WARPS = 4;  // most issuers of any variant
 constexpr int QC_EPI_WARPS = 16;
 __host__ __device__ constexpr int qc_partials(int oc) { return oc <= 64 ? 2 : 256 / oc; }
 __host__ __device__ constexpr int qc_epi_warp0(int oc) { return (qc_partials(oc) + 2 + 3) & ~3; }
-__host__ __device__ constexpr int qc_threads(int oc) { return 32 * (qc_epi_warp0(oc) + QC_EPI_WARPS); }
+__host__ __device__ constexpr int qc_pub_warp(int oc) { return qc_epi_warp0(oc) + QC_EPI_WARPS; }
+__host__ __device__ constexpr int qc_threads(int oc) { return 32 * (qc_pub_warp(oc) + 1); }
 constexpr int QC_TILE_M = 128;
 
 // A chain of up to QC_MAX_CHAIN convolutions run by one launch (see
@@ -238,9 +243,7 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
   constexpr int P = qc_partials(OC);
   constexpr int RESID_WARP = P + 1;
   constexpr int EPI_WARP0 = qc_epi_warp0(OC);
-  // the chain's progress publisher: a warp of its own where one is free, else
-  // lane 1 of the residual producer's warp
-  constexpr int PUB_WARP = P + 2 < EPI_WARP0 ? P + 2 : RESID_WARP;
+  constexpr int PUB_WARP = qc_pub_warp(OC);
   constexpr uint32_t TMEM_COLS = 512;
   static_assert(G % 8 == 0, "OC must be a multiple of 32");
   const QConvTcParams& g = cp.layer[0];  // geometry shared by every layer
@@ -281,8 +284,9 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + QC_RSTAGES);
   // per epilogue warp: how many published tiles it has stored (monotonic; the publisher reads them)
   uint32_t* s_stored = tmem_holder + 4;
-  // per MMA k of a tile: byte offsets of its A (window) and B (weights) operands
-  uint32_t* s_koff = s_stored + QC_EPI_WARPS;  // [2 * MMAs per tile]
+  // per MMA k of a tile: offsets of its A (window) and B (weights) operands in
+  // 16-byte units, the unit of a descriptor's start-address field
+  uint32_t* s_koff = s_stored + QC_EPI_WARPS;  // [2 * MMAs per tile], 8-byte aligned
   // residual ring after that (128-byte aligned)
   uint8_t* s_r = smem + ((uint32_t)(reinterpret_cast<uint8_t*>(s_koff + 2 * g.kh * g.kw * KSTEPS) - smem) + 127u & ~127u);
 
@@ -316,8 +320,8 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
     for (int k = 0; k < g.kh * g.kw * KSTEPS; ++k) {
       const int tap = k / KSTEPS, s = k - tap * KSTEPS;
       const int kh = tap / g.kw, kw = tap - kh * g.kw;
-      s_koff[2 * k] = (uint32_t)(kh * g.wp + kw) * CIN + 32u * s;
-      s_koff[2 * k + 1] = (uint32_t)tap * (OC * CIN) + 32u * s;
+      s_koff[2 * k] = ((uint32_t)(kh * g.wp + kw) * CIN + 32u * s) >> 4;
+      s_koff[2 * k + 1] = ((uint32_t)tap * (OC * CIN) + 32u * s) >> 4;
     }
     for (int w = 0; w < QC_MMA_WARPS; ++w) mbar_init(&drain[w], 1);
     for (int r = 0; r < QC_RSTAGES; ++r) {
@@ -451,7 +455,7 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
       for (int l = 0; l < L && ok; ++l) {
         const uint32_t idesc = cp.layer[l].idesc;
         const int wb = wbufs == 2 ? (l & 1) : 0;
-        const uint32_t b_base = smem_u32(s_b + (size_t)wb * wbuf_bytes);
+        const uint64_t b_desc0 = smem_desc_k_swizzled(smem_u32(s_b + (size_t)wb * wbuf_bytes), CIN);
         if (!mbar_wait(&bbar[wb], (uint32_t)(wbufs == 2 ? (l >> 1) : l) & 1u, err, DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
@@ -471,12 +475,14 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
           // MMA number k of the tile accumulates into partial k % P (integer
           // partial sums are exact in any order; the epilogue adds the P
           // partials), issued by warp 1 + k % P.
+          // An operand's descriptor is its base's plus the operand offset: the
+          // start-address field holds address >> 4 in 14 bits and every shared
+          // address stays below 256 KB, so the sum never carries out of the field.
           const uint32_t d_tmem = tmem_base + (uint32_t)((acc * P + my) * OC);
-          const uint32_t a_stage = a_base + (uint32_t)stage * g.stage_bytes;
+          const uint64_t a_desc0 = smem_desc_k_swizzled(a_base + (uint32_t)stage * g.stage_bytes, CIN);
           for (int k = my; k < n_mma; k += PE) {
-            const uint64_t adesc = smem_desc_k_swizzled(a_stage + s_koff[2 * k], CIN);
-            const uint64_t bdesc = smem_desc_k_swizzled(b_base + s_koff[2 * k + 1], CIN);
-            mma_i8(d_tmem, adesc, bdesc, idesc, k >= PE ? 1u : 0u);
+            const uint2 o = *reinterpret_cast<const uint2*>(&s_koff[2 * k]);
+            mma_i8(d_tmem, a_desc0 + o.x, b_desc0 + o.y, idesc, k >= PE ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           tc_commit(&accf[acc]);
@@ -492,11 +498,9 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
         (void)mbar_wait(&drain[my], 0, nullptr, 0);
       }
     }
-  } else if (warp == PUB_WARP && PUB_WARP != RESID_WARP) {
+  } else if (warp == PUB_WARP) {
     if (lane == 0 && chained && L > 1) qc_publish(cp, s_stored, progress, n_tiles, t_first, t_step);
   } else if (warp == RESID_WARP) {
-    if (PUB_WARP == RESID_WARP && lane == 1 && chained && L > 1)
-      qc_publish(cp, s_stored, progress, n_tiles, t_first, t_step);
     if (lane == 0 && cp.use_ring) {
       // ---------------- residual producer: the tile's residual rows, one bulk copy each
       pdl_wait();  // the residual may come from the preceding kernel
@@ -513,9 +517,9 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
             ok = false;
             break;
           }
-          if (chained && l > 0) {  // the residual may be an earlier layer's output
-            if (!wait_flags_at_least(progress, tile - cp.rlo, tile + cp.rhi, n_tiles, epoch * 64ull + (unsigned)l,
-                                     err, DEV_TIMEOUT_GRID)) {
+          if (chained && lp.r_src >= 0) {  // the residual is layer r_src's output: wait for those rows
+            if (!wait_flags_at_least(progress, tile - cp.rlo, tile + cp.rhi, n_tiles,
+                                     epoch * 64ull + (unsigned)(lp.r_src + 1), err, DEV_TIMEOUT_GRID)) {
               ok = false;
               break;
             }
@@ -536,7 +540,7 @@ __global__ void __launch_bounds__(qc_threads(OC), 1) qconv_chain_kernel(const __
         for (int s2 = 0; s2 < QC_RSTAGES; ++s2)
           if (issued & (1u << s2)) (void)mbar_wait(&rfull[s2], (parity_of >> s2) & 1u, nullptr, 0);
     }
-  } else if (warp >= EPI_WARP0) {
+  } else if (warp >= EPI_WARP0 && warp < PUB_WARP) {
     // ---------------- epilogue: TMEM -> registers -> requant (+ QLinearAdd) -> global
     const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;
@@ -926,6 +930,7 @@ static void fill_params(QConvTcParams& p, const PlanOp& op, void* const* ptrs, c
   p.lut = st->use_lut && op.t[5] >= 0 ? (const uint8_t*)ptrs[op.t[5]] : nullptr;
   p.r_bulk = 0;
   p.r_off = 0;
+  p.r_src = -1;
   if (p.has_add && st->resid_ring && p.r_hp == p.hp && p.r_wp == p.wp) {
     p.r_off = (int64_t)p.r_pt * p.wp + p.r_pl;
     const int64_t last_row = (int64_t)((op.ip[QC_N] * (int64_t)p.hp * p.wp + QC_TILE_M - 1) / QC_TILE_M) *
@@ -1051,6 +1056,8 @@ static bool build_chain(const PlanOp& op, void* const* ptrs, const LaunchCtx& ct
                                    QC_TILE_M + p.r_off;
       if (last_row > m.ip[QC_R_ROWS]) return false;
       p.r_bulk = 1;
+      for (int j = 0; j < k; ++j)  // written inside the chain, by layer j?
+        if (m.t[3] == ctx.ops[ctx.index + j].t[4]) p.r_src = j;
       p.lut = m.t[5] >= 0 ? (const uint8_t*)ptrs[m.t[5]] : nullptr;
       any_lut = any_lut || p.lut != nullptr;
     }
