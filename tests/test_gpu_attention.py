@@ -1,8 +1,8 @@
 """ONNX Attention (opset 23) fp16 on the B200 kernel: bit-identical to the
 reference's generated C (golden fixtures) and to the CPU restatement, which
 repeats the reference's statement-by-statement fp16 rounding.  Covers causal
-and non-causal, sequence lengths off the 16-row / 64-key tiles, head sizes
-8..128, and inputs with inf / NaN / overflowing scores (the path that
+and non-causal, sequence lengths off the 16-row / 64- and 128-key tiles,
+head sizes 8..128 (both kernels), and inputs with inf / NaN / overflowing scores (the path that
 evaluates masked keys with the reference's mask arithmetic)."""
 import numpy as np
 import pytest
@@ -30,6 +30,7 @@ def test_golden(name):
     dict(batch=1, heads=1, seq=77, head_dim=32, causal=False),
     dict(batch=3, heads=1, seq=16, head_dim=8),
     dict(batch=1, heads=1, seq=1, head_dim=16),
+    dict(batch=1, heads=2, seq=70, head_dim=12),  # D not a multiple of 8: the 64-key-tile kernel
 ])
 def test_vs_port(kw):
     require_gpu()
