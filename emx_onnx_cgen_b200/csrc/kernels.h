@@ -35,6 +35,7 @@ enum KernelId : uint32_t {
   K_MAXPOOL = 22,          // 2-D MaxPool, 8-bit
   K_QLINEAR_AVGPOOL = 23,  // com.microsoft QLinearAveragePool, 2-D NCHW, 8-bit
   K_QLINEAR_SOFTMAX = 24,  // com.microsoft QLinearSoftmax, 8-bit
+  K_NBITS_I8 = 25,         // MatMulNBits accuracy_level 4: int8 activations, exact block sums (nbits_i8.cu)
 };
 
 // Chunk-planar zero-bordered layout ("planar" below): [C/16][rows][16 bytes],
@@ -81,6 +82,11 @@ enum {
   NB_ROUNDED_DEQUANT /*1: one MMA per K slice on fp16-rounded weights (default 0: exact hi + lo)*/
 };
 enum { NBF_ALPHA };
+
+// ---- K_NBITS_I8: t[0]=A f16 [rows][K], t[1]=weights int8 (q - zp) [N][KP] (zero past K),
+//      t[2]=scales f32 [N][NBLK], t[3]=bias f32 [N] | -1, t[4]=scratch int8 [rows][KP] (quantised A),
+//      t[5]=scratch f32 [rows][NBLK] (A's block scales), t[6]=Y f16 [rows][N]; KP = NBLK * BLOCK
+enum { NI_ROWS, NI_K, NI_KP, NI_N, NI_BLOCK, NI_NBLK, NI_ROWS_PER_BATCH };
 
 // ---- K_ATTENTION_F16 and K_ATTENTION_TC (same slots; the latter needs head sizes of 128 and
 //      ignores t[4]): t[0]=Q, t[1]=K, t[2]=V, t[3]=Y (fp16), t[4]=scratch (4 words);
@@ -226,6 +232,8 @@ void launch_hold(const int* flag, int seq, int* err, cudaStream_t stream);
 int launch_relu_f32(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_nbits(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_nbits(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
+int prepare_nbits_i8(const PlanOp&, void* const*, OpState*, int, char*, size_t);
+int launch_nbits_i8(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int prepare_swish_f16(const PlanOp&, void* const*, OpState*, int, char*, size_t);
 int launch_swish_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);
 int launch_mul_f16(const PlanOp&, void* const*, const OpState*, const LaunchCtx&, int*);

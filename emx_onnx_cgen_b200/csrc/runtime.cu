@@ -48,6 +48,7 @@ const KernelEntry kKernels[] = {
     {emx::K_GEMM_F32, emx::prepare_gemm_f32, emx::launch_gemm_f32, "gemm_f32"},
     {emx::K_RELU_F32, nullptr, emx::launch_relu_f32, "relu_f32"},
     {emx::K_NBITS_GEMM, emx::prepare_nbits, emx::launch_nbits, "nbits_gemm"},
+    {emx::K_NBITS_I8, emx::prepare_nbits_i8, emx::launch_nbits_i8, "nbits_i8"},
     {emx::K_SWISH_F16, emx::prepare_swish_f16, emx::launch_swish_f16, "swish_f16"},
     {emx::K_MUL_F16, nullptr, emx::launch_mul_f16, "mul_f16"},
     {emx::K_LSTM_F32, emx::prepare_lstm_f32, emx::launch_lstm_f32, "lstm_f32"},

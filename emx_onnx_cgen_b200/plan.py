@@ -1417,10 +1417,62 @@ class B200PlanEmitter:
                  if fused_alpha is not None else f"{out_name} (tcgen05 f16)")
         self._b.op(K.K_NBITS_GEMM, [a, t_w, t_b, y], ip, fp, label=label, batched=batched)
 
+    def _nbits_i8_reject(self, op) -> str | None:
+        """Why an accuracy_level-4 MatMulNBits has no int8-path kernel (None: it has one)."""
+        if int(op.bits) != 4:
+            return f"{op.bits}-bit weights on the int8 activation path"
+        if self._dtype(op.input0) != "f16" or _suffix(op.output_dtype) != "f16":
+            return "only fp16 activations and outputs on the int8 activation path"
+        bs = int(op.block_size)
+        if bs < 16 or bs % 16 or bs > 4096:
+            return f"block_size {bs} on the int8 activation path"
+        for what, name in (("B", op.input1), ("scales", op.scales), ("zero_points", op.zero_points),
+                           ("bias", op.bias)):
+            if name is not None and name not in self._consts:
+                return f"{what} must be an initializer"
+        if op.zero_points is not None and self._dtype(op.zero_points) != "u8":
+            return "only packed uint8 zero points on the int8 activation path"
+        if op.bias is not None and self._dtype(op.bias) != "f16":
+            return "only fp16 bias"
+        return None
+
+    def _nbits_i8_emit(self, op):
+        """accuracy_level 4 (templates/matmul_nbits_int8_op.c.j2): weights packed
+        as int8 (q - zp) [N][KP] with KP the K blocks' padded length (zeros past
+        K, so a partial last block adds exact zeros), scales as float
+        [N][n_blocks]; the quantised activations and their block scales are
+        per-run scratch."""
+        n, k, bs = int(op.n), int(op.k), int(op.block_size)
+        nblk = -(-k // bs)
+        kp = nblk * bs
+        q, zp, sc, bias = self._nbits_part(op)
+        w = np.zeros((n, kp), np.int8)
+        w[:, :k] = (q[:, :k].astype(np.int16) - np.repeat(zp.astype(np.int16), bs, axis=1)[:, :k]).astype(np.int8)
+        t_w = self._b.weight(w, "i8", op.input1 + ":int8-minus-zp")
+        t_s = self._b.weight(np.ascontiguousarray(sc.astype(np.float32)), "f32", op.scales + ":f32")
+        t_b = self._b.weight(bias, "f32", op.bias + ":f32") if bias is not None else -1
+        a = self._src(op.input0)
+        a_shape = tuple(self._shape(op.input0))
+        rows = int(np.prod(a_shape[:-1])) if len(a_shape) > 1 else 1
+        t_qa = self._b.arena_tensor(T_TEMP, "i8", (rows, kp), name=f"{op.output}:int8-activations")
+        t_as = self._b.arena_tensor(T_TEMP, "f32", (rows, nblk), name=f"{op.output}:activation-block-scales")
+        y = self._dest(op.output, "f16", a_shape[:-1] + (n,))
+        batched = (len(a_shape) > 1 and a_shape[0] == self._batch and self._batch > 0
+                   and self._is_batched(op.input0))
+        ip = {K.NI_ROWS: rows, K.NI_K: k, K.NI_KP: kp, K.NI_N: n, K.NI_BLOCK: bs, K.NI_NBLK: nblk,
+              K.NI_ROWS_PER_BATCH: rows // self._batch if batched else 0}
+        self._b.op(K.K_NBITS_I8, [a, t_w, t_s, t_b, t_qa, t_as, y], ip,
+                   label=f"{op.output} (int8 activations, accuracy_level 4)", batched=batched)
+
     def _emit_MatMulNBitsOp(self, i, op):
         if i in self._nbits_fused:
             f = self._nbits_fused[i]
             return self._nbits_emit([f["gate"], f["up"]], f["mul"].output, fused_alpha=f["alpha"])
+        if int(op.accuracy_level) == 4:
+            why = self._nbits_i8_reject(op)
+            if why:
+                raise UnsupportedOpError(f"MatMulNBits: {why}")
+            return self._nbits_i8_emit(op)
         why = self._nbits_reject(op)
         if why:
             raise UnsupportedOpError(f"MatMulNBits: {why}")

@@ -241,8 +241,11 @@ def lstm_fp32(seq: int = 512, batch: int = 256, input_size: int = 512, hidden: i
 
 # --------------------------------------------------------------------------- single ops
 def matmul_nbits_f16(m: int = 64, k: int = 256, n: int = 192, block: int = 32, zero_points: str = "none",
-                     bias: bool = False, weight_seed: int = 1) -> Workload:
+                     bias: bool = False, weight_seed: int = 1, accuracy_level: int = 0) -> Workload:
     """One com.microsoft MatMulNBits (bits 4) on fp16 activations ~N(0,1).
+
+    accuracy_level 4 selects the int8 activation path (activations quantised
+    per row and K block, exact int32 block sums).
 
     zero_points: "none" (default zero point 8), "block" (uint8 [N][ceil(n_blocks/2)],
     4-bit packed per block) or "column" (uint8 [N], one per column).  Optional
@@ -269,7 +272,8 @@ def matmul_nbits_f16(m: int = 64, k: int = 256, n: int = 192, block: int = 32, z
         inputs=[TensorSpec("A", "f16", (m, k))],
         outputs=[TensorSpec("Y", "f16", (m, n))],
         nodes=[NodeSpec("MatMulNBits", "mm", tuple(ins), ("Y",),
-                        {"bits": 4, "block_size": block, "K": k, "N": n, "accuracy_level": 0}, "com.microsoft")],
+                        {"bits": 4, "block_size": block, "K": k, "N": n, "accuracy_level": accuracy_level},
+                        "com.microsoft")],
         initializers=inits,
         opset_imports=(("", 21), ("com.microsoft", 1)),
     )
@@ -278,7 +282,8 @@ def matmul_nbits_f16(m: int = 64, k: int = 256, n: int = 192, block: int = 32, z
         return {"A": np.random.default_rng(seed).standard_normal((m, k)).astype(np.float16)}
 
     return Workload("matmul_nbits_f16", g, make_inputs, {"A": 0, "Y": 0},
-                    dict(m=m, k=k, n=n, block=block, zero_points=zero_points, bias=bias))
+                    dict(m=m, k=k, n=n, block=block, zero_points=zero_points, bias=bias,
+                         accuracy_level=accuracy_level))
 
 
 def swish_mul_f16(shape: tuple[int, ...] = (256, 512), alpha: float = 1.0) -> Workload:

@@ -199,6 +199,74 @@ void orc_matmul_nbits_f16(const f16 *a, const uint8_t *b, const f16 *scales, int
     }
 }
 
+/* ---------------------------------------------------------------------------
+ * com.microsoft MatMulNBits, bits=4, accuracy_level 4 on fp16 A: the int8
+ * activation path (templates/matmul_nbits_int8_op.c.j2:1-78, selected at
+ * ir/ops/nn.py:1183-1190).  Per row and K block: amax = max |a| (float),
+ * a_scale = amax / 127, a_inv = amax > 0 ? 127 / amax : 0, qa = int8 of
+ * nearbyintf(a * a_inv) clamped to [-128, 127]; per output: acc = 0, then per
+ * block in order acc += (float)isum * (a_scale * b_scale), isum the exact
+ * int32 sum of qa * (q - zp) over the block (a partial last block stops at K);
+ * bias added after the blocks, result cast to _Float16.  Weight, scale and
+ * zero-point layouts as in orc_matmul_nbits_f16.
+ * ------------------------------------------------------------------------- */
+void orc_matmul_nbits_i8_f16(const f16 *a, const uint8_t *b, const f16 *scales, int scales_per_block,
+                             const uint8_t *zero_points, int zp_per_block, const f16 *bias,
+                             int m, int n, int k, int block, f16 *y)
+{
+    const int n_blocks = (k + block - 1) / block;
+    const int blob = block / 2;
+    const int zp_cols = (n_blocks * 4 + 7) / 8;
+    int8_t *qa = (int8_t *)malloc((size_t)(k > 0 ? k : 1));
+    float *a_scale = (float *)malloc(sizeof(float) * (size_t)(n_blocks > 0 ? n_blocks : 1));
+    for (int i0 = 0; i0 < m; ++i0) {
+        const f16 *arow = a + (size_t)i0 * k;
+        for (int blk = 0; blk < n_blocks; ++blk) {
+            float amax = 0.0f;
+            for (int kk = 0; kk < block; ++kk) {
+                const int kx = blk * block + kk;
+                if (kx >= k) break;
+                const float av = fabsf((float)arow[kx]);
+                if (av > amax) amax = av;
+            }
+            a_scale[blk] = amax / (float)127;
+            const float a_inv = amax > 0.0f ? (float)127 / amax : 0.0f;
+            for (int kk = 0; kk < block; ++kk) {
+                const int kx = blk * block + kk;
+                if (kx >= k) break;
+                float q = nearbyintf((float)arow[kx] * a_inv);
+                if (q > (float)127) q = (float)127;
+                if (q < (float)-128) q = (float)-128;
+                qa[kx] = (int8_t)q;
+            }
+        }
+        for (int i1 = 0; i1 < n; ++i1) {
+            float acc = 0.0f;
+            for (int blk = 0; blk < n_blocks; ++blk) {
+                int32_t isum = 0;
+                for (int kk = 0; kk < block; ++kk) {
+                    const int kx = blk * block + kk;
+                    if (kx >= k) break;
+                    const int quant_val = ((int)(unsigned char)b[((size_t)i1 * n_blocks + blk) * blob + kk * 4 / 8]
+                                           >> ((kk * 4) % 8)) & 15;
+                    int zp = 8;
+                    if (zero_points && zp_per_block)
+                        zp = ((int)zero_points[(size_t)i1 * zp_cols + blk * 4 / 8] >> ((blk * 4) % 8)) & 15;
+                    else if (zero_points)
+                        zp = (int)zero_points[i1] & 15;
+                    isum += (int32_t)qa[kx] * (int32_t)(quant_val - zp);
+                }
+                const float b_scale = (float)scales[scales_per_block ? (size_t)i1 * n_blocks + blk : (size_t)i1];
+                acc += (float)isum * (a_scale[blk] * b_scale);
+            }
+            if (bias) acc += (float)bias[i1];
+            y[(size_t)i0 * n + i1] = (f16)acc;
+        }
+    }
+    free(qa);
+    free(a_scale);
+}
+
 /* Swish fp16: a / (1.0 + exp(-alpha * a)) with a double-precision exp
  * (shared/scalar_functions.py:880-896; double libm call for f16, :503-506). */
 void orc_swish_f16(const f16 *x, f16 *y, size_t count, float alpha_f)

@@ -203,7 +203,8 @@ def mul_f32(a, b): return _binary("orc_mul_f32", a, b, np.float32)
 def add_f32(a, b): return _binary("orc_add_f32", a, b, np.float32)
 
 
-def matmul_nbits_f16(a, b_packed, scales, k, n, block=32, zero_points=None, bias=None):
+def matmul_nbits_f16(a, b_packed, scales, k, n, block=32, zero_points=None, bias=None, accuracy_level=0):
+    """accuracy_level 4 selects the reference's int8 activation path."""
     a = np.ascontiguousarray(a, np.float16)
     m = int(np.prod(a.shape[:-1]))
     y = np.zeros((*a.shape[:-1], n), np.float16)
@@ -213,8 +214,9 @@ def matmul_nbits_f16(a, b_packed, scales, k, n, block=32, zero_points=None, bias
     zp_pb = int(zero_points is not None and np.ndim(zero_points) >= 2)
     zp = None if zero_points is None else np.ascontiguousarray(zero_points, np.uint8)
     bias = None if bias is None else np.ascontiguousarray(bias, np.float16)
-    lib().orc_matmul_nbits_f16(_p(a), _p(b_packed), _p(scales), _i(scales_pb), _p(zp), _i(zp_pb), _p(bias),
-                               _i(m), _i(n), _i(k), _i(block), _p(y))
+    fn = lib().orc_matmul_nbits_i8_f16 if int(accuracy_level) == 4 else lib().orc_matmul_nbits_f16
+    fn(_p(a), _p(b_packed), _p(scales), _i(scales_pb), _p(zp), _i(zp_pb), _p(bias), _i(m), _i(n), _i(k), _i(block),
+       _p(y))
     return y
 
 
@@ -359,7 +361,8 @@ def run_graph(spec: GraphSpec, inputs: dict[str, np.ndarray]) -> dict[str, np.nd
             res = [matmul_nbits_f16(ins[0], ins[1], ins[2], int(a["K"]), int(a["N"]),
                                     int(a.get("block_size", 32)),
                                     ins[3] if len(ins) > 3 else None,
-                                    ins[5] if len(ins) > 5 else None)]
+                                    ins[5] if len(ins) > 5 else None,
+                                    int(a.get("accuracy_level", 0)))]
         elif op == "Swish":
             res = [swish_f16(ins[0], float(a.get("alpha", 1.0)))]
         elif op == "Sigmoid":

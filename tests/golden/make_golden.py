@@ -55,6 +55,13 @@ CASES = [
      dict(m=5, k=96, n=40, block=32, zero_points="block", bias=True), 0),
     ("nbits1_m3_k64_n24_zpcol_b16", "matmul_nbits_f16", dict(m=3, k=64, n=24, block=16, zero_points="column"), 1),
     ("nbits1_m2_k256_n16_b128", "matmul_nbits_f16", dict(m=2, k=256, n=16, block=128), 2),
+    # accuracy_level 4: the int8 activation path (matmul_nbits_int8_op.c.j2)
+    ("nbits8_m5_k96_n40_zpblock_bias", "matmul_nbits_f16",
+     dict(m=5, k=96, n=40, block=32, zero_points="block", bias=True, accuracy_level=4), 0),
+    ("nbits8_m3_k64_n24_zpcol_b16", "matmul_nbits_f16",
+     dict(m=3, k=64, n=24, block=16, zero_points="column", accuracy_level=4), 1),
+    ("nbits8_m4_k80_n16_partial", "matmul_nbits_f16", dict(m=4, k=80, n=16, block=32, accuracy_level=4), 2),
+    ("nbits8_m2_k256_n24_b128", "matmul_nbits_f16", dict(m=2, k=256, n=24, block=128, accuracy_level=4), 3),
     ("swishmul_8x24", "swish_mul_f16", dict(shape=(8, 24)), 0),
     ("swishmul_5x16_alpha1702", "swish_mul_f16", dict(shape=(5, 16), alpha=1.702), 1),
     ("qmm_m5_k40_n24", "qlinear_matmul_u8", dict(m=5, k=40, n=24), 0),
