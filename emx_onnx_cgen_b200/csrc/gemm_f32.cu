@@ -128,9 +128,9 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const G
 
 // Y = op(A) * B^T with A [M][K] and B [N][K] row-major (no transA, transB = 1:
 // K contiguous in both): the cp.async-pipelined exact chains of exact_chain.cuh.
-template <int BM, int BN, int RM, int RN>
+template <int BM, int BN, int RM, int RN, int BK = 32, int S = 4>
 __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(const GemmF32Params p) {
-  using XC = ExactChain<BM, BN, RM, RN, 32, 4>;
+  using XC = ExactChain<BM, BN, RM, RN, BK, S>;
   extern __shared__ __align__(16) float xc_smem[];
   pdl_wait();
   pdl_launch_dependents();
@@ -178,19 +178,36 @@ struct ChainVariant {
   size_t smem;
   GemmKernel fn;
 };
-#define EMX_CHAIN_VARIANT(BM, BN, RM, RN)                                                        \
-  {BM, BN, (BM / RM) * (BN / RN), ExactChain<BM, BN, RM, RN, 32, 4>::SMEM_BYTES,                 \
-   gemm_f32_chain_kernel<BM, BN, RM, RN>}
+#define EMX_CHAIN_VARIANT(BM, BN, RM, RN, BK, S)                                                 \
+  {BM, BN, (BM / RM) * (BN / RN), ExactChain<BM, BN, RM, RN, BK, S>::SMEM_BYTES,                 \
+   gemm_f32_chain_kernel<BM, BN, RM, RN, BK, S>}
+// Several CTAs per SM, a short K stage (small problems, many CTAs)
 static const ChainVariant kChainVariants[] = {
-    EMX_CHAIN_VARIANT(64, 64, 4, 4), EMX_CHAIN_VARIANT(32, 64, 4, 4), EMX_CHAIN_VARIANT(32, 32, 2, 2),
-    EMX_CHAIN_VARIANT(16, 32, 2, 2), EMX_CHAIN_VARIANT(16, 16, 2, 2), EMX_CHAIN_VARIANT(8, 16, 1, 2),
+    EMX_CHAIN_VARIANT(64, 64, 4, 4, 32, 4), EMX_CHAIN_VARIANT(32, 64, 4, 4, 32, 4),
+    EMX_CHAIN_VARIANT(32, 32, 2, 2, 32, 4), EMX_CHAIN_VARIANT(16, 32, 2, 2, 32, 4),
+    EMX_CHAIN_VARIANT(16, 16, 2, 2, 32, 4), EMX_CHAIN_VARIANT(8, 16, 1, 2, 32, 4),
+};
+// Long chains (K >= 1024): 256-thread CTAs with 64-wide K stages, chosen by
+// outputs per SM (measured on B200 over tile shapes, 2-8 chains per thread,
+// K stages 32-128 deep, 1-8 CTAs per SM, on the 64 x 1024 -> 4096 -> 1024
+// MLP): with at least 1024 outputs per SM, 4 chains per thread and 3 CTAs per
+// SM (64 x 4096, K 1024: 52 -> 41 us); with fewer, 2 chains per thread and
+// twice the warps to hide the chains' latency (64 x 1024, K 4096: 102 -> 77 us).
+static const ChainVariant kLongKVariants[] = {
+    EMX_CHAIN_VARIANT(32, 32, 2, 2, 64, 4),  // >= 1024 outputs per SM
+    EMX_CHAIN_VARIANT(16, 32, 1, 2, 64, 4),  // >= 256 outputs per SM
 };
 #undef EMX_CHAIN_VARIANT
 
 int prepare_gemm_f32(const PlanOp&, void* const*, OpState*, int, char* msg, size_t n) {
-  for (const auto& v : kChainVariants) {
-    cudaError_t e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem);
-    if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  for (const auto* table : {kChainVariants, kLongKVariants}) {
+    const size_t count = table == kChainVariants ? sizeof(kChainVariants) / sizeof(kChainVariants[0])
+                                                 : sizeof(kLongKVariants) / sizeof(kLongKVariants[0]);
+    for (size_t i = 0; i < count; ++i) {
+      cudaError_t e = cudaFuncSetAttribute(table[i].fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)table[i].smem);
+      if (e != cudaSuccess) return fail(msg, n, 4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
   }
   return 0;
 }
@@ -225,13 +242,20 @@ int launch_gemm_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   if (p.trans_a && p.m != op.ip[GM_M]) return 5;  // a transposed A cannot be sliced by rows
   if (p.m <= 0 || p.n <= 0) return 0;
   if (!p.trans_a && p.trans_b && p.k % 4 == 0 && !(((uintptr_t)p.a | (uintptr_t)p.b) & 15u)) {
-    // the largest tile that still gives >= 3 CTAs per SM; else the smallest tile
-    const ChainVariant* v = &kChainVariants[sizeof(kChainVariants) / sizeof(kChainVariants[0]) - 1];
-    for (const auto& c : kChainVariants) {
-      const long ctas = (long)((p.m + c.bm - 1) / c.bm) * ((p.n + c.bn - 1) / c.bn);
-      if (ctas >= 3L * ctx.num_sms) {
-        v = &c;
-        break;
+    // long chains: by outputs per SM; else the largest tile that still gives
+    // >= 3 CTAs per SM; else the smallest tile
+    const ChainVariant* v = nullptr;
+    const long outputs = (long)p.m * p.n;
+    if (p.k >= 1024 && outputs >= 1024L * ctx.num_sms) v = &kLongKVariants[0];
+    else if (p.k >= 1024 && outputs >= 256L * ctx.num_sms) v = &kLongKVariants[1];
+    if (!v) {
+      v = &kChainVariants[sizeof(kChainVariants) / sizeof(kChainVariants[0]) - 1];
+      for (const auto& c : kChainVariants) {
+        const long ctas = (long)((p.m + c.bm - 1) / c.bm) * ((p.n + c.bn - 1) / c.bn);
+        if (ctas >= 3L * ctx.num_sms) {
+          v = &c;
+          break;
+        }
       }
     }
     dim3 grid((unsigned)((p.n + v->bn - 1) / v->bn), (unsigned)((p.m + v->bm - 1) / v->bm));

@@ -118,6 +118,10 @@ def test_repeated_runs_are_identical():
     dict(batch=2, channels=32, height=7, width=130, n_convs=3, wscale_range=(0.0001, 0.001)),
     dict(batch=1, channels=128, height=9, width=23, n_convs=4, wscale_range=(0.00002, 0.0002)),
     dict(batch=33, channels=64, height=8, width=8, n_convs=6, wscale_range=(0.0001, 0.001)),
+    # more tiles than SMs: every CTA owns several tiles per layer (rounds), so
+    # layers overlap across CTAs and the progress words order them
+    dict(batch=16, channels=64, height=56, width=56, n_convs=4, wscale_range=(0.0001, 0.001)),
+    dict(batch=12, channels=32, height=40, width=52, n_convs=5, wscale_range=(0.0001, 0.001)),
 ])
 def test_chain_matches_separate_launches_and_port(kw):
     """A conv stack run as one persistent launch (layers ordered by per-tile
