@@ -133,7 +133,6 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(c
   using XC = ExactChain<BM, BN, RM, RN, BK, S>;
   extern __shared__ __align__(16) float xc_smem[];
   pdl_wait();
-  pdl_launch_dependents();
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   uint64_t acc[RM][RN / 2];
 #pragma unroll
@@ -141,6 +140,10 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(c
 #pragma unroll
     for (int c = 0; c < RN / 2; ++c) acc[r][c] = 0;  // +0.0f pairs
   XC::run(p.a, p.k, p.b, p.k, p.m, p.n, p.k, m0, n0, acc, xc_smem);
+  // The next kernel's CTAs may be scheduled only now: launched at the start,
+  // they would sit in their own pdl_wait holding shared memory and thread
+  // slots that this grid's later CTAs need.
+  pdl_launch_dependents();
   const int tx = threadIdx.x % XC::TX, ty = threadIdx.x / XC::TX;
 #pragma unroll
   for (int r = 0; r < RM; ++r) {
@@ -187,15 +190,15 @@ static const ChainVariant kChainVariants[] = {
     EMX_CHAIN_VARIANT(32, 32, 2, 2, 32, 4), EMX_CHAIN_VARIANT(16, 32, 2, 2, 32, 4),
     EMX_CHAIN_VARIANT(16, 16, 2, 2, 32, 4), EMX_CHAIN_VARIANT(8, 16, 1, 2, 32, 4),
 };
-// Long chains (K >= 1024): 256-thread CTAs with 64-wide K stages, chosen by
-// outputs per SM (measured on B200 over tile shapes, 2-8 chains per thread,
-// K stages 32-128 deep, 1-8 CTAs per SM, on the 64 x 1024 -> 4096 -> 1024
-// MLP): with at least 1024 outputs per SM, 4 chains per thread and 3 CTAs per
-// SM (64 x 4096, K 1024: 52 -> 41 us); with fewer, 2 chains per thread and
-// twice the warps to hide the chains' latency (64 x 1024, K 4096: 102 -> 77 us).
+// Long chains over few outputs (K >= 1024, 256 to 1024 outputs per SM):
+// 256-thread CTAs of 2 chains per thread with 64-wide K stages, so each SM
+// holds enough warps to hide the chains' latency (64 x 1024, K 4096, the MLP's
+// second Gemm: the whole MLP plan 147 -> 135 us on B200).  A sweep of 16 tile
+// shapes also favoured 4-chain 256-thread CTAs for the first Gemm when timed
+// alone, but inside the plan (after its predecessor, before the second Gemm)
+// they ran 8 us slower than the small-CTA rule, which stays for that class.
 static const ChainVariant kLongKVariants[] = {
-    EMX_CHAIN_VARIANT(32, 32, 2, 2, 64, 4),  // >= 1024 outputs per SM
-    EMX_CHAIN_VARIANT(16, 32, 1, 2, 64, 4),  // >= 256 outputs per SM
+    EMX_CHAIN_VARIANT(16, 32, 1, 2, 64, 4),
 };
 #undef EMX_CHAIN_VARIANT
 
@@ -242,12 +245,11 @@ int launch_gemm_f32(const PlanOp& op, void* const* ptrs, const OpState*, const L
   if (p.trans_a && p.m != op.ip[GM_M]) return 5;  // a transposed A cannot be sliced by rows
   if (p.m <= 0 || p.n <= 0) return 0;
   if (!p.trans_a && p.trans_b && p.k % 4 == 0 && !(((uintptr_t)p.a | (uintptr_t)p.b) & 15u)) {
-    // long chains: by outputs per SM; else the largest tile that still gives
+    // long chains over few outputs; else the largest tile that still gives
     // >= 3 CTAs per SM; else the smallest tile
     const ChainVariant* v = nullptr;
     const long outputs = (long)p.m * p.n;
-    if (p.k >= 1024 && outputs >= 1024L * ctx.num_sms) v = &kLongKVariants[0];
-    else if (p.k >= 1024 && outputs >= 256L * ctx.num_sms) v = &kLongKVariants[1];
+    if (p.k >= 1024 && outputs >= 256L * ctx.num_sms && outputs < 1024L * ctx.num_sms) v = &kLongKVariants[0];
     if (!v) {
       v = &kChainVariants[sizeof(kChainVariants) / sizeof(kChainVariants[0]) - 1];
       for (const auto& c : kChainVariants) {
