@@ -16,8 +16,10 @@
 //
 // Work split: one CTA per (128 query rows, head, batch); heads in groups of 8
 // run all their query tiles together (K/V stay in L2), heaviest causal query
-// tiles first within a group.  Warp 0: TMA producer (the Q tile once, then K and V
-// tiles of 128 keys, double-buffered).  Warp 1: issues S_j = Q K_j^T into one
+// tiles first within a group.  Two CTAs share an SM (112 KB of shared memory
+// and 256 TMEM columns each), so each scheduler holds two softmax warps: one
+// CTA's exponentials overlap the other's MMAs and TMEM loads.  Warp 0: TMA
+// producer (the Q tile once, then K and V tiles of 64 keys, double-buffered).  Warp 1: issues S_j = Q K_j^T into one
 // of two TMEM score buffers.  Warp 2: issues O += P_j V_j into the TMEM output
 // accumulator.  Warps 4-7: one thread per query row -- scores from TMEM,
 // running max, exponentials, P_j (fp16) into shared memory, row sums, and the
@@ -27,13 +29,15 @@
 // accumulators hold exactly as well.
 //
 // Operands in shared memory, all 128-byte swizzled (the TMA writes them so):
-//   Q, K tiles [128 rows][128 d] fp16 as two 64-wide slabs [128][128 B]: the
-//   K-major A / B operands of S = Q K^T;
-//   P [128 queries][128 keys] fp16, same layout, written by the softmax
+//   Q tile [128 rows][128 d] and K tiles [64 keys][128 d] fp16 as two 64-wide
+//   slabs [rows][128 B]: the K-major A / B operands of S = Q K^T;
+//   P [128 queries][64 keys] fp16, one such slab, written by the softmax
 //   threads: the K-major A operand of O += P V;
-//   V tile [128 keys][128 d] as two 64-wide d slabs: the B operand of P V in
-//   MN-major form (N = d contiguous), slabs 16 KB apart (LBO), 8-key groups
+//   V tile [64 keys][128 d] as two 64-wide d slabs: the B operand of P V in
+//   MN-major form (N = d contiguous), slabs 8 KB apart (LBO), 8-key groups
 //   1 KB apart (SBO).
+// The shared-memory window must start on a 1 KB boundary (the swizzle atom);
+// the kernel checks it and reports DEV_BAD_CONFIG otherwise.
 // Every wait is bounded (tc100.cuh) and reports through the plan's error word.
 #include <cuda_fp16.h>
 
@@ -44,11 +48,16 @@
 namespace emx {
 
 constexpr int ATC_M = 128;        // query rows per CTA
-constexpr int ATC_N = 128;        // keys per K / V tile
+constexpr int ATC_N = 64;         // keys per K / V tile
 constexpr int ATC_D = 128;        // head size (Q/K and V)
 constexpr int ATC_THREADS = 256;  // 8 warps
-constexpr uint32_t ATC_SLAB = 128u * 128u;     // one 64-wide slab of a 128-row tile: 16 KB
-constexpr uint32_t ATC_TILE = 2u * ATC_SLAB;   // a 128 x 128 fp16 tile: 32 KB
+constexpr uint32_t ATC_QSLAB = (uint32_t)ATC_M * 128u;  // one 64-wide d slab of the Q tile: 16 KB
+constexpr uint32_t ATC_QTILE = 2u * ATC_QSLAB;          // Q tile: 32 KB
+constexpr uint32_t ATC_KSLAB = (uint32_t)ATC_N * 128u;  // one 64-wide d slab of a K or V tile: 8 KB
+constexpr uint32_t ATC_KTILE = 2u * ATC_KSLAB;          // K or V tile: 16 KB
+constexpr uint32_t ATC_PTILE = (uint32_t)ATC_M * ATC_N * 2u;  // P: 16 KB (one 128-byte-row slab)
+constexpr uint32_t ATC_TMEM_COLS = 256;  // score buffers at columns 0 and ATC_N, output at ATC_O_COL
+constexpr uint32_t ATC_O_COL = 2u * ATC_N;
 constexpr float ATC_RESCALE = 8.0f;            // lazy-rescale threshold, log2 units
 constexpr int ATC_GROUP = 8;                   // heads whose query tiles run together
 
@@ -127,14 +136,18 @@ __device__ __forceinline__ uint64_t atc_desc_mn(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
-__global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __grid_constant__ AttnTcParams p) {
+__global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __grid_constant__ AttnTcParams p) {
   extern __shared__ __align__(1024) uint8_t atc_raw[];
-  uint8_t* sm = atc_raw + ((1024u - (smem_u32(atc_raw) & 1023u)) & 1023u);
+  if (smem_u32(atc_raw) & 1023u) {  // the swizzled operands need a 1 KB aligned window
+    if (threadIdx.x == 0) record_error(p.err, DEV_BAD_CONFIG);
+    return;
+  }
+  uint8_t* sm = atc_raw;
   uint8_t* s_q = sm;
-  uint8_t* s_k = sm + ATC_TILE;          // [2] K stages
-  uint8_t* s_v = s_k + 2 * ATC_TILE;     // [2] V stages
-  uint8_t* s_p = s_v + 2 * ATC_TILE;     // P
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_p + ATC_TILE);
+  uint8_t* s_k = sm + ATC_QTILE;          // [2] K stages
+  uint8_t* s_v = s_k + 2 * ATC_KTILE;     // [2] V stages
+  uint8_t* s_p = s_v + 2 * ATC_KTILE;     // P
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_p + ATC_PTILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -182,13 +195,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(holder, 512);
+    tmem_alloc(holder, ATC_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *holder;  // score buffers at columns 0 and 128, output accumulator at 256
+  const uint32_t tmem = *holder;  // score buffers at columns 0 and ATC_N, output accumulator at ATC_O_COL
   pdl_launch_dependents();
 
   if (warp == 0) {
@@ -197,9 +210,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       pdl_wait();  // Q, K, V may come from the preceding kernel
       bool ok = true;
       int k_last[2] = {-1, -1}, v_last[2] = {-1, -1};  // per stage: last tile whose loads were issued
-      mbar_arrive_expect_tx(q_full, ATC_TILE);
+      mbar_arrive_expect_tx(q_full, ATC_QTILE);
       tma_load_4d(s_q, &p.map_q, q_full, 0, q0, h, b);
-      tma_load_4d(s_q + ATC_SLAB, &p.map_q, q_full, 64, q0, h, b);
+      tma_load_4d(s_q + ATC_QSLAB, &p.map_q, q_full, 64, q0, h, b);
       for (int j = 0; j < J && ok; ++j) {
         const int s = j & 1;
         const int key0 = j * ATC_N;
@@ -207,17 +220,17 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[s], ATC_TILE);
-        tma_load_4d(s_k + s * ATC_TILE, &p.map_k, &k_full[s], 0, key0, kvh, b);
-        tma_load_4d(s_k + s * ATC_TILE + ATC_SLAB, &p.map_k, &k_full[s], 64, key0, kvh, b);
+        mbar_arrive_expect_tx(&k_full[s], ATC_KTILE);
+        tma_load_4d(s_k + s * ATC_KTILE, &p.map_k, &k_full[s], 0, key0, kvh, b);
+        tma_load_4d(s_k + s * ATC_KTILE + ATC_KSLAB, &p.map_k, &k_full[s], 64, key0, kvh, b);
         k_last[s] = j;
         if (j >= 2 && !mbar_wait(&v_empty[s], (uint32_t)((j >> 1) - 1) & 1u, err, DEV_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&v_full[s], ATC_TILE);
-        tma_load_4d(s_v + s * ATC_TILE, &p.map_v, &v_full[s], 0, key0, kvh, b);
-        tma_load_4d(s_v + s * ATC_TILE + ATC_SLAB, &p.map_v, &v_full[s], 64, key0, kvh, b);
+        mbar_arrive_expect_tx(&v_full[s], ATC_KTILE);
+        tma_load_4d(s_v + s * ATC_KTILE, &p.map_v, &v_full[s], 0, key0, kvh, b);
+        tma_load_4d(s_v + s * ATC_KTILE + ATC_KSLAB, &p.map_v, &v_full[s], 64, key0, kvh, b);
         v_last[s] = j;
       }
       if (!ok) {  // error path: let the copies in flight land before the CTA exits
@@ -238,11 +251,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         if (!mbar_wait(&k_full[s], (uint32_t)(j >> 1) & 1u, err, DEV_TIMEOUT_MMA)) break;
         if (j >= 2 && !mbar_wait(&s_empty[s], (uint32_t)((j >> 1) - 1) & 1u, err, DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t qa = smem_u32(s_q), kb = smem_u32(s_k + s * ATC_TILE);
+        const uint32_t qa = smem_u32(s_q), kb = smem_u32(s_k + s * ATC_KTILE);
 #pragma unroll
         for (int ks = 0; ks < ATC_D / 16; ++ks) {
-          const uint32_t off = (uint32_t)(ks >> 2) * ATC_SLAB + (uint32_t)(ks & 3) * 32u;
-          mma_f16(tmem + (uint32_t)(s * ATC_N), atc_desc_k(qa + off), atc_desc_k(kb + off), idesc, ks > 0 ? 1u : 0u);
+          const uint32_t qoff = (uint32_t)(ks >> 2) * ATC_QSLAB + (uint32_t)(ks & 3) * 32u;
+          const uint32_t koff = (uint32_t)(ks >> 2) * ATC_KSLAB + (uint32_t)(ks & 3) * 32u;
+          mma_f16(tmem + (uint32_t)(s * ATC_N), atc_desc_k(qa + qoff), atc_desc_k(kb + koff), idesc,
+                  ks > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[s]);
         tc_commit(&k_empty[s]);
@@ -260,12 +275,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         if (!mbar_wait(p_full, (uint32_t)j & 1u, err, DEV_TIMEOUT_MMA)) break;
         if (!mbar_wait(&v_full[s], (uint32_t)(j >> 1) & 1u, err, DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t pa = smem_u32(s_p), vb = smem_u32(s_v + s * ATC_TILE);
+        const uint32_t pa = smem_u32(s_p), vb = smem_u32(s_v + s * ATC_KTILE);
 #pragma unroll
         for (int kk = 0; kk < ATC_N / 16; ++kk) {
-          const uint32_t aoff = (uint32_t)(kk >> 2) * ATC_SLAB + (uint32_t)(kk & 3) * 32u;
-          const uint64_t bdesc = atc_desc_mn(vb + (uint32_t)kk * 16u * 128u, ATC_SLAB, 1024u);
-          mma_f16(tmem + 256u, atc_desc_k(pa + aoff), bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t aoff = (uint32_t)kk * 32u;  // P is one 128-byte-row slab: 16 keys = 32 bytes
+          const uint64_t bdesc = atc_desc_mn(vb + (uint32_t)kk * 16u * 128u, ATC_KSLAB, 1024u);
+          mma_f16(tmem + ATC_O_COL, atc_desc_k(pa + aoff), bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(o_done);
         tc_commit(&v_empty[s]);
@@ -292,9 +307,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         break;
       }
       tc_fence_after();
-      uint32_t sv[4][32];
+      constexpr int NC = ATC_N / 32;  // 32-column chunks of a score row
+      uint32_t sv[NC][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + (uint32_t)(s * ATC_N + 32 * c), sv[c]);
+      for (int c = 0; c < NC; ++c) tmem_ld32(tmem + lane_base + (uint32_t)(s * ATC_N + 32 * c), sv[c]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       const int nvalid = min(ATC_N, max(0, row_last - j * ATC_N + 1));  // keys [0, nvalid) of the tile are visible
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float x = __uint_as_float(sv[c][i]) * p.scale_log2;
@@ -318,9 +334,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       const float alpha = rescale ? ex2_approx(m_used - m_new) : 1.0f;
       l *= alpha;
       // exponentials against m_new, rounded to fp16 (the P.V operand); the row sum adds the same values
-      uint32_t pw[4][16];
+      uint32_t pw[NC][16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k0 = 32 * c + 2 * i;
@@ -342,20 +358,20 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_base + 256u + 32u * c, o);
+            tmem_ld32(tmem + lane_base + ATC_O_COL + 32u * c, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_base + 256u + 32u * c, o);
+            tmem_st32(tmem + lane_base + ATC_O_COL + 32u * c, o);
           }
           tmem_wait_st();
         }
       }
-      // P row r: keys 8g .. 8g+7 are 16-byte chunk g % 8 of slab g / 8, swizzled by the row
+      // P row r: keys 8g .. 8g+7 are 16-byte chunk g of the row, swizzled by the row
 #pragma unroll
-      for (int g = 0; g < 16; ++g) {
+      for (int g = 0; g < ATC_N / 8; ++g) {
         const int c = g >> 2, i = (g & 3) * 4;
-        uint8_t* dst = s_p + (g >> 3) * ATC_SLAB + r * 128 + (((g & 7) ^ (r & 7)) << 4);
+        uint8_t* dst = s_p + r * 128 + ((g ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(pw[c][i], pw[c][i + 1], pw[c][i + 2], pw[c][i + 3]);
       }
       fence_async_shared();  // the generic writes of P become visible to the tensor cores
@@ -377,7 +393,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         if (J > 0) {
-          tmem_ld32(tmem + lane_base + 256u + 32u * c, o);
+          tmem_ld32(tmem + lane_base + ATC_O_COL + 32u * c, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -401,12 +417,14 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, ATC_TMEM_COLS);
   }
 }
 
 // ------------------------------------------------------------------ host side
-constexpr size_t ATC_SMEM = 1024 + 6 * (size_t)ATC_TILE + 256;
+// no alignment slack: two CTAs of this size fit one SM only without it (the
+// kernel checks that the window starts on a 1 KB boundary)
+constexpr size_t ATC_SMEM = (size_t)ATC_QTILE + 4 * (size_t)ATC_KTILE + ATC_PTILE + 256;
 
 // The fast mode needs 128-wide fp16 heads and 16-byte aligned token strides.
 int prepare_attention_tc(const PlanOp& op, void* const*, OpState*, int, char* msg, size_t n) {
@@ -420,14 +438,15 @@ int prepare_attention_tc(const PlanOp& op, void* const*, OpState*, int, char* ms
   return 0;
 }
 
-// 4-D map (d, t, h, b) over an fp16 tensor with element strides (1, st, sh, sb).
+// 4-D map (d, t, h, b) over an fp16 tensor with element strides (1, st, sh, sb),
+// boxes of 64 d x `rows` tokens.
 static int make_tmap_attn(CUtensorMap* map, const void* base, int64_t t, int64_t heads, int64_t batch, int64_t st,
-                          int64_t sh, int64_t sb) {
+                          int64_t sh, int64_t sb, uint32_t rows) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc || ((uintptr_t)base & 15u)) return 5;
   cuuint64_t dims[4] = {(cuuint64_t)ATC_D, (cuuint64_t)t, (cuuint64_t)heads, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {64, ATC_N, 1, 1};
+  cuuint32_t box[4] = {64, rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -454,9 +473,9 @@ int launch_attention_tc(const PlanOp& op, void* const* ptrs, const OpState*, con
   p.err = ctx.d_error;
   if (p.B <= 0 || p.TQ <= 0) return 0;
   const int hkv = p.HQ / p.group;
-  int rc = make_tmap_attn(&p.map_q, ptrs[op.t[0]], p.TQ, p.HQ, p.B, s[2], s[1], s[0]);
-  if (!rc) rc = make_tmap_attn(&p.map_k, ptrs[op.t[1]], p.TK, hkv, p.B, s[5], s[4], s[3]);
-  if (!rc) rc = make_tmap_attn(&p.map_v, ptrs[op.t[2]], p.TK, hkv, p.B, s[8], s[7], s[6]);
+  int rc = make_tmap_attn(&p.map_q, ptrs[op.t[0]], p.TQ, p.HQ, p.B, s[2], s[1], s[0], ATC_M);
+  if (!rc) rc = make_tmap_attn(&p.map_k, ptrs[op.t[1]], p.TK, hkv, p.B, s[5], s[4], s[3], ATC_N);
+  if (!rc) rc = make_tmap_attn(&p.map_v, ptrs[op.t[2]], p.TK, hkv, p.B, s[8], s[7], s[6], ATC_N);
   if (rc) return rc;
   const unsigned grid = (unsigned)(p.n_qtiles * p.HQ * p.B);
   cudaError_t e = launch_pdl(attention_tc_kernel, dim3(grid), dim3(ATC_THREADS), ATC_SMEM, ctx.stream, p);
