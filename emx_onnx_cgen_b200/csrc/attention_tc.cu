@@ -316,15 +316,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);  // the score buffer may be overwritten
       const int nvalid = min(ATC_N, max(0, row_last - j * ATC_N + 1));  // keys [0, nvalid) of the tile are visible
-      float mx = -INFINITY;
+      // Row maximum in 4 independent partials (max is exact in any order).  With a
+      // positive scale the maximum of the scaled scores is the scaled maximum
+      // (rounding is monotone), so the scores stay raw and each exponential takes
+      // one fma: 2^(s * scale_log2 - m).
+      const float sc = p.scale_log2;
+      const bool pos = sc > 0.0f;
+      float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(sv[c][i]) * p.scale_log2;
-          sv[c][i] = __float_as_uint(x);
-          if (32 * c + i < nvalid) mx = fmaxf(mx, x);
+          float x = __uint_as_float(sv[c][i]);
+          if (!pos) {
+            x *= sc;
+            sv[c][i] = __float_as_uint(x);
+          }
+          if (32 * c + i < nvalid) mxp[i & 3] = fmaxf(mxp[i & 3], x);
         }
+      float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+      if (pos) mx *= sc;
+      const float mul = pos ? sc : 1.0f;
       float m_new = m_used;
       bool rescale = false;
       if (mx > m_used + ATC_RESCALE || m_used == -INFINITY) {
@@ -332,19 +344,22 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
         rescale = j > 0 && m_used != -INFINITY;
       }
       const float alpha = rescale ? ex2_approx(m_used - m_new) : 1.0f;
-      l *= alpha;
-      // exponentials against m_new, rounded to fp16 (the P.V operand); the row sum adds the same values
+      // exponentials against m_new, rounded to fp16 (the P.V operand); the row sum adds the same
+      // values, in 4 independent partials
       uint32_t pw[NC][16];
+      float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const float neg_m = -m_new;
 #pragma unroll
       for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k0 = 32 * c + 2 * i;
-          const float e0 = k0 < nvalid ? ex2_approx(__uint_as_float(sv[c][2 * i]) - m_new) : 0.0f;
-          const float e1 = k0 + 1 < nvalid ? ex2_approx(__uint_as_float(sv[c][2 * i + 1]) - m_new) : 0.0f;
+          const float e0 = k0 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i]), mul, neg_m)) : 0.0f;
+          const float e1 = k0 + 1 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i + 1]), mul, neg_m)) : 0.0f;
           pw[c][i] = pack_f16x2(e0, e1);
-          l += f16lo(pw[c][i]) + f16hi(pw[c][i]);
+          lp[i & 3] += f16lo(pw[c][i]) + f16hi(pw[c][i]);
         }
+      l = l * alpha + ((lp[0] + lp[1]) + (lp[2] + lp[3]));
       m_used = m_new;
       // P_{j-1} V_{j-1} must be done before P is overwritten and O rescaled
       if (j > 0) {
