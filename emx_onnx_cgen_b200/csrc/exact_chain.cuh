@@ -9,11 +9,11 @@
 // __fmul_rn followed by a __fadd_rn, which CUDA never merges into an FMA.
 // (Packed f32x2 multiply/add pairs were measured to be contracted into
 // fused multiply-adds by the code generator here, which changes the
-// rounding, so they are not used.)  Accumulators are kept as pairs of
-// floats in 64-bit registers.
+// rounding, so they are not used.)  Accumulators are plain floats: packing
+// them as pairs in 64-bit integers cost integer instructions per step.
 //
 // Thread (tx, ty) of the CTA owns rows m0 + ty*RM + r (r < RM) and columns
-// n0 + tx + c*TX (c < RN, TX = BN / RN): columns are strided so that the
+// n0 + tx + c*TX (c < RN, TX = BN / RN), accumulator acc[r][c]: columns are strided so that the
 // threads of a quarter warp read consecutive shared-memory rows
 // (conflict-free 16-byte loads).  A is [M][K] with row pitch lda, B is [N][K]
 // with row pitch ldb (K contiguous in both), K % 4 == 0, both bases and pitches
@@ -22,12 +22,6 @@
 #include <stdint.h>
 
 namespace emx {
-
-__device__ __forceinline__ uint64_t xc_pack(float lo, float hi) {
-  return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
-}
-__device__ __forceinline__ float xc_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float xc_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
 __device__ __forceinline__ void xc_cp16(float* dst, const float* src, bool valid) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
@@ -60,7 +54,7 @@ __device__ __forceinline__ void xc_wait() {
 // B_KEEP: B's rows are loaded with an L2 evict-last policy (B re-read by later launches).
 template <int BM, int BN, int RM, int RN, int BK, int S, bool B_KEEP = false>
 struct ExactChain {
-  static_assert(RN % 2 == 0 && BK % 4 == 0 && RM >= 1, "tile shape");
+  static_assert(RN >= 1 && BK % 4 == 0 && RM >= 1, "tile shape");
   static constexpr int TX = BN / RN, TY = BM / RM, NT = TX * TY;
   static constexpr int PITCH = BK + 4;  // floats per shared-memory row (keeps 16-byte rows, shifts banks)
   static constexpr size_t SMEM_BYTES = (size_t)S * (BM + BN) * PITCH * sizeof(float);
@@ -86,8 +80,8 @@ struct ExactChain {
   }
 
   static __device__ __forceinline__ void run(const float* __restrict__ A, int lda, const float* __restrict__ B,
-                                             int ldb, int M, int N, int K, int m0, int n0,
-                                             uint64_t (&acc)[RM][RN / 2], float* smem) {
+                                             int ldb, int M, int N, int K, int m0, int n0, float (&acc)[RM][RN],
+                                             float* smem) {
     const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
     float* As = smem;                          // [S][BM][PITCH]
     float* Bs = smem + (size_t)S * BM * PITCH;  // [S][BN][PITCH]
@@ -117,21 +111,14 @@ struct ExactChain {
         for (int c = 0; c < RN; ++c) b4[c] = *reinterpret_cast<const float4*>(bs + c * TX * PITCH + kk);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          uint64_t b2[RN / 2];
+          float bj[RN];
 #pragma unroll
-          for (int c = 0; c < RN / 2; ++c) {
-            const float lo = j == 0 ? b4[2 * c].x : j == 1 ? b4[2 * c].y : j == 2 ? b4[2 * c].z : b4[2 * c].w;
-            const float hi =
-                j == 0 ? b4[2 * c + 1].x : j == 1 ? b4[2 * c + 1].y : j == 2 ? b4[2 * c + 1].z : b4[2 * c + 1].w;
-            b2[c] = xc_pack(lo, hi);
-          }
+          for (int c = 0; c < RN; ++c) bj[c] = j == 0 ? b4[c].x : j == 1 ? b4[c].y : j == 2 ? b4[c].z : b4[c].w;
 #pragma unroll
           for (int r = 0; r < RM; ++r) {
             const float a = j == 0 ? a4[r].x : j == 1 ? a4[r].y : j == 2 ? a4[r].z : a4[r].w;
 #pragma unroll
-            for (int c = 0; c < RN / 2; ++c)
-              acc[r][c] = xc_pack(__fadd_rn(xc_lo(acc[r][c]), __fmul_rn(a, xc_lo(b2[c]))),
-                                  __fadd_rn(xc_hi(acc[r][c]), __fmul_rn(a, xc_hi(b2[c]))));
+            for (int c = 0; c < RN; ++c) acc[r][c] = __fadd_rn(acc[r][c], __fmul_rn(a, bj[c]));
           }
         }
       }
@@ -140,8 +127,8 @@ struct ExactChain {
     __syncthreads();
   }
 
-  // column of pair c (0..RN/2-1), half h (0/1) for thread tx
-  static __device__ __forceinline__ int col(int tx, int c, int h) { return tx + (2 * c + h) * TX; }
+  // column of accumulator c (0..RN-1) for thread tx
+  static __device__ __forceinline__ int col(int tx, int c) { return tx + c * TX; }
 };
 
 }  // namespace emx

@@ -134,11 +134,11 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(c
   extern __shared__ __align__(16) float xc_smem[];
   pdl_wait();
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  uint64_t acc[RM][RN / 2];
+  float acc[RM][RN];
 #pragma unroll
   for (int r = 0; r < RM; ++r)
 #pragma unroll
-    for (int c = 0; c < RN / 2; ++c) acc[r][c] = 0;  // +0.0f pairs
+    for (int c = 0; c < RN; ++c) acc[r][c] = 0.0f;
   XC::run(p.a, p.k, p.b, p.k, p.m, p.n, p.k, m0, n0, acc, xc_smem);
   // The next kernel's CTAs may be scheduled only now: launched at the start,
   // they would sit in their own pdl_wait holding shared memory and thread
@@ -150,12 +150,10 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(c
     const int i = m0 + ty * RM + r;
     if (i >= p.m) continue;
 #pragma unroll
-    for (int c = 0; c < RN / 2; ++c)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = n0 + XC::col(tx, c, h);
+    for (int c = 0; c < RN; ++c) {
+        const int j = n0 + XC::col(tx, c);
         if (j >= p.n) continue;
-        const float a = h ? xc_hi(acc[r][c]) : xc_lo(acc[r][c]);
+        const float a = acc[r][c];
         float y;
         if (p.bias_mode) {
           float bias;

@@ -49,9 +49,11 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
   pdl_wait();
   pdl_launch_dependents();
   const int m0 = blockIdx.y * GX_BM, n0 = blockIdx.x * GX_BN;
-  uint64_t acc[4][2];
+  float acc[4][4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = 0;  // +0.0f pairs
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
   GxChain::run(x, K, wp, K, M, N, K, m0, n0, acc, xc_smem);
   const int tx = threadIdx.x % GxChain::TX, ty = threadIdx.x / GxChain::TX;
   // the partials (T*B x 4Hp floats, read once by their step) must not push the
@@ -62,12 +64,10 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
     const int m = m0 + ty * 4 + r;
     if (m >= M) continue;
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = n0 + GxChain::col(tx, c, h);
-        if (n < N) st_evict_first(gx + (size_t)m * N + n, h ? xc_hi(acc[r][c]) : xc_lo(acc[r][c]), pol);
-      }
+    for (int c = 0; c < 4; ++c) {
+      const int n = n0 + GxChain::col(tx, c);
+      if (n < N) st_evict_first(gx + (size_t)m * N + n, acc[r][c], pol);
+    }
   }
 }
 
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
   const int tx = threadIdx.x % StChain::TX, ty = threadIdx.x / StChain::TX;
   pdl_wait();  // h_prev and c come from the previous step
   pdl_launch_dependents();
-  uint64_t acc[ST_RM][2];
+  float acc[ST_RM][4];
   const float* g0 = p.gx + (size_t)p.t * p.B * p.N;
   const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
     if (m < p.B)
 #pragma unroll
       for (int q = 0; q < 4; ++q) g[q] = ld_evict_first(g0 + (size_t)m * p.N + n0 + tx + q * StChain::TX, pol);
-    acc[r][0] = xc_pack(g[0], g[1]);
-    acc[r][1] = xc_pack(g[2], g[3]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[r][q] = g[q];
   }
   StChain::run(p.h_prev, p.H, p.rp, p.H, p.B, p.N, p.H, m0, n0, acc, xc_smem);
   const int h = (n0 / ST_BN) * LS_TILE_UNITS + tx;
@@ -123,10 +123,10 @@ __global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepPa
   for (int r = 0; r < ST_RM; ++r) {
     const int b = m0 + ty * ST_RM + r;
     if (b >= p.B) continue;
-    const float gi = __fadd_rn(xc_lo(acc[r][0]), bs[0]);
-    const float go = __fadd_rn(xc_hi(acc[r][0]), bs[1]);
-    const float gf = __fadd_rn(xc_lo(acc[r][1]), bs[2]);
-    const float gc = __fadd_rn(xc_hi(acc[r][1]), bs[3]);
+    const float gi = __fadd_rn(acc[r][0], bs[0]);
+    const float go = __fadd_rn(acc[r][1], bs[1]);
+    const float gf = __fadd_rn(acc[r][2], bs[2]);
+    const float gc = __fadd_rn(acc[r][3], bs[3]);
     const float ig = sigmoid_ref(gi);
     const float fg = sigmoid_ref(gf);
     const float cg = tanhf(gc);
