@@ -188,6 +188,8 @@ def cmd_export(args) -> int:
 
 
 def _common(p):
+    p.add_argument("--target", choices=["b200"], default="b200",
+                   help="emit target: a B200 launch plan (the reference CLI's C target stays with the reference)")
     p.add_argument("--input-dim", action="append", default=[],
                    help="pin a dynamic dimension: NAME=INT (every axis named NAME) or INPUT:AXIS=INT")
     p.add_argument("--weights-bin", type=Path, default=None,

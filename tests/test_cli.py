@@ -207,3 +207,13 @@ def test_integer_outputs_compare_exactly():
     b[7] = 0
     c = check_output("y", a, b)
     assert not c.ok and c.mismatches == 1 and c.worst[0] == (7,)
+
+
+def test_target_flag(tmp_path, capsys):
+    """``compile --target b200`` is the B200 emit target; other targets are the reference CLI's."""
+    wl = W.mlp_fp32(m=4, k=64, hidden=128)
+    model = write_onnx(wl.graph, tmp_path / "m.onnx")
+    assert cli.main(["compile", str(model), "--target", "b200", "-o", str(tmp_path / "out")]) == 0
+    assert (tmp_path / "out" / f"{wl.graph.name}.plan").exists()
+    with pytest.raises(SystemExit):
+        cli.main(["compile", str(model), "--target", "c"])
