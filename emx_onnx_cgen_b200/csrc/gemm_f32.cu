@@ -182,21 +182,23 @@ struct ChainVariant {
 #define EMX_CHAIN_VARIANT(BM, BN, RM, RN, BK, S)                                                 \
   {BM, BN, (BM / RM) * (BN / RN), ExactChain<BM, BN, RM, RN, BK, S>::SMEM_BYTES,                 \
    gemm_f32_chain_kernel<BM, BN, RM, RN, BK, S>}
-// Several CTAs per SM, a short K stage (small problems, many CTAs)
+// Several CTAs per SM (many outputs).  64-wide K stages where the tile is
+// small enough to keep three to four CTAs on an SM (64 x 4096, K 1024: 39 ->
+// 37.5 us alone on B200).
 static const ChainVariant kChainVariants[] = {
     EMX_CHAIN_VARIANT(64, 64, 4, 4, 32, 4), EMX_CHAIN_VARIANT(32, 64, 4, 4, 32, 4),
-    EMX_CHAIN_VARIANT(32, 32, 2, 2, 32, 4), EMX_CHAIN_VARIANT(16, 32, 2, 2, 32, 4),
+    EMX_CHAIN_VARIANT(32, 32, 2, 2, 64, 4), EMX_CHAIN_VARIANT(16, 32, 2, 2, 64, 4),
     EMX_CHAIN_VARIANT(16, 16, 2, 2, 32, 4), EMX_CHAIN_VARIANT(8, 16, 1, 2, 32, 4),
 };
 // Long chains over few outputs (K >= 1024, 256 to 1024 outputs per SM):
-// 256-thread CTAs of 2 chains per thread with 64-wide K stages, so each SM
-// holds enough warps to hide the chains' latency (64 x 1024, K 4096, the MLP's
-// second Gemm: the whole MLP plan 147 -> 135 us on B200).  A sweep of 16 tile
-// shapes also favoured 4-chain 256-thread CTAs for the first Gemm when timed
-// alone, but inside the plan (after its predecessor, before the second Gemm)
-// they ran 8 us slower than the small-CTA rule, which stays for that class.
+// 256-thread CTAs of 2 chains per thread (two rows of one column) with 64-wide
+// K stages, so each SM holds enough warps to hide the chains' latency.  A
+// sweep of 29 tile shapes on 64 x 1024, K 4096 (the MLP's second Gemm) on
+// B200 put this one first (57.5 us alone; 1-chain tiles 72 us, 4-chain tiles
+// 68-70 us, 148 CTAs of 14 columns 68 us, deeper rings of 6 or 8 stages no
+// faster: shared-memory operand reads, not the copy latency, bound it).
 static const ChainVariant kLongKVariants[] = {
-    EMX_CHAIN_VARIANT(16, 32, 1, 2, 64, 4),
+    EMX_CHAIN_VARIANT(32, 16, 2, 1, 64, 4),
 };
 #undef EMX_CHAIN_VARIANT
 

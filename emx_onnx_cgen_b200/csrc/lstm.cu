@@ -74,9 +74,9 @@ __global__ void __launch_bounds__(GxChain::NT) lstm_gx_kernel(const float* __res
 // ---- 2. one recurrent step.  A 64-column tile holds LS_TILE_UNITS = 16 units:
 // thread tx's four columns tx + g*16 are gates g = i, o, f, c of unit
 // tile*16 + tx, so the cell update runs in the thread that owns the chains.
-constexpr int ST_RM = 4;  // batch rows per thread (8 warps' rows = the CTA's ST_BM)
-using StChain = ExactChain<8 * ST_RM, 64, ST_RM, 4, 32, 4, true>;  // R kept in L2 across steps
-constexpr int ST_BM = 8 * ST_RM, ST_BN = 64;
+constexpr int ST_RM = 4;  // batch rows per thread (16 row groups of threads = the CTA's ST_BM rows)
+using StChain = ExactChain<16 * ST_RM, 64, ST_RM, 4, 32, 4>;
+constexpr int ST_BM = 16 * ST_RM, ST_BN = 64;
 static_assert(StChain::TX == LS_TILE_UNITS && ST_BN == 4 * LS_TILE_UNITS, "gate tile layout");
 
 struct LstmStepParams {
