@@ -148,7 +148,7 @@ __global__ void attn_stats_kernel(const uint16_t* __restrict__ q, int64_t nq, co
   }
 }
 
-__global__ void __launch_bounds__(AT_THREADS) attention_exact_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(AT_THREADS) attention_exact_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t at_smem[];
   uint16_t* qs = reinterpret_cast<uint16_t*>(at_smem);        // [QB][D]
   uint16_t* kt = qs + AT_QB * p.D;                              // [D][KT]
@@ -309,7 +309,7 @@ constexpr int AE_QB = 16;      // query rows per CTA
 constexpr int AE_KT = 128;     // keys per K / V tile
 constexpr int AE_THREADS = 256;
 
-__global__ void __launch_bounds__(AE_THREADS, 2) attention_exact2_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(AE_THREADS, 2) attention_exact2_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t ae_smem[];
   uint16_t* qT = reinterpret_cast<uint16_t*>(ae_smem);       // [D][QB]
   uint16_t* kv = qT + p.D * AE_QB;                            // K tile [D][KT], later V tile [KT][DV]

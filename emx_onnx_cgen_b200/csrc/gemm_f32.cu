@@ -30,7 +30,7 @@ struct GemmF32Params {
 };
 
 template <int BM, int BN, int RM, int RN>
-__global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const GemmF32Params p) {
+__global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const __grid_constant__ GemmF32Params p) {
   constexpr int BK = 16;
   constexpr int TX = BN / RN, TY = BM / RM, NT = TX * TY;
   __shared__ __align__(16) float As[2][BK][BM];
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_kernel(const G
 // Y = op(A) * B^T with A [M][K] and B [N][K] row-major (no transA, transB = 1:
 // K contiguous in both): the cp.async-pipelined exact chains of exact_chain.cuh.
 template <int BM, int BN, int RM, int RN, int BK = 32, int S = 4>
-__global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(const GemmF32Params p) {
+__global__ void __launch_bounds__((BM / RM) * (BN / RN)) gemm_f32_chain_kernel(const __grid_constant__ GemmF32Params p) {
   using XC = ExactChain<BM, BN, RM, RN, BK, S>;
   extern __shared__ __align__(16) float xc_smem[];
   pdl_wait();

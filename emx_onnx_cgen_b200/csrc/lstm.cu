@@ -94,7 +94,7 @@ struct LstmStepParams {
 
 __device__ __forceinline__ float sigmoid_ref(float a) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a))); }
 
-__global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const LstmStepParams p) {
+__global__ void __launch_bounds__(StChain::NT) lstm_step_kernel(const __grid_constant__ LstmStepParams p) {
   extern __shared__ __align__(16) float xc_smem[];
   const int m0 = blockIdx.y * ST_BM, n0 = blockIdx.x * ST_BN;
   const int tx = threadIdx.x % StChain::TX, ty = threadIdx.x / StChain::TX;

@@ -31,7 +31,7 @@ __device__ __forceinline__ int32_t load8(const uint8_t* p, int64_t i, int is_sig
 }
 
 // ------------------------------------------------------------------ QLinearMatMul / MatMulInteger
-__global__ void qmatmul_kernel(const QMatMulParams p) {
+__global__ void qmatmul_kernel(const __grid_constant__ QMatMulParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int n = blockIdx.x * 32 + (threadIdx.x & 31);
@@ -96,7 +96,7 @@ struct ConvF32Params {
   int zero_taps_ok;  // out-of-image taps may be added as zeros (planner-checked weights and bias)
 };
 
-__global__ void conv2d_f32_kernel(const ConvF32Params p) {
+__global__ void conv2d_f32_kernel(const __grid_constant__ ConvF32Params p) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;
@@ -175,7 +175,7 @@ __device__ __forceinline__ void conv_tile_channel(float (&acc)[CT_RI][4], const 
 }
 
 template <int TAPS>
-__global__ void __launch_bounds__(CT_THREADS) conv2d_f32_tiled_kernel(const ConvF32Params p, int p_tiles,
+__global__ void __launch_bounds__(CT_THREADS) conv2d_f32_tiled_kernel(const __grid_constant__ ConvF32Params p, int p_tiles,
                                                                       int oc_tiles) {
   __shared__ __align__(16) float xs[2][CT_MAX_TAPS * CT_P];   // [tap][pixel]
   __shared__ __align__(16) float ws[2][CT_MAX_TAPS * CT_OC];  // [tap][channel]

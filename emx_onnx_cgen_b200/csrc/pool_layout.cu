@@ -68,7 +68,7 @@ struct TransposeParams {
 };
 
 template <typename T>
-__global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ y, const TransposeParams p) {
+__global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ y, const __grid_constant__ TransposeParams p) {
   pdl_wait();
   pdl_launch_dependents();
   for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < p.count; o += (int64_t)gridDim.x * blockDim.x) {
@@ -120,7 +120,7 @@ struct PoolParams {
 };
 
 // one thread per output element
-__global__ void maxpool8_kernel(const PoolParams p) {
+__global__ void maxpool8_kernel(const __grid_constant__ PoolParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t total = (int64_t)p.n * p.c * p.oh * p.ow;
@@ -144,7 +144,7 @@ __global__ void maxpool8_kernel(const PoolParams p) {
   }
 }
 
-__global__ void qavgpool8_kernel(const PoolParams p) {
+__global__ void qavgpool8_kernel(const __grid_constant__ PoolParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t total = (int64_t)p.n * p.c * p.oh * p.ow;
@@ -235,7 +235,7 @@ struct QSoftmaxParams {
 // them once with the C library's expf (the function the reference calls) and
 // the kernel reads them, indexed by the element's byte and the byte that gave
 // the row maximum (equal v values give equal table rows).
-__global__ void qsoftmax8_kernel(const QSoftmaxParams p) {
+__global__ void qsoftmax8_kernel(const __grid_constant__ QSoftmaxParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t rows = p.outer * p.inner;

@@ -25,7 +25,7 @@ struct QConvGenericParams {
   float xs, ys;
 };
 
-__global__ void qconv_generic_kernel(const QConvGenericParams p) {
+__global__ void qconv_generic_kernel(const __grid_constant__ QConvGenericParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t total = (int64_t)p.n * p.oc * p.oh * p.ow;

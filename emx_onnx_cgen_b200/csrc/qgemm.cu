@@ -70,7 +70,7 @@ struct QGemmPrepParams {
 // Blocks [0, b_blocks): a 32-column x QG_PREP_KSPLIT-row slab of B, transposed
 // through shared memory into B^T, its column sums added into colsum.  Blocks
 // after that: eight A rows each (one warp per row), summed into rowsum.
-__global__ void __launch_bounds__(256) qgemm_prep_kernel(const QGemmPrepParams p) {
+__global__ void __launch_bounds__(256) qgemm_prep_kernel(const __grid_constant__ QGemmPrepParams p) {
   __shared__ uint8_t tile[QG_PREP_K][QG_PREP_COLS + 1];
   pdl_wait();
   pdl_launch_dependents();
