@@ -81,10 +81,16 @@ __device__ __forceinline__ float fma_h(uint16_t a, uint16_t b, float c) {
   asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
   return d;
 }
-// RN32(a + c) for fp16 a
-__device__ __forceinline__ float add_h(uint16_t a, float c) {
-  float d;
-  asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(a), "f"(c));
+// RN16(a + b) for fp16 a, b, one rounding.  Equal to the reference's
+// RN16(RN32(a + b)): when the exponents of a and b differ by at most 12 the
+// sum has at most 24 significant bits and RN32 is exact; otherwise the smaller
+// operand is below a quarter of the larger one's fp16 ulp, both roundings
+// return the larger operand, and RN32 cannot land on an fp16 rounding
+// midpoint (the largest such fp16 operand stays more than half an fp32 ulp
+// away from it).
+__device__ __forceinline__ uint16_t add_hh(uint16_t a, uint16_t b) {
+  uint16_t d;
+  asm("add.rn.f16 %0, %1, %2;" : "=h"(d) : "h"(a), "h"(b));
   return d;
 }
 // two floats rounded to fp16 (nearest even), packed: lo in bits 0-15
@@ -432,7 +438,7 @@ __global__ void __launch_bounds__(AE_THREADS, 2) attention_exact2_kernel(const _
   if (tid < rows) {
     uint16_t sum = 0;  // fp16 +0
     const int e = row_end(tid);
-    for (int key = 0; key < e; ++key) sum = f2h(add_h(sum, h2f(sc[key * AE_QB + tid])));
+    for (int key = 0; key < e; ++key) sum = add_hh(sum, sc[key * AE_QB + tid]);
     const float sf = h2f(sum);
     rowinv[tid] = sf == 0.0f ? 0.0f : r16(__fdiv_rn(1.0f, sf));
   }
