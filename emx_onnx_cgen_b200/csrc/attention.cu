@@ -467,24 +467,29 @@ __global__ void __launch_bounds__(AE_THREADS, 2) attention_exact2_kernel(const _
     }
     __syncthreads();
     if (!vd_ok || r0 >= rows) continue;
-    for (int kk2 = 0; kk2 < kn; ++kk2) {
+    // acc = r16(acc + w * v) for key k0 + kk2 on the rows selected (w already the scaled fp16 weight)
+    auto accumulate = [&](int kk2, bool row0, bool row1) {
       const int key = k0 + kk2;
       const uint32_t ww = *reinterpret_cast<const uint32_t*>(&sc[key * AE_QB + r0]);  // rows r0, r0+1
       const uint2 vv = *reinterpret_cast<const uint2*>(&kv[kk2 * p.DV + 4 * vq]);
       const uint16_t vh[4] = {(uint16_t)vv.x, (uint16_t)(vv.x >> 16), (uint16_t)vv.y, (uint16_t)(vv.y >> 16)};
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        if (key >= (i ? e1 : e0)) continue;
+        if (!(i ? row1 : row0)) continue;
         const uint16_t wh = (uint16_t)(ww >> (16 * i));
 #pragma unroll
         for (int cp2 = 0; cp2 < 2; ++cp2) {
-          // acc = r16(acc + w * v), w already the scaled fp16 weight
           const float a = fma_h((uint16_t)acc[i][cp2], kHalfOne, fma_h(wh, vh[2 * cp2], -0.0f));
           const float c = fma_h((uint16_t)(acc[i][cp2] >> 16), kHalfOne, fma_h(wh, vh[2 * cp2 + 1], -0.0f));
           acc[i][cp2] = pack_r16(a, c);
         }
       }
-    }
+    };
+    // keys both rows visit need no per-key bound test; the longer row's few extra keys follow
+    const int both = max(0, min(kn, min(e0, e1) - k0));
+    const int tail = max(0, min(kn, max(e0, e1) - k0));
+    for (int kk2 = 0; kk2 < both; ++kk2) accumulate(kk2, true, true);
+    for (int kk2 = both; kk2 < tail; ++kk2) accumulate(kk2, e0 > e1, e1 > e0);
   }
   if (!vd_ok) return;
 #pragma unroll
