@@ -39,6 +39,7 @@
 // The shared-memory window must start on a 1 KB boundary (the swizzle atom);
 // the kernel checks it and reports DEV_BAD_CONFIG otherwise.
 // Every wait is bounded (tc100.cuh) and reports through the plan's error word.
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "host_util.h"
@@ -323,17 +324,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
       const float sc = p.scale_log2;
       const bool pos = sc > 0.0f;
       float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // tiles whose keys are all visible (every tile but a causal row block's
+      // last) run the element loops without the per-key visibility test
+      const bool full_tile = nvalid == ATC_N;
+      auto row_max = [&](auto full_c) {
+        constexpr bool FULL = decltype(full_c)::value;
 #pragma unroll
-      for (int c = 0; c < NC; ++c)
+        for (int c = 0; c < NC; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(sv[c][i]);
-          if (!pos) {
-            x *= sc;
-            sv[c][i] = __float_as_uint(x);
+          for (int i = 0; i < 32; ++i) {
+            float x = __uint_as_float(sv[c][i]);
+            if (!pos) {
+              x *= sc;
+              sv[c][i] = __float_as_uint(x);
+            }
+            if (FULL || 32 * c + i < nvalid) mxp[i & 3] = fmaxf(mxp[i & 3], x);
           }
-          if (32 * c + i < nvalid) mxp[i & 3] = fmaxf(mxp[i & 3], x);
-        }
+      };
+      if (full_tile)
+        row_max(std::true_type{});
+      else
+        row_max(std::false_type{});
       float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
       if (pos) mx *= sc;
       const float mul = pos ? sc : 1.0f;
@@ -349,16 +360,25 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
       uint32_t pw[NC][16];
       float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       const float neg_m = -m_new;
+      auto exps = [&](auto full_c) {
+        constexpr bool FULL = decltype(full_c)::value;
 #pragma unroll
-      for (int c = 0; c < NC; ++c)
+        for (int c = 0; c < NC; ++c)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = 32 * c + 2 * i;
-          const float e0 = k0 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i]), mul, neg_m)) : 0.0f;
-          const float e1 = k0 + 1 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i + 1]), mul, neg_m)) : 0.0f;
-          pw[c][i] = pack_f16x2(e0, e1);
-          lp[i & 3] += f16lo(pw[c][i]) + f16hi(pw[c][i]);
-        }
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = 32 * c + 2 * i;
+            const float e0 =
+                FULL || k0 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i]), mul, neg_m)) : 0.0f;
+            const float e1 =
+                FULL || k0 + 1 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i + 1]), mul, neg_m)) : 0.0f;
+            pw[c][i] = pack_f16x2(e0, e1);
+            lp[i & 3] += f16lo(pw[c][i]) + f16hi(pw[c][i]);
+          }
+      };
+      if (full_tile)
+        exps(std::true_type{});
+      else
+        exps(std::false_type{});
       l = l * alpha + ((lp[0] + lp[1]) + (lp[2] + lp[3]));
       m_used = m_new;
       // P_{j-1} V_{j-1} must be done before P is overwritten and O rescaled
