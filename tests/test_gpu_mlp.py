@@ -21,8 +21,12 @@ def test_golden(name):
     assert_bitexact(out["Y"], ref["Y"], name)
 
 
+# beyond the default MLP: ragged rows / columns with many full 64-wide K stages and a partial
+# last one, through the long-chain 32x16 tile (k 1100 -> hidden 1000; hidden 4000 -> 1000) and
+# the 16x32 and 8x16 tiles
 @pytest.mark.parametrize("kw", [dict(), dict(m=7, k=33, hidden=65), dict(m=300, k=16, hidden=40),
-                                dict(m=1, k=1, hidden=1)])
+                                dict(m=1, k=1, hidden=1), dict(m=40, k=1100, hidden=1000),
+                                dict(m=64, k=1000, hidden=4000)])
 def test_vs_port(kw):
     require_gpu()
     wl = W.mlp_fp32(**kw)
