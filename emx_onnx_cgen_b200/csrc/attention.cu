@@ -246,10 +246,11 @@ __global__ void __launch_bounds__(AT_THREADS) attention_exact_kernel(const __gri
   __syncthreads();
   // ---- sequential sums and reciprocals, one thread per row
   if (tid < AT_QB && q0 + tid < p.TQ) {
-    float sum = 0.0f;
+    uint16_t sum = 0;  // fp16 +0
     const int e = row_end(tid);
-    for (int key = 0; key < e; ++key) sum = r16(__fadd_rn(sum, h2f(sc[tid * p.scn + key])));
-    rowinv[tid] = sum == 0.0f ? 0.0f : r16(__fdiv_rn(1.0f, sum));
+    for (int key = 0; key < e; ++key) sum = add_hh(sum, sc[tid * p.scn + key]);
+    const float sf = h2f(sum);
+    rowinv[tid] = sf == 0.0f ? 0.0f : r16(__fdiv_rn(1.0f, sf));
   }
   __syncthreads();
   // ---- scaled weights r16(w * inv)
