@@ -119,8 +119,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return r;
 }
 
-__device__ __forceinline__ float f16lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
-__device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+// c + (the fp16 value h), rounded to fp32: one mixed-precision add
+__device__ __forceinline__ float add_f16(uint16_t h, float c) {
+  float d;
+  asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+  return d;
+}
 
 // K-major SW128 operand descriptor: 128-byte rows, 8-row atoms 1 KB apart.
 __device__ __forceinline__ uint64_t atc_desc_k(uint32_t saddr) { return smem_desc_k_sw128(saddr, 1024); }
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
             const float e1 =
                 FULL || k0 + 1 < nvalid ? ex2_approx(fmaf(__uint_as_float(sv[c][2 * i + 1]), mul, neg_m)) : 0.0f;
             pw[c][i] = pack_f16x2(e0, e1);
-            lp[i & 3] += f16lo(pw[c][i]) + f16hi(pw[c][i]);
+            lp[i & 3] = add_f16((uint16_t)(pw[c][i] >> 16), add_f16((uint16_t)pw[c][i], lp[i & 3]));
           }
       };
       if (full_tile)
