@@ -13,7 +13,7 @@ ABI ``_Bool <model>_load(const char *)`` / ``void <model>(inputs..., outputs...)
 (``docs/output-format.md:132-193``).
 
 Only ``tests/``, ``__graft_entry__`` and ``bench.py``'s CPU-baseline legs use
-this, and only as the checker.  The reference itself is needed only to
+this, and only to check results against.  The reference itself is needed only to
 *generate* the C (in the build container); the compiled libraries in
 ``oracle/_ref/`` run without it.
 """
