@@ -998,9 +998,13 @@ int prepare_qconv_tc(const PlanOp& op, void* const* ptrs, OpState* st_, int devi
     int* d_mis = nullptr;
     int mis = -1;
     if (cudaMalloc(&d_mis, sizeof(int)) != cudaSuccess) return fail(msg, n, 7, "check buffer");
-    cudaMemset(d_mis, 0, sizeof(int));
-    qadd_fastdiv_check_kernel<<<256, 256>>>(p, d_mis);
-    e = cudaMemcpy(&mis, d_mis, sizeof(int), cudaMemcpyDeviceToHost);
+    // the fast division is kept only when the check itself ran to the end
+    e = cudaMemset(d_mis, 0, sizeof(int));
+    if (e == cudaSuccess) {
+      qadd_fastdiv_check_kernel<<<256, 256>>>(p, d_mis);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(&mis, d_mis, sizeof(int), cudaMemcpyDeviceToHost);
     cudaFree(d_mis);
     if (e != cudaSuccess) return fail(msg, n, 4, "fast-division check: %s", cudaGetErrorString(e));
     st->fast_div = mis == 0 ? 1 : 0;
