@@ -348,6 +348,15 @@ class Ctx:
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(self.local)
+        # under torchrun: this rank's host threads and page-locked buffers on
+        # its GPU's NUMA node (first touch), next to that GPU's PCIe root
+        self.host_binding = None
+        if self.world > 1:
+            from emx_onnx_cgen_b200.distributed import bind_host_to_gpu
+            try:
+                self.host_binding = bind_host_to_gpu(self.local)
+            except OSError as exc:  # placement is an optimisation, never a reason to stop
+                self.host_binding = {"numa_node": None, "error": str(exc)[:120]}
         if self.world > 1:
             from datetime import timedelta
             dist.init_process_group("nccl", timeout=timedelta(seconds=300),
@@ -536,6 +545,8 @@ def run_workload(ctx: Ctx, name: str, shard: int = 1) -> dict:
     }
     if shard > 1:
         line["config"]["parallelism"] = f"one inference split along its batch dimension over {shard} GPUs"
+    if ctx.host_binding is not None:
+        line["config"]["host_numa"] = ctx.host_binding
     if ms_copy is not None:
         line["copy_ceiling"] = {
             "value": per * 1000.0 / ms_copy, "unit": "inferences/s", "ms_per_step": ms_copy,

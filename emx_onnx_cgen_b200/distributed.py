@@ -29,6 +29,50 @@ def shard_rows(batch: int, world_size: int, rank: int) -> tuple[int, int]:
     return begin, base + (1 if rank < extra else 0)
 
 
+def parse_cpulist(text: str) -> list[int]:
+    """CPU numbers of a sysfs cpulist such as ``"0-3,8,10-11"``."""
+    cpus: list[int] = []
+    for part in text.strip().split(","):
+        part = part.strip()
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.extend(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def numa_cpus_for_pci(domain: int, bus: int, device: int, sysfs: str = "/sys") -> tuple[int, list[int]]:
+    """(NUMA node, its CPUs) of the PCI device ``domain:bus:device.0``;
+    (-1, []) where the platform does not say (no sysfs entry, node -1)."""
+    dev = os.path.join(sysfs, "bus", "pci", "devices", f"{domain:04x}:{bus:02x}:{device:02x}.0")
+    try:
+        with open(os.path.join(dev, "numa_node")) as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return -1, []
+        with open(os.path.join(sysfs, "devices", "system", "node", f"node{node}", "cpulist")) as f:
+            return node, parse_cpulist(f.read())
+    except (OSError, ValueError):
+        return -1, []
+
+
+def bind_host_to_gpu(device_index: int, sysfs: str = "/sys") -> dict:
+    """Pin this process to the CPUs of its GPU's NUMA node, so page-locked host
+    buffers allocated afterwards (first touch) sit in that node's memory, next
+    to the GPU's PCIe root.  Returns what was done; changes nothing where the
+    node is unknown or none of its CPUs is allowed to this process."""
+    import torch
+    pr = torch.cuda.get_device_properties(device_index)
+    node, cpus = numa_cpus_for_pci(pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id, sysfs)
+    allowed = os.sched_getaffinity(0)
+    cpus = [c for c in cpus if c in allowed]
+    if node < 0 or not cpus:
+        return {"numa_node": node, "cpus": None}
+    os.sched_setaffinity(0, cpus)
+    return {"numa_node": node, "cpus": f"{cpus[0]}-{cpus[-1]}" if cpus == list(range(cpus[0], cpus[-1] + 1))
+            else ",".join(map(str, cpus))}
+
+
 def replica_seed(rank: int, base: int = 0) -> int:
     """Input seed of a rank's independent inferences."""
     return base + rank

@@ -6,7 +6,7 @@ import socket
 
 import pytest
 
-from emx_onnx_cgen_b200.distributed import shard_rows
+from emx_onnx_cgen_b200.distributed import numa_cpus_for_pci, parse_cpulist, shard_rows
 
 
 def _free_port() -> int:
@@ -62,3 +62,23 @@ def test_shards_tile_the_batch(batch, world):
         pos += c
     assert pos == batch
     assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
+
+
+def test_cpulist_forms():
+    assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    assert parse_cpulist("5") == [5]
+    assert parse_cpulist("") == []
+
+
+def test_numa_cpus_for_pci_reads_sysfs(tmp_path):
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    (dev / "numa_node").write_text("1\n")
+    node = tmp_path / "devices" / "system" / "node" / "node1"
+    node.mkdir(parents=True)
+    (node / "cpulist").write_text("32-35,96\n")
+    assert numa_cpus_for_pci(0, 0x1B, 0, str(tmp_path)) == (1, [32, 33, 34, 35, 96])
+    # unknown placement: no entry, or node -1 (single-node platforms)
+    assert numa_cpus_for_pci(0, 0x1C, 0, str(tmp_path)) == (-1, [])
+    (dev / "numa_node").write_text("-1\n")
+    assert numa_cpus_for_pci(0, 0x1B, 0, str(tmp_path)) == (-1, [])
