@@ -355,7 +355,7 @@ class Ctx:
             from emx_onnx_cgen_b200.distributed import bind_host_to_gpu
             try:
                 self.host_binding = bind_host_to_gpu(self.local)
-            except OSError as exc:  # placement is an optimisation, never a reason to stop
+            except Exception as exc:  # placement is an optimisation, never a reason to stop
                 self.host_binding = {"numa_node": None, "error": str(exc)[:120]}
         if self.world > 1:
             from datetime import timedelta

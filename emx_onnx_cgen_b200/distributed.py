@@ -56,21 +56,55 @@ def numa_cpus_for_pci(domain: int, bus: int, device: int, sysfs: str = "/sys") -
         return -1, []
 
 
-def bind_host_to_gpu(device_index: int, sysfs: str = "/sys") -> dict:
-    """Pin this process to the CPUs of its GPU's NUMA node, so page-locked host
-    buffers allocated afterwards (first touch) sit in that node's memory, next
-    to the GPU's PCIe root.  Returns what was done; changes nothing where the
-    node is unknown or none of its CPUs is allowed to this process."""
+def cpus_from_affinity_words(words) -> list[int]:
+    """CPU numbers set in a bitmask given as 64-bit words, lowest word first
+    (the form NVML's ``nvmlDeviceGetCpuAffinity`` returns)."""
+    return [64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1]
+
+
+def nvml_cpus_for_pci(domain: int, bus: int, device: int, nvml=None) -> list[int]:
+    """The CPUs the driver reports as closest to the GPU at ``domain:bus:device``
+    (a read-only NVML query); [] when NVML is absent or does not say."""
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        nvml.nvmlInit()
+        try:
+            h = nvml.nvmlDeviceGetHandleByPciBusId(f"{domain:08x}:{bus:02x}:{device:02x}.0".encode())
+            n_words = (max(os.cpu_count() or 1, 1) + 63) // 64
+            return cpus_from_affinity_words(nvml.nvmlDeviceGetCpuAffinity(h, n_words))
+        finally:
+            nvml.nvmlShutdown()
+    except Exception:  # no NVML, no device entry: placement is unknown
+        return []
+
+
+def _cpu_span(cpus: list[int]) -> str:
+    if cpus == list(range(cpus[0], cpus[-1] + 1)):
+        return f"{cpus[0]}-{cpus[-1]}"
+    return ",".join(map(str, cpus))
+
+
+def bind_host_to_gpu(device_index: int, sysfs: str = "/sys", nvml=None) -> dict:
+    """Pin this process to the CPUs nearest its GPU -- its NUMA node's CPUs from
+    sysfs, else the CPU affinity the driver reports through NVML -- so
+    page-locked host buffers allocated afterwards (first touch) sit in that
+    node's memory, next to the GPU's PCIe root.  Returns what was done; changes
+    nothing where neither source says or none of those CPUs is allowed to this
+    process."""
     import torch
     pr = torch.cuda.get_device_properties(device_index)
     node, cpus = numa_cpus_for_pci(pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id, sysfs)
+    source = "sysfs"
+    if node < 0:
+        cpus, source = nvml_cpus_for_pci(pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id, nvml), "nvml"
     allowed = os.sched_getaffinity(0)
     cpus = [c for c in cpus if c in allowed]
-    if node < 0 or not cpus:
+    if not cpus:
         return {"numa_node": node, "cpus": None}
-    os.sched_setaffinity(0, cpus)
-    return {"numa_node": node, "cpus": f"{cpus[0]}-{cpus[-1]}" if cpus == list(range(cpus[0], cpus[-1] + 1))
-            else ",".join(map(str, cpus))}
+    if set(cpus) != allowed:
+        os.sched_setaffinity(0, cpus)
+    return {"numa_node": node, "cpus": _cpu_span(cpus), "source": source}
 
 
 def replica_seed(rank: int, base: int = 0) -> int:

@@ -6,7 +6,8 @@ import socket
 
 import pytest
 
-from emx_onnx_cgen_b200.distributed import numa_cpus_for_pci, parse_cpulist, shard_rows
+from emx_onnx_cgen_b200.distributed import (cpus_from_affinity_words, numa_cpus_for_pci,
+                                              nvml_cpus_for_pci, parse_cpulist, shard_rows)
 
 
 def _free_port() -> int:
@@ -82,3 +83,30 @@ def test_numa_cpus_for_pci_reads_sysfs(tmp_path):
     assert numa_cpus_for_pci(0, 0x1C, 0, str(tmp_path)) == (-1, [])
     (dev / "numa_node").write_text("-1\n")
     assert numa_cpus_for_pci(0, 0x1B, 0, str(tmp_path)) == (-1, [])
+
+
+def test_nvml_affinity_fallback():
+    assert cpus_from_affinity_words([0xFFFF]) == list(range(16))
+    assert cpus_from_affinity_words([0, 1 << 3]) == [67]
+
+    class FakeNvml:
+        calls = []
+
+        def nvmlInit(self):
+            self.calls.append("init")
+
+        def nvmlShutdown(self):
+            self.calls.append("shutdown")
+
+        def nvmlDeviceGetHandleByPciBusId(self, bus_id):
+            if bus_id != b"00000000:1b:00.0":
+                raise RuntimeError("no such device")
+            return "h"
+
+        def nvmlDeviceGetCpuAffinity(self, h, n_words):
+            return [0x0F0] + [0] * (n_words - 1)
+
+    fake = FakeNvml()
+    assert nvml_cpus_for_pci(0, 0x1B, 0, fake) == [4, 5, 6, 7]
+    assert fake.calls == ["init", "shutdown"]
+    assert nvml_cpus_for_pci(0, 0x1C, 0, fake) == []  # unknown device: no placement
