@@ -312,6 +312,7 @@ int launch_ops(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launche
 // cudaGraphLaunch on the caller's stream.  Host<->device staging copies stay
 // outside the graph (they may involve pageable host memory).
 int run_graph(emx_plan* p, int64_t run_batch, cudaStream_t stream, int* launches) {
+  if (p->ops.empty()) return EMX_OK;  // every op had only empty outputs: nothing to launch
   std::vector<void*> key;
   key.reserve(p->inputs.size() + p->outputs.size());
   for (uint32_t id : p->inputs) key.push_back(p->ptrs[id]);

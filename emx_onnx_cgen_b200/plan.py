@@ -440,6 +440,19 @@ class B200PlanEmitter:
 
         self._analyse(ops)
         for i, op in enumerate(ops):
+            outs = self._op_outputs(op)
+            if outs and all(int(np.prod(self._shape(o), dtype=np.int64)) == 0 for o in outs):
+                # every output is empty (a zero extent): the reference's loops run
+                # zero times, so the op launches nothing; its outputs still exist
+                for o in outs:
+                    if o not in self._nchw:
+                        self._dest(o, self._dtype(o), tuple(self._shape(o)))
+                continue
+            empty_in = [n for n in self._op_inputs(op) if int(np.prod(self._shape(n), dtype=np.int64)) == 0]
+            if empty_in:
+                # e.g. an LSTM over zero steps or a Gemm with K = 0: outputs that are not
+                # sums over the empty extent have no kernel path here
+                raise UnsupportedOpError(f"{_name(op)}: empty input {empty_in[0]} with non-empty outputs")
             if i in self._absorbed:
                 continue
             handler = getattr(self, "_emit_" + _name(op), None)

@@ -78,6 +78,35 @@ def test_unsupported_op_raises():
         B200PlanEmitter().emit_plan(lowering.lower(g))
 
 
+EMPTY_EXTENT_CASES = {
+    "qconv_batch0": lambda: W.qconv_stack_int8(batch=0, height=8, width=8),
+    "mlp_rows0": lambda: W.mlp_fp32(m=0, k=8, hidden=16),
+    "attention_batch0": lambda: W.attention_fp16(batch=0, heads=1, seq=8, head_dim=16),
+    "attention_seq0": lambda: W.attention_fp16(batch=1, heads=1, seq=0, head_dim=16),
+    "lstm_batch0": lambda: W.lstm_fp32(seq=3, batch=0, input_size=4, hidden=4),
+    "int4_mlp_rows0": lambda: W.llama_mlp_int4(m=0, hidden=64, inter=64),
+}
+
+
+@pytest.mark.parametrize("name", sorted(EMPTY_EXTENT_CASES))
+def test_ops_with_only_empty_outputs_launch_nothing(name):
+    """A zero extent (the reference accepts zero dimensions) empties every
+    output: the reference's loops run zero times, and the plan has no op."""
+    wl = EMPTY_EXTENT_CASES[name]()
+    plan = B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+    assert plan.ops == []
+    assert all(0 in shp for shp in plan.output_shapes)
+
+
+def test_empty_input_with_non_empty_outputs_is_rejected():
+    # an LSTM over zero steps still has Y_h / Y_c; a Gemm with K = 0 still has Y
+    with np.errstate(divide="ignore"):
+        cases = [W.lstm_fp32(seq=0, batch=2, input_size=4, hidden=4), W.mlp_fp32(m=2, k=0, hidden=16)]
+    for wl in cases:
+        with pytest.raises(lowering.UnsupportedOpError, match="empty input"):
+            B200PlanEmitter().emit_plan(lowering.lower(wl.graph))
+
+
 def test_weight_image_layout():
     """Tensor-core weight image: [tap][oc][cin] with each row's 16-byte chunks
     at their swizzled positions (chunk j of row r at j ^ ((r*cin >> 7) & (cin/16-1)))."""
